@@ -1,0 +1,262 @@
+/*
+ * oasis_b200.h - C ABI of the B200 (sm_100a) Oasis-500M frame-generation library.
+ *
+ * One frame = 4 DDIM v-prediction steps through the 16-block spatio-temporal DiT,
+ * then the 12-block ViT VAE decode. The functions below are what a host binding
+ * (ctypes here; cgo/JNI/N-API elsewhere) calls in place of the reference's device
+ * code in zoecarver/open-oasis `oasis_inference.py`.
+ *
+ * Conventions
+ *   - All pointers are caller-owned DEVICE pointers. Tensors marked bf16 hold
+ *     IEEE bfloat16 (uint16 storage); everything else is fp32. Row-major.
+ *   - The library never allocates on these paths: scratch comes from a caller
+ *     workspace sized by the matching *_workspace_size() function.
+ *   - Every call is stream-ordered on `stream` (a cudaStream_t; NULL = legacy
+ *     default stream) and returns 0 or a negative OASIS_ERR_* code; the reason is
+ *     in oasis_last_error(). Nothing exits, traps or prints.
+ *   - Kernels never spin forever: a wait that exceeds its limit sets a device
+ *     error word (oasis_device_error) and the kernel returns.
+ *
+ * Model constants: D = 1024, 16 heads x 64, MLP 4096, 144 tokens per frame
+ * (9 x 16 patches of 2 x 2 over a 16 x 18 x 32 latent), VAE 576 tokens (18 x 32)
+ * decoding 20 x 20 x 3 pixel patches into a 3 x 360 x 640 frame.
+ */
+#ifndef OASIS_B200_H
+#define OASIS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* oasis_stream_t; /* cudaStream_t */
+
+#define OASIS_OK 0
+#define OASIS_ERR_INVALID_ARG (-1)
+#define OASIS_ERR_CUDA (-2)
+#define OASIS_ERR_WORKSPACE (-3)
+#define OASIS_ERR_DEVICE_TIMEOUT (-4)
+#define OASIS_ERR_UNSUPPORTED (-5)
+
+#define OASIS_DIT_SUBBLOCKS 32       /* blocks.{0..15}.{s,t} interleaved: 2i = spatial, 2i+1 = temporal */
+#define OASIS_ADALN_WIDTH 6144       /* per sub-block adaLN output (shift, 1+scale, gate) x (msa, mlp) */
+#define OASIS_ADALN_ROWS (OASIS_DIT_SUBBLOCKS * OASIS_ADALN_WIDTH + 2048) /* + final (shift, 1+scale) */
+#define OASIS_VAE_BLOCKS 12
+
+/* ---------------------------------------------------------------- errors -- */
+
+/* Message of the last failing call on this host thread ("" if none). */
+const char* oasis_last_error(void);
+/* Reads (and with reset != 0 clears) the device error word; synchronizes the device. */
+int oasis_device_error(int reset);
+/* Library version string. */
+const char* oasis_version(void);
+
+/* ------------------------------------------------------------- weights --- */
+
+/* One DiT sub-block (blocks.i.s or blocks.i.t). Replaces the per-prefix device
+ * tensors of preload_dit_weights (oasis_inference.py:546-626): the reference's
+ * [Q|K|V|Qswap|Kswap] packing is unnecessary because RoPE is applied in the QKV
+ * GEMM epilogue. Weights keep the nn.Linear [out, in] layout. */
+typedef struct OasisDitSubBlock {
+  const void* qkv_w;  /* bf16 [3072, 1024], no bias (to_qkv) */
+  const void* out_w;  /* bf16 [1024, 1024] (to_out) */
+  const float* out_b; /* [1024] */
+  const void* fc1_w;  /* bf16 [4096, 1024] */
+  const float* fc1_b; /* [4096] */
+  const void* fc2_w;  /* bf16 [1024, 4096] */
+  const float* fc2_b; /* [1024] */
+} OasisDitSubBlock;
+
+typedef struct OasisDitWeights {
+  int num_subblocks; /* 32 for Oasis-500M; fewer runs a truncated stack (tests) */
+  OasisDitSubBlock sub[OASIS_DIT_SUBBLOCKS];
+  /* All sub-block adaLN linears plus the final layer's, stacked along the
+   * output dim: rows [6144 i, 6144 i + 6144) = blocks.(i/2).(s|t)_adaLN_modulation.1,
+   * rows [6144 S, 6144 S + 2048) = final_layer.adaLN_modulation.1 (S = num_subblocks).
+   * Bias has +1 folded into every scale slice (oasis_inference.py:549-556, 531). */
+  const void* adaln_w;  /* bf16 [6144 S + 2048, 1024] */
+  const float* adaln_b; /* [6144 S + 2048] */
+  const void* final_w;  /* bf16 [64, 1024] final_layer.linear */
+  const float* final_b; /* [64] */
+  /* x_embedder conv 2x2/2 as a linear map over a (p, q, c)-ordered 64-vector
+   * (W_rt of oasis_inference.py:1821-1826), stored input-major: [64, 1024]. */
+  const float* embed_w; /* [64, 1024] */
+  const float* embed_b; /* [1024] */
+  /* RoPE tables as (cos, sin) pairs per position and head-dim pair. */
+  const float* rope_spatial;  /* [144, 32, 2] axial (h, w) */
+  const float* rope_temporal; /* [32, 32, 2]  frame index t < 32 */
+} OasisDitWeights;
+
+typedef struct OasisVaeBlock {
+  const float* norm1_w; const float* norm1_b; /* [1024] */
+  const void* qkv_w; const float* qkv_b;      /* bf16 [3072, 1024], [3072] */
+  const void* proj_w; const float* proj_b;    /* bf16 [1024, 1024], [1024] */
+  const float* norm2_w; const float* norm2_b; /* [1024] */
+  const void* fc1_w; const float* fc1_b;      /* bf16 [4096, 1024], [4096] */
+  const void* fc2_w; const float* fc2_b;      /* bf16 [1024, 4096], [1024] */
+} OasisVaeBlock;
+
+typedef struct OasisVaeWeights {
+  const float* post_quant_w; /* [16, 1024] input-major (post_quant_conv as a linear map) */
+  const float* post_quant_b; /* [1024] */
+  int num_blocks;            /* 12 for Oasis-500M's decoder; fewer in tests */
+  OasisVaeBlock blk[OASIS_VAE_BLOCKS];
+  const float* norm_w; const float* norm_b; /* dec_norm [1024] */
+  const void* pred_w;                       /* bf16 [1200, 1024] predictor */
+  const float* pred_b;                      /* [1200] */
+  const float* rope;                        /* [576, 32, 2]; pairs >= 16 are (1, 0) */
+} OasisVaeWeights;
+
+/* ---------------------------------------------------------- composite ---- */
+
+/* DiT forward over B sessions x T frames (T <= 32).
+ * Replaces dit_forward_device (oasis_inference.py:1438-1526).
+ *   z     [B, T, 144, 1024] fp32 token embeddings; used as the residual stream
+ *         and overwritten.
+ *   cond  [B, T, 1024] fp32 conditioning per frame (before SiLU).
+ *   v_out last_frame_only ? [B, 144, 64] : [B, T, 144, 64] fp32 v-prediction. */
+typedef struct OasisDitArgs {
+  int batch;
+  int frames;
+  float* z;
+  const float* cond;
+  float* v_out;
+  int last_frame_only;
+  void* workspace;
+  size_t workspace_bytes;
+} OasisDitArgs;
+
+size_t oasis_dit_workspace_size(int batch, int frames);
+int oasis_dit_forward(const OasisDitWeights* w, const OasisDitArgs* a, oasis_stream_t stream);
+
+/* DDIM coefficients of one step (oasis_inference.py:1843-1860):
+ * x0 = at_sqrt x - one_minus_at_sqrt v; eps = (inv_at_sqrt x - x0) inv_sigma;
+ * x' = an_sqrt x0 + one_minus_an_sqrt eps. */
+typedef struct OasisDdimCoeffs {
+  float at_sqrt, one_minus_at_sqrt, inv_at_sqrt, inv_sigma, an_sqrt, one_minus_an_sqrt;
+} OasisDdimCoeffs;
+
+/* In-place DDIM update of n elements. Replaces the eltwise tail of ddim_step_fn
+ * (oasis_inference.py:1920-1931). */
+int oasis_ddim_update(float* chunk, const float* v, const OasisDdimCoeffs* c, long long n,
+                      oasis_stream_t stream);
+
+/* One full DDIM step (ddim_step_fn, oasis_inference.py:1909-1932):
+ * z = concat(context_z, patch_embed(chunk)); v = DiT(z, cond)[last frame];
+ * chunk = ddim(chunk, v).
+ *   chunk     [B, 144, 64] fp32 noisy latent patches, (p, q, c) order; updated in place
+ *   context_z [B, T-1, 144, 1024] fp32 embedded context frames (may be NULL if T == 1)
+ *   cond      [B, T, 1024] fp32 */
+typedef struct OasisStepArgs {
+  int batch;
+  int frames;
+  float* chunk;
+  const float* context_z;
+  const float* cond;
+  OasisDdimCoeffs coeffs;
+  void* workspace;
+  size_t workspace_bytes;
+} OasisStepArgs;
+
+size_t oasis_step_workspace_size(int batch, int frames);
+int oasis_ddim_step(const OasisDitWeights* w, const OasisStepArgs* a, oasis_stream_t stream);
+
+/* Patch-embed latent patches [rows, 64] into token rows of z:
+ * out_row = (r / 144) * out_group + out_off + r % 144. */
+int oasis_patch_embed(const OasisDitWeights* w, const float* patches, int rows, float* z,
+                      long long out_group, long long out_off, oasis_stream_t stream);
+
+/* DiT output chunk [B, 144, 64] -> VAE latent tokens [B, 576, 16] scaled by
+ * 1 / 0.07843137255. Replaces bridge_unpatchify (oasis_inference.py:1697-1709). */
+int oasis_bridge_unpatchify(const float* chunk, float* latent, int batch, oasis_stream_t stream);
+
+/* VAE decode of B frames. Replaces vae_decode_forward (oasis_inference.py:1546-1618)
+ * plus vae_unpatchify and the clamp (oasis_inference.py:1636-1645, 2292).
+ *   latent [B, 576, 16] fp32 (already divided by the scaling factor)
+ *   image  [B, 3, 360, 640] fp32 clamped to [-1, 1] */
+typedef struct OasisVaeArgs {
+  int batch;
+  const float* latent;
+  float* image;
+  void* workspace;
+  size_t workspace_bytes;
+} OasisVaeArgs;
+
+size_t oasis_vae_workspace_size(int batch);
+int oasis_vae_decode(const OasisVaeWeights* w, const OasisVaeArgs* a, oasis_stream_t stream);
+
+/* ------------------------------------------------------------ op level --- */
+
+/* tcgen05 GEMM: acc = A[M,K] . W[N,K]^T (bf16 in, fp32 accumulate) + bias, then
+ * the fused epilogue `mode`:
+ *   0 F32          out_f32 = acc
+ *   1 BF16         out_bf16 = acc
+ *   2 GELU_TANH    out_bf16 = gelu_tanh(acc)          (DiT FC1, ttnn.linear gelu)
+ *   3 GELU_ERF     out_bf16 = gelu_erf(acc)           (VAE FC1)
+ *   4 GATED_RESID  out_f32 = resid + gate[r / rows_per_frame, n] * acc   (O / FC2)
+ *   5 RESID        out_f32 = resid + acc              (VAE proj / FC2)
+ *   6 ROPE         out_bf16 = acc with interleaved RoPE on columns [0, 2048)
+ *                  at position (r / rope_div) % rope_mod    (QKV + rope_layout)
+ *   7 IMAGE        VAE predictor: scatter 20x20x3 patches into [frames, 3, 360, 640],
+ *                  clamped to [-1, 1]
+ * K must be a multiple of 64 and N of 16. Split-K needs `workspace`. */
+typedef struct OasisGemmArgs {
+  const void* a; long long lda; /* bf16 */
+  const void* w;                /* bf16 [N, K] */
+  int m, n, k;
+  int mode;
+  void* out; long long ldo;
+  const float* bias;
+  const float* resid; long long ldr;
+  const float* gate; long long ldg; int rows_per_frame;
+  const float* rope; int rope_div; int rope_mod;
+  int block_n; /* 0 = heuristic, else 64 / 128 / 256 */
+  int splits;  /* 0 = heuristic, 1 = none */
+  void* workspace; size_t workspace_bytes;
+} OasisGemmArgs;
+
+int oasis_gemm(const OasisGemmArgs* a, oasis_stream_t stream);
+size_t oasis_gemm_workspace_size(int m, int n, int k);
+
+/* LayerNorm (eps, no affine) + adaLN modulate, or LayerNorm with affine w/b:
+ * y_bf16[r] = LN(x[in_row]) * mul + add, where
+ *   in_row = (r / P) * in_group + in_off + r % P
+ *   modulated: frame = (r / P) * frame_mul + frame_add,
+ *              add = mod[frame * ld_mod + shift_off + :], mul = mod[frame * ld_mod + scale_off + :]
+ *   affine:    mul = affine_w, add = affine_b.
+ * Replaces ttnn.layer_norm + ttnn.addcmul (oasis_inference.py:1053-1056) and
+ * layernorm_d1024 (src/layernorm.py:15-96). Width is 1024. */
+typedef struct OasisLayerNormArgs {
+  const float* x; void* y; int rows_out;
+  int P; long long in_group, in_off, frame_mul, frame_add;
+  float eps;
+  const float* mod; long long ld_mod, shift_off, scale_off;
+  const float* affine_w; const float* affine_b;
+} OasisLayerNormArgs;
+
+int oasis_layernorm(const OasisLayerNormArgs* a, oasis_stream_t stream);
+
+/* SiLU of fp32 x into bf16 y (silu_kernel, src/silu.py:8-47). n % 4 == 0. */
+int oasis_silu_bf16(const float* x, void* y, long long n, oasis_stream_t stream);
+
+/* Spatial / VAE attention: non-causal within groups of `seq` rows of a packed
+ * qkv [rows, 3072] bf16; out [rows, 1024] bf16. Replaces sdpa_spatial
+ * (src/sdpa.py:27-113, but over exactly `seq` keys) and the VAE ttnn SDPA. */
+int oasis_attention_spatial(const void* qkv, void* out, int groups, int seq, oasis_stream_t stream);
+
+/* Causal temporal attention per (session, patch, head) over T frames; token row
+ * of (b, t, p) = (b T + t) 144 + p. Replaces sdpa_temporal_causal
+ * (src/sdpa_causal.py:17-100) and its block-diagonal packing. */
+int oasis_attention_temporal(const void* qkv, void* out, int batch, int frames, oasis_stream_t stream);
+
+/* VAE post_quant_conv as a linear map: z[r] = latent[r, :16] . w + b. */
+int oasis_post_quant(const float* latent, const float* w, const float* b, float* z, int rows,
+                     oasis_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* OASIS_B200_H */

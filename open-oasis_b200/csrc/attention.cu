@@ -1,0 +1,312 @@
+// Attention kernels of the Oasis frame path.
+//
+// Both read q/k/v straight out of the packed QKV GEMM output [rows, 3072] bf16
+// (q | k | v, 16 heads x 64; RoPE already applied by the GEMM epilogue), so the
+// reference's separate RoPE/layout kernels and reshapes disappear: a head is a
+// 128-byte column slice of each row.
+//
+// attention_full: non-causal softmax(q k^T / 8) v within groups of `seq`
+//   consecutive rows (DiT spatial: one frame, seq = 144, exactly 144 keys - the
+//   tail of the last key tile is masked; VAE: one frame, seq = 576).
+//   Flash-style: K/V tiles of 64 keys staged in swizzled shared memory with
+//   cp.async double buffering, online softmax in fp32, bf16 mma.sync m16n8k16.
+// attention_temporal: causal softmax over the T frames of one session, per
+//   (patch, head). One warp per problem, lane = 2 of the 64 head dims, k/v for
+//   all frames held in registers, scores reduced with warp shuffles.
+#include "common.cuh"
+#include "pointwise.cuh"
+#include "status.h"
+
+namespace oasis {
+namespace {
+
+constexpr int kHeads = 16;
+constexpr int kDh = 64;
+constexpr int kQkvLd = 3 * kHeads * kDh;  // 3072
+constexpr int kOutLd = kHeads * kDh;      // 1024
+constexpr int kKeyTile = 64;
+
+__device__ __forceinline__ int swz(int row, int col) {
+  return row * kDh + ((((col >> 3) ^ (row & 7))) << 3) + (col & 7);
+}
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(gmem),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+
+__device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Loads `rows` rows (64 bf16 each) of one head slice into a swizzled tile; rows past
+// `valid` are zero-filled.
+template <int NT>
+__device__ __forceinline__ void load_tile(__nv_bfloat16* dst, const __nv_bfloat16* src, int rows, int valid) {
+  for (int i = threadIdx.x; i < rows * 8; i += NT) {
+    const int r = i >> 3, c = (i & 7) * 8;
+    const bool ok = r < valid;
+    cp_async16(dst + swz(r, c), src + (long long)(ok ? r : 0) * kQkvLd + c, ok);
+  }
+}
+
+template <int NW>
+__global__ void __launch_bounds__(NW * 32) attention_full_kernel(const __nv_bfloat16* __restrict__ qkv,
+                                                                 __nv_bfloat16* __restrict__ out, int seq) {
+  constexpr int NT = NW * 32;
+  constexpr int QROWS = NW * 16;
+  __shared__ __align__(128) __nv_bfloat16 sQ[QROWS * kDh];
+  __shared__ __align__(128) __nv_bfloat16 sK[2][kKeyTile * kDh];
+  __shared__ __align__(128) __nv_bfloat16 sV[2][kKeyTile * kDh];
+
+  const int q0 = blockIdx.x * QROWS;
+  const int head = blockIdx.y;
+  const long long grp_row = (long long)blockIdx.z * seq;
+  const __nv_bfloat16* qb = qkv + grp_row * kQkvLd + head * kDh;
+  const __nv_bfloat16* kb = qb + kOutLd;
+  const __nv_bfloat16* vb = qb + 2 * kOutLd;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int ntiles = (seq + kKeyTile - 1) / kKeyTile;
+
+  load_tile<NT>(sQ, qb + (long long)q0 * kQkvLd, QROWS, seq - q0);
+  load_tile<NT>(sK[0], kb, kKeyTile, seq);
+  load_tile<NT>(sV[0], vb, kKeyTile, seq);
+  cp_async_commit();
+
+  uint32_t qa[4][4];
+  float o[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  const float sc = 0.125f * 1.4426950408889634f;  // 1/sqrt(64) * log2(e)
+
+  for (int j = 0; j < ntiles; ++j) {
+    const int buf = j & 1;
+    if (j + 1 < ntiles) {
+      const int k0n = (j + 1) * kKeyTile;
+      load_tile<NT>(sK[buf ^ 1], kb + (long long)k0n * kQkvLd, kKeyTile, seq - k0n);
+      load_tile<NT>(sV[buf ^ 1], vb + (long long)k0n * kQkvLd, kKeyTile, seq - k0n);
+    }
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    if (j == 0) {
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const int r = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int c = kk * 16 + (lane >> 4) * 8;
+        ldsm_x4(qa[kk], sQ + swz(r, c));
+      }
+    }
+    // S = Q K^T for 64 keys: 8 n-tiles of 8 keys
+    float s[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
+#pragma unroll
+    for (int np = 0; np < 4; ++np) {  // pairs of n-tiles
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        uint32_t b[4];
+        const int m = lane >> 3;
+        const int key = np * 16 + (lane & 7) + (m >> 1) * 8;
+        const int c = kk * 16 + (m & 1) * 8;
+        ldsm_x4(b, sK[buf] + swz(key, c));
+        mma_bf16(s[2 * np], qa[kk], b[0], b[1]);
+        mma_bf16(s[2 * np + 1], qa[kk], b[2], b[3]);
+      }
+    }
+    // scale, mask the key tail, online softmax (rows g and g+8 of this warp)
+    const int kbase = j * kKeyTile;
+    float mx0 = m0, mx1 = m1;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int key = kbase + i * 8 + 2 * t + (e & 1);
+        s[i][e] = key < seq ? s[i][e] * sc : -INFINITY;
+      }
+      mx0 = fmaxf(mx0, fmaxf(s[i][0], s[i][1]));
+      mx1 = fmaxf(mx1, fmaxf(s[i][2], s[i][3]));
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float alpha0 = exp2f(m0 - mx0), alpha1 = exp2f(m1 - mx1);
+    m0 = mx0;
+    m1 = mx1;
+    float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      s[i][0] = exp2f(s[i][0] - mx0);
+      s[i][1] = exp2f(s[i][1] - mx0);
+      s[i][2] = exp2f(s[i][2] - mx1);
+      s[i][3] = exp2f(s[i][3] - mx1);
+      rs0 += s[i][0] + s[i][1];
+      rs1 += s[i][2] + s[i][3];
+    }
+    l0 = l0 * alpha0 + rs0;
+    l1 = l1 * alpha1 + rs1;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      o[i][0] *= alpha0; o[i][1] *= alpha0;
+      o[i][2] *= alpha1; o[i][3] *= alpha1;
+    }
+    // O += P V : 4 k-steps of 16 keys, 8 n-tiles of 8 head dims
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      uint32_t pa[4];
+      pa[0] = pack_bf16x2(s[2 * kk][0], s[2 * kk][1]);
+      pa[1] = pack_bf16x2(s[2 * kk][2], s[2 * kk][3]);
+      pa[2] = pack_bf16x2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      pa[3] = pack_bf16x2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+      for (int dp = 0; dp < 4; ++dp) {  // pairs of d n-tiles
+        uint32_t b[4];
+        const int m = lane >> 3;
+        const int key = kk * 16 + (lane & 7) + (m & 1) * 8;
+        const int c = dp * 16 + (m >> 1) * 8;
+        ldsm_x4_t(b, sV[buf] + swz(key, c));
+        mma_bf16(o[2 * dp], pa, b[0], b[1]);
+        mma_bf16(o[2 * dp + 1], pa, b[2], b[3]);
+      }
+    }
+    __syncthreads();
+  }
+  // row sums across the 4 lanes of a quad
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  const float inv0 = 1.f / l0, inv1 = 1.f / l1;
+  const int r0 = q0 + warp * 16 + g, r1 = r0 + 8;
+  __nv_bfloat16* ob = out + grp_row * kOutLd + head * kDh;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int c = i * 8 + 2 * t;
+    if (r0 < seq)
+      *reinterpret_cast<uint32_t*>(ob + (long long)r0 * kOutLd + c) = pack_bf16x2(o[i][0] * inv0, o[i][1] * inv0);
+    if (r1 < seq)
+      *reinterpret_cast<uint32_t*>(ob + (long long)r1 * kOutLd + c) = pack_bf16x2(o[i][2] * inv1, o[i][3] * inv1);
+  }
+}
+
+// One warp per (session, patch, head); lane owns head dims 2*lane, 2*lane+1.
+template <int TMAX>
+__global__ void __launch_bounds__(256) attention_temporal_kernel(const __nv_bfloat16* __restrict__ qkv,
+                                                                 __nv_bfloat16* __restrict__ out, int batch,
+                                                                 int T, int P) {
+  const long long w = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const long long total = (long long)batch * P * kHeads;
+  if (w >= total) return;
+  const int head = w % kHeads;
+  const long long bp = w / kHeads;
+  const int p = bp % P;
+  const long long b = bp / P;
+  const long long row0 = b * T * P + p;  // row of frame t = row0 + t * P
+  const int col = head * kDh + 2 * lane;
+
+  __nv_bfloat162 kr[TMAX], vr[TMAX];
+#pragma unroll
+  for (int s = 0; s < TMAX; ++s) {
+    if (s < T) {
+      const __nv_bfloat16* rp = qkv + (row0 + (long long)s * P) * kQkvLd + col;
+      kr[s] = *reinterpret_cast<const __nv_bfloat162*>(rp + kOutLd);
+      vr[s] = *reinterpret_cast<const __nv_bfloat162*>(rp + 2 * kOutLd);
+    }
+  }
+  const float sc = 0.125f * 1.4426950408889634f;
+#pragma unroll
+  for (int tq = 0; tq < TMAX; ++tq) {
+    if (tq < T) {
+      const float2 q = __bfloat1622float2(
+          *reinterpret_cast<const __nv_bfloat162*>(qkv + (row0 + (long long)tq * P) * kQkvLd + col));
+      float sc_[TMAX];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int s = 0; s <= tq; ++s) {
+        const float2 k = __bfloat1622float2(kr[s]);
+        float d = q.x * k.x + q.y * k.y;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+        sc_[s] = d * sc;
+        mx = fmaxf(mx, sc_[s]);
+      }
+      float l = 0.f, o0 = 0.f, o1 = 0.f;
+#pragma unroll
+      for (int s = 0; s <= tq; ++s) {
+        const float e = exp2f(sc_[s] - mx);
+        const float2 v = __bfloat1622float2(vr[s]);
+        l += e;
+        o0 = fmaf(e, v.x, o0);
+        o1 = fmaf(e, v.y, o1);
+      }
+      const float inv = 1.f / l;
+      *reinterpret_cast<uint32_t*>(out + (row0 + (long long)tq * P) * kOutLd + col) = pack_bf16x2(o0 * inv, o1 * inv);
+    }
+  }
+}
+
+}  // namespace
+
+int attention_full_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, int groups, int seq, cudaStream_t s) {
+  OASIS_REQUIRE(qkv && out, "attention_full: null pointer");
+  OASIS_REQUIRE(groups >= 0 && seq > 0, "attention_full: bad shape");
+  if (groups == 0) return OASIS_OK;
+  if (seq <= 160) {
+    constexpr int NW = 3;  // 48 query rows per CTA: 144 = 3 x 48
+    dim3 grid((seq + NW * 16 - 1) / (NW * 16), kHeads, groups);
+    attention_full_kernel<NW><<<grid, NW * 32, 0, s>>>(qkv, out, seq);
+  } else {
+    constexpr int NW = 4;
+    dim3 grid((seq + NW * 16 - 1) / (NW * 16), kHeads, groups);
+    attention_full_kernel<NW><<<grid, NW * 32, 0, s>>>(qkv, out, seq);
+  }
+  return check_launch("attention_full_kernel");
+}
+
+int attention_temporal_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, int batch, int frames, int P,
+                              cudaStream_t s) {
+  OASIS_REQUIRE(qkv && out, "attention_temporal: null pointer");
+  OASIS_REQUIRE(frames >= 1 && frames <= 32, "attention_temporal: frames=%d outside [1, 32]", frames);
+  const long long warps = (long long)batch * P * kHeads;
+  if (warps == 0) return OASIS_OK;
+  const int grid = (int)((warps * 32 + 255) / 256);
+  if (frames <= 2)
+    attention_temporal_kernel<2><<<grid, 256, 0, s>>>(qkv, out, batch, frames, P);
+  else if (frames <= 4)
+    attention_temporal_kernel<4><<<grid, 256, 0, s>>>(qkv, out, batch, frames, P);
+  else if (frames <= 8)
+    attention_temporal_kernel<8><<<grid, 256, 0, s>>>(qkv, out, batch, frames, P);
+  else if (frames <= 16)
+    attention_temporal_kernel<16><<<grid, 256, 0, s>>>(qkv, out, batch, frames, P);
+  else
+    attention_temporal_kernel<32><<<grid, 256, 0, s>>>(qkv, out, batch, frames, P);
+  return check_launch("attention_temporal_kernel");
+}
+
+}  // namespace oasis

@@ -1,0 +1,503 @@
+// C ABI of the library (include/oasis_b200.h): argument checking, workspace
+// carving, and the composite DiT / DDIM-step / VAE-decode drivers that issue the
+// kernel sequence of one sub-block, one step and one decode on a caller stream.
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include "../../include/oasis_b200.h"
+#include "gemm.cuh"
+#include "pointwise.cuh"
+#include "status.h"
+
+namespace oasis {
+
+static thread_local char g_msg[512] = "";
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int read_device_error(int reset);  // gemm.cu
+
+namespace {
+
+constexpr int kD = 1024;
+constexpr int kP = 144;        // tokens per DiT frame
+constexpr int kOut = 64;       // patch vector (2 x 2 x 16)
+constexpr int kMlp = 4096;
+constexpr int kVaeTok = 576;
+constexpr float kScalingFactor = 0.07843137255f;
+
+inline cudaStream_t S(oasis_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Bump allocator over a caller workspace (256-byte aligned slices).
+struct Carve {
+  uint8_t* base;
+  size_t used = 0;
+  size_t cap;
+  Carve(void* b, size_t c) : base(static_cast<uint8_t*>(b)), cap(c) {}
+  template <class T>
+  T* take(size_t count) {
+    used = (used + 255) & ~size_t(255);
+    T* p = base ? reinterpret_cast<T*>(base + used) : nullptr;
+    used += count * sizeof(T);
+    return p;
+  }
+  bool ok() const { return used <= cap; }
+};
+
+size_t splitk_bytes_dit(int B, int T, bool last_only) {
+  const int F = B * T, M = F * kP;
+  size_t m = 0;
+  auto upd = [&](size_t x) { m = x > m ? x : m; };
+  upd(gemm_workspace_bytes(M, 3 * kD, kD));
+  upd(gemm_workspace_bytes(M, kD, kD));
+  upd(gemm_workspace_bytes(M, kMlp, kD));
+  upd(gemm_workspace_bytes(M, kD, kMlp));
+  upd(gemm_workspace_bytes(F, OASIS_ADALN_ROWS, kD));
+  upd(gemm_workspace_bytes(last_only ? B * kP : M, kOut, kD));
+  return m;
+}
+
+struct DitScratch {
+  __nv_bfloat16* silu;
+  float* adaln;
+  __nv_bfloat16* xn;
+  __nv_bfloat16* qkv;
+  __nv_bfloat16* attn;
+  __nv_bfloat16* h;
+  void* splitk;
+  size_t splitk_bytes;
+};
+
+size_t carve_dit(Carve& c, int B, int T, DitScratch* s) {
+  const size_t F = (size_t)B * T, M = F * kP;
+  DitScratch d;
+  d.silu = c.take<__nv_bfloat16>(F * kD);
+  d.adaln = c.take<float>(F * OASIS_ADALN_ROWS);
+  d.xn = c.take<__nv_bfloat16>(M * kD);
+  d.qkv = c.take<__nv_bfloat16>(M * 3 * kD);
+  d.attn = c.take<__nv_bfloat16>(M * kD);
+  d.h = c.take<__nv_bfloat16>(M * kMlp);
+  d.splitk_bytes = splitk_bytes_dit(B, T, false);
+  d.splitk = d.splitk_bytes ? c.take<uint8_t>(d.splitk_bytes) : nullptr;
+  if (s) *s = d;
+  return c.used;
+}
+
+GemmProblem gemm(const void* A, const void* W, int M, int N, int K, void* ws, size_t ws_bytes) {
+  GemmProblem p;
+  p.A = A;
+  p.lda = K;
+  p.W = W;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.workspace = ws;
+  p.workspace_bytes = ws_bytes;
+  return p;
+}
+
+int dit_forward_impl(const OasisDitWeights* w, const OasisDitArgs* a, cudaStream_t st) {
+  OASIS_REQUIRE(w && a, "dit_forward: null argument");
+  const int B = a->batch, T = a->frames;
+  OASIS_REQUIRE(B > 0 && T > 0 && T <= 32, "dit_forward: batch=%d frames=%d (need frames in [1, 32])", B, T);
+  OASIS_REQUIRE(a->z && a->cond && a->v_out, "dit_forward: null tensor");
+  Carve c(a->workspace, a->workspace_bytes);
+  DitScratch s;
+  carve_dit(c, B, T, &s);
+  if (!a->workspace || !c.ok())
+    return set_error(OASIS_ERR_WORKSPACE, "dit_forward: workspace %zu bytes < %zu", a->workspace_bytes, c.used);
+  const int F = B * T, M = F * kP;
+  const int nsub = w->num_subblocks;
+  OASIS_REQUIRE(nsub >= 0 && nsub <= OASIS_DIT_SUBBLOCKS, "dit_forward: num_subblocks=%d", nsub);
+  const long long ldm = (long long)nsub * OASIS_ADALN_WIDTH + 2 * kD;
+
+  // adaLN parameters of every sub-block and the final layer, all frames, one GEMM.
+  OASIS_TRY(silu_bf16_launch(a->cond, s.silu, (long long)F * kD, st));
+  {
+    GemmProblem p = gemm(s.silu, w->adaln_w, F, (int)ldm, kD, s.splitk, s.splitk_bytes);
+    p.epi.mode = kEpiF32;
+    p.epi.out = s.adaln;
+    p.epi.ldo = ldm;
+    p.epi.bias = w->adaln_b;
+    OASIS_TRY(gemm_launch(p, st));
+  }
+
+  for (int i = 0; i < nsub; ++i) {
+    const OasisDitSubBlock& sb = w->sub[i];
+    const bool spatial = (i % 2) == 0;
+    const long long off = (long long)i * OASIS_ADALN_WIDTH;
+    LayerNormParams ln;
+    ln.rows_out = M;
+    ln.P = kP;
+    ln.in_group = kP;
+    ln.mod = s.adaln;
+    ln.ld_mod = ldm;
+    ln.shift_off = off;
+    ln.scale_off = off + kD;
+    OASIS_TRY(layernorm_launch(a->z, s.xn, ln, st));
+    {
+      GemmProblem p = gemm(s.xn, sb.qkv_w, M, 3 * kD, kD, s.splitk, s.splitk_bytes);
+      p.epi.mode = kEpiRopeBF16;
+      p.epi.out = s.qkv;
+      p.epi.ldo = 3 * kD;
+      p.epi.rope = spatial ? w->rope_spatial : w->rope_temporal;
+      p.epi.rope_div = spatial ? 1 : kP;
+      p.epi.rope_mod = spatial ? kP : T;
+      OASIS_TRY(gemm_launch(p, st));
+    }
+    if (spatial)
+      OASIS_TRY(attention_full_launch(s.qkv, s.attn, F, kP, st));
+    else
+      OASIS_TRY(attention_temporal_launch(s.qkv, s.attn, B, T, kP, st));
+    {
+      GemmProblem p = gemm(s.attn, sb.out_w, M, kD, kD, s.splitk, s.splitk_bytes);
+      p.epi.mode = kEpiGatedResid;
+      p.epi.out = a->z;
+      p.epi.ldo = kD;
+      p.epi.resid = a->z;
+      p.epi.ldr = kD;
+      p.epi.bias = sb.out_b;
+      p.epi.gate = s.adaln + off + 2 * kD;
+      p.epi.ldg = ldm;
+      p.epi.rows_per_frame = kP;
+      OASIS_TRY(gemm_launch(p, st));
+    }
+    ln.shift_off = off + 3 * kD;
+    ln.scale_off = off + 4 * kD;
+    OASIS_TRY(layernorm_launch(a->z, s.xn, ln, st));
+    {
+      GemmProblem p = gemm(s.xn, sb.fc1_w, M, kMlp, kD, s.splitk, s.splitk_bytes);
+      p.epi.mode = kEpiGeluTanhBF16;
+      p.epi.out = s.h;
+      p.epi.ldo = kMlp;
+      p.epi.bias = sb.fc1_b;
+      OASIS_TRY(gemm_launch(p, st));
+    }
+    {
+      GemmProblem p = gemm(s.h, sb.fc2_w, M, kD, kMlp, s.splitk, s.splitk_bytes);
+      p.epi.mode = kEpiGatedResid;
+      p.epi.out = a->z;
+      p.epi.ldo = kD;
+      p.epi.resid = a->z;
+      p.epi.ldr = kD;
+      p.epi.bias = sb.fc2_b;
+      p.epi.gate = s.adaln + off + 5 * kD;
+      p.epi.ldg = ldm;
+      p.epi.rows_per_frame = kP;
+      OASIS_TRY(gemm_launch(p, st));
+    }
+  }
+
+  // Final layer: LN + final adaLN modulate (only the rows that are returned) + linear.
+  const long long foff = (long long)nsub * OASIS_ADALN_WIDTH;
+  LayerNormParams ln;
+  ln.P = kP;
+  ln.mod = s.adaln;
+  ln.ld_mod = ldm;
+  ln.shift_off = foff;
+  ln.scale_off = foff + kD;
+  if (a->last_frame_only) {
+    ln.rows_out = B * kP;
+    ln.in_group = (long long)T * kP;
+    ln.in_off = (long long)(T - 1) * kP;
+    ln.frame_mul = T;
+    ln.frame_add = T - 1;
+  } else {
+    ln.rows_out = M;
+    ln.in_group = kP;
+  }
+  OASIS_TRY(layernorm_launch(a->z, s.xn, ln, st));
+  GemmProblem p = gemm(s.xn, w->final_w, ln.rows_out, kOut, kD, s.splitk, s.splitk_bytes);
+  p.epi.mode = kEpiF32;
+  p.epi.out = a->v_out;
+  p.epi.ldo = kOut;
+  p.epi.bias = w->final_b;
+  return gemm_launch(p, st);
+}
+
+size_t step_ws(int B, int T, DitScratch* s, float** z, float** v, void* base, size_t cap) {
+  Carve c(base, cap);
+  carve_dit(c, B, T, s);
+  float* zz = c.take<float>((size_t)B * T * kP * kD);
+  float* vv = c.take<float>((size_t)B * kP * kOut);
+  if (z) *z = zz;
+  if (v) *v = vv;
+  return c.used;
+}
+
+struct VaeScratch {
+  float* z;
+  __nv_bfloat16* xn;
+  __nv_bfloat16* qkv;
+  __nv_bfloat16* attn;
+  __nv_bfloat16* h;
+  void* splitk;
+  size_t splitk_bytes;
+};
+
+size_t carve_vae(Carve& c, int B, VaeScratch* s) {
+  const size_t R = (size_t)B * kVaeTok;
+  VaeScratch d;
+  d.z = c.take<float>(R * kD);
+  d.xn = c.take<__nv_bfloat16>(R * kD);
+  d.qkv = c.take<__nv_bfloat16>(R * 3 * kD);
+  d.attn = c.take<__nv_bfloat16>(R * kD);
+  d.h = c.take<__nv_bfloat16>(R * kMlp);
+  size_t m = 0;
+  auto upd = [&](size_t x) { m = x > m ? x : m; };
+  upd(gemm_workspace_bytes((int)R, 3 * kD, kD));
+  upd(gemm_workspace_bytes((int)R, kD, kD));
+  upd(gemm_workspace_bytes((int)R, kMlp, kD));
+  upd(gemm_workspace_bytes((int)R, kD, kMlp));
+  upd(gemm_workspace_bytes((int)R, 1200, kD));
+  d.splitk_bytes = m;
+  d.splitk = m ? c.take<uint8_t>(m) : nullptr;
+  if (s) *s = d;
+  return c.used;
+}
+
+int vae_decode_impl(const OasisVaeWeights* w, const OasisVaeArgs* a, cudaStream_t st) {
+  OASIS_REQUIRE(w && a, "vae_decode: null argument");
+  const int B = a->batch;
+  OASIS_REQUIRE(B > 0, "vae_decode: batch=%d", B);
+  OASIS_REQUIRE(a->latent && a->image, "vae_decode: null tensor");
+  Carve c(a->workspace, a->workspace_bytes);
+  VaeScratch s;
+  carve_vae(c, B, &s);
+  if (!a->workspace || !c.ok())
+    return set_error(OASIS_ERR_WORKSPACE, "vae_decode: workspace %zu bytes < %zu", a->workspace_bytes, c.used);
+  const int R = B * kVaeTok;
+  OASIS_TRY(post_quant_launch(a->latent, w->post_quant_w, w->post_quant_b, s.z, R, st));
+  LayerNormParams ln;
+  ln.rows_out = R;
+  ln.P = R;
+  ln.in_group = R;
+  OASIS_REQUIRE(w->num_blocks >= 0 && w->num_blocks <= OASIS_VAE_BLOCKS, "vae_decode: num_blocks=%d", w->num_blocks);
+  for (int i = 0; i < w->num_blocks; ++i) {
+    const OasisVaeBlock& b = w->blk[i];
+    ln.affine_w = b.norm1_w;
+    ln.affine_b = b.norm1_b;
+    OASIS_TRY(layernorm_launch(s.z, s.xn, ln, st));
+    {
+      GemmProblem p = gemm(s.xn, b.qkv_w, R, 3 * kD, kD, s.splitk, s.splitk_bytes);
+      p.epi.mode = kEpiRopeBF16;
+      p.epi.out = s.qkv;
+      p.epi.ldo = 3 * kD;
+      p.epi.bias = b.qkv_b;
+      p.epi.rope = w->rope;
+      p.epi.rope_div = 1;
+      p.epi.rope_mod = kVaeTok;
+      OASIS_TRY(gemm_launch(p, st));
+    }
+    OASIS_TRY(attention_full_launch(s.qkv, s.attn, B, kVaeTok, st));
+    {
+      GemmProblem p = gemm(s.attn, b.proj_w, R, kD, kD, s.splitk, s.splitk_bytes);
+      p.epi.mode = kEpiResid;
+      p.epi.out = s.z;
+      p.epi.ldo = kD;
+      p.epi.resid = s.z;
+      p.epi.ldr = kD;
+      p.epi.bias = b.proj_b;
+      OASIS_TRY(gemm_launch(p, st));
+    }
+    ln.affine_w = b.norm2_w;
+    ln.affine_b = b.norm2_b;
+    OASIS_TRY(layernorm_launch(s.z, s.xn, ln, st));
+    {
+      GemmProblem p = gemm(s.xn, b.fc1_w, R, kMlp, kD, s.splitk, s.splitk_bytes);
+      p.epi.mode = kEpiGeluErfBF16;
+      p.epi.out = s.h;
+      p.epi.ldo = kMlp;
+      p.epi.bias = b.fc1_b;
+      OASIS_TRY(gemm_launch(p, st));
+    }
+    {
+      GemmProblem p = gemm(s.h, b.fc2_w, R, kD, kMlp, s.splitk, s.splitk_bytes);
+      p.epi.mode = kEpiResid;
+      p.epi.out = s.z;
+      p.epi.ldo = kD;
+      p.epi.resid = s.z;
+      p.epi.ldr = kD;
+      p.epi.bias = b.fc2_b;
+      OASIS_TRY(gemm_launch(p, st));
+    }
+  }
+  ln.affine_w = w->norm_w;
+  ln.affine_b = w->norm_b;
+  OASIS_TRY(layernorm_launch(s.z, s.xn, ln, st));
+  GemmProblem p = gemm(s.xn, w->pred_w, R, 1200, kD, s.splitk, s.splitk_bytes);
+  p.epi.mode = kEpiImage;
+  p.epi.out = a->image;
+  p.epi.bias = w->pred_b;
+  p.epi.img_grid_w = 32;
+  p.epi.img_tokens = kVaeTok;
+  p.epi.img_patch = 20;
+  return gemm_launch(p, st);
+}
+
+}  // namespace
+}  // namespace oasis
+
+using namespace oasis;
+
+extern "C" {
+
+const char* oasis_last_error(void) { return g_msg; }
+
+int oasis_device_error(int reset) { return read_device_error(reset); }
+
+const char* oasis_version(void) { return "oasis_b200 0.1 (sm_100a)"; }
+
+size_t oasis_dit_workspace_size(int batch, int frames) {
+  Carve c(nullptr, 0);
+  return carve_dit(c, batch, frames, nullptr) + 256;
+}
+
+int oasis_dit_forward(const OasisDitWeights* w, const OasisDitArgs* a, oasis_stream_t stream) {
+  g_msg[0] = 0;
+  return dit_forward_impl(w, a, S(stream));
+}
+
+int oasis_ddim_update(float* chunk, const float* v, const OasisDdimCoeffs* c, long long n, oasis_stream_t stream) {
+  OASIS_REQUIRE(c, "ddim_update: null coefficients");
+  DdimCoeffs k{c->at_sqrt, c->one_minus_at_sqrt, c->inv_at_sqrt, c->inv_sigma, c->an_sqrt, c->one_minus_an_sqrt};
+  return ddim_launch(chunk, v, k, n, S(stream));
+}
+
+size_t oasis_step_workspace_size(int batch, int frames) {
+  return step_ws(batch, frames, nullptr, nullptr, nullptr, nullptr, 0) + 256;
+}
+
+int oasis_ddim_step(const OasisDitWeights* w, const OasisStepArgs* a, oasis_stream_t stream) {
+  g_msg[0] = 0;
+  OASIS_REQUIRE(w && a, "ddim_step: null argument");
+  const int B = a->batch, T = a->frames;
+  OASIS_REQUIRE(B > 0 && T > 0 && T <= 32, "ddim_step: batch=%d frames=%d", B, T);
+  OASIS_REQUIRE(a->chunk && a->cond, "ddim_step: null tensor");
+  OASIS_REQUIRE(T == 1 || a->context_z, "ddim_step: frames > 1 needs context_z");
+  DitScratch s;
+  float *z, *v;
+  const size_t need = step_ws(B, T, &s, &z, &v, a->workspace, a->workspace_bytes);
+  if (!a->workspace || need > a->workspace_bytes)
+    return set_error(OASIS_ERR_WORKSPACE, "ddim_step: workspace %zu bytes < %zu", a->workspace_bytes, need);
+  cudaStream_t st = S(stream);
+  if (T > 1) {
+    const size_t ctx_bytes = (size_t)(T - 1) * kP * kD * sizeof(float);
+    cudaError_t e = cudaMemcpy2DAsync(z, (size_t)T * kP * kD * sizeof(float), a->context_z, ctx_bytes, ctx_bytes, B,
+                                      cudaMemcpyDeviceToDevice, st);
+    if (e != cudaSuccess) return set_error(OASIS_ERR_CUDA, "ddim_step: context copy: %s", cudaGetErrorString(e));
+  }
+  PatchEmbedParams pe;
+  pe.rows = B * kP;
+  pe.P = kP;
+  pe.out_group = (long long)T * kP;
+  pe.out_off = (long long)(T - 1) * kP;
+  OASIS_TRY(patch_embed_launch(a->chunk, w->embed_w, w->embed_b, z, pe, st));
+  OasisDitArgs da{B, T, z, a->cond, v, 1, a->workspace, a->workspace_bytes};
+  OASIS_TRY(dit_forward_impl(w, &da, st));
+  DdimCoeffs k{a->coeffs.at_sqrt, a->coeffs.one_minus_at_sqrt, a->coeffs.inv_at_sqrt, a->coeffs.inv_sigma,
+               a->coeffs.an_sqrt, a->coeffs.one_minus_an_sqrt};
+  return ddim_launch(a->chunk, v, k, (long long)B * kP * kOut, st);
+}
+
+int oasis_patch_embed(const OasisDitWeights* w, const float* patches, int rows, float* z, long long out_group,
+                      long long out_off, oasis_stream_t stream) {
+  OASIS_REQUIRE(w, "patch_embed: null weights");
+  PatchEmbedParams pe;
+  pe.rows = rows;
+  pe.P = kP;
+  pe.out_group = out_group;
+  pe.out_off = out_off;
+  return patch_embed_launch(patches, w->embed_w, w->embed_b, z, pe, S(stream));
+}
+
+int oasis_bridge_unpatchify(const float* chunk, float* latent, int batch, oasis_stream_t stream) {
+  return bridge_launch(chunk, latent, batch, 1.0f / kScalingFactor, S(stream));
+}
+
+size_t oasis_vae_workspace_size(int batch) {
+  Carve c(nullptr, 0);
+  return carve_vae(c, batch, nullptr) + 256;
+}
+
+int oasis_vae_decode(const OasisVaeWeights* w, const OasisVaeArgs* a, oasis_stream_t stream) {
+  g_msg[0] = 0;
+  return vae_decode_impl(w, a, S(stream));
+}
+
+int oasis_gemm(const OasisGemmArgs* a, oasis_stream_t stream) {
+  OASIS_REQUIRE(a, "gemm: null args");
+  GemmProblem p;
+  p.A = a->a;
+  p.lda = a->lda ? a->lda : a->k;
+  p.W = a->w;
+  p.M = a->m;
+  p.N = a->n;
+  p.K = a->k;
+  p.epi.mode = a->mode;
+  p.epi.out = a->out;
+  p.epi.ldo = a->ldo ? a->ldo : a->n;
+  p.epi.bias = a->bias;
+  p.epi.resid = a->resid;
+  p.epi.ldr = a->ldr ? a->ldr : a->n;
+  p.epi.gate = a->gate;
+  p.epi.ldg = a->ldg;
+  p.epi.rows_per_frame = a->rows_per_frame > 0 ? a->rows_per_frame : 1;
+  p.epi.rope = a->rope;
+  p.epi.rope_div = a->rope_div > 0 ? a->rope_div : 1;
+  p.epi.rope_mod = a->rope_mod > 0 ? a->rope_mod : 1;
+  p.block_n = a->block_n;
+  p.splits = a->splits;
+  p.workspace = a->workspace;
+  p.workspace_bytes = a->workspace_bytes;
+  OASIS_REQUIRE(a->mode >= 0 && a->mode <= kEpiImage, "gemm: mode %d unknown", a->mode);
+  return gemm_launch(p, S(stream));
+}
+
+size_t oasis_gemm_workspace_size(int m, int n, int k) { return gemm_workspace_bytes(m, n, k); }
+
+int oasis_layernorm(const OasisLayerNormArgs* a, oasis_stream_t stream) {
+  OASIS_REQUIRE(a, "layernorm: null args");
+  LayerNormParams p;
+  p.rows_out = a->rows_out;
+  p.P = a->P > 0 ? a->P : 1;
+  p.in_group = a->in_group ? a->in_group : p.P;
+  p.in_off = a->in_off;
+  p.frame_mul = a->frame_mul ? a->frame_mul : 1;
+  p.frame_add = a->frame_add;
+  p.eps = a->eps > 0 ? a->eps : 1e-6f;
+  p.mod = a->mod;
+  p.ld_mod = a->ld_mod;
+  p.shift_off = a->shift_off;
+  p.scale_off = a->scale_off;
+  p.affine_w = a->affine_w;
+  p.affine_b = a->affine_b;
+  return layernorm_launch(a->x, static_cast<__nv_bfloat16*>(a->y), p, S(stream));
+}
+
+int oasis_silu_bf16(const float* x, void* y, long long n, oasis_stream_t stream) {
+  return silu_bf16_launch(x, static_cast<__nv_bfloat16*>(y), n, S(stream));
+}
+
+int oasis_attention_spatial(const void* qkv, void* out, int groups, int seq, oasis_stream_t stream) {
+  return attention_full_launch(static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out), groups,
+                               seq, S(stream));
+}
+
+int oasis_attention_temporal(const void* qkv, void* out, int batch, int frames, oasis_stream_t stream) {
+  return attention_temporal_launch(static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out), batch,
+                                   frames, kP, S(stream));
+}
+
+int oasis_post_quant(const float* latent, const float* w, const float* b, float* z, int rows, oasis_stream_t stream) {
+  return post_quant_launch(latent, w, b, z, rows, S(stream));
+}
+
+}  // extern "C"

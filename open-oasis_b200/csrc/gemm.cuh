@@ -1,0 +1,60 @@
+// Host-visible declarations for the tcgen05 GEMM family.
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace oasis {
+
+// Epilogue variants fused into the GEMM (acc = A . W^T in fp32, +bias[n] first).
+enum EpiMode : int {
+  kEpiF32 = 0,          // out_f32 = acc + bias
+  kEpiBF16 = 1,         // out_bf16 = acc + bias
+  kEpiGeluTanhBF16 = 2, // out_bf16 = gelu_tanh(acc + bias)
+  kEpiGeluErfBF16 = 3,  // out_bf16 = gelu_erf(acc + bias)
+  kEpiGatedResid = 4,   // out_f32 = resid + gate[frame(r), n] * (acc + bias)
+  kEpiResid = 5,        // out_f32 = resid + acc + bias
+  kEpiRopeBF16 = 6,     // out_bf16 = rope(acc + bias) on the q and k thirds of a qkv row
+  kEpiImage = 7,        // VAE predictor: unpatchify 20x20x3 patches into a clamped image
+};
+
+struct EpiParams {
+  int mode = kEpiF32;
+  void* out = nullptr;
+  long long ldo = 0;              // elements between output rows
+  const float* bias = nullptr;    // [N] or null
+  const float* resid = nullptr;   // residual input (may alias out)
+  long long ldr = 0;
+  const float* gate = nullptr;    // gated residual: gate[(r / rows_per_frame) * ldg + n]
+  long long ldg = 0;
+  int rows_per_frame = 1;
+  const float* rope = nullptr;    // (cos, sin) pairs: rope[(pos * 32 + pair) * 2 + {0,1}]
+  int rope_div = 1;               // pos = (r / rope_div) % rope_mod
+  int rope_mod = 1;
+  int rope_dim = 1024;            // q occupies [0, rope_dim), k [rope_dim, 2 rope_dim)
+  int img_grid_w = 32;            // image mode: tokens per patch row
+  int img_tokens = 576;           // image mode: tokens per frame
+  int img_patch = 20;             // image mode: patch edge in pixels
+};
+
+struct GemmProblem {
+  const void* A = nullptr;  // bf16 [M, K], row stride lda elements
+  long long lda = 0;
+  const void* W = nullptr;  // bf16 [N, K] (nn.Linear layout), row stride K
+  int M = 0, N = 0, K = 0;
+  EpiParams epi;
+  int block_n = 0;          // 0 = heuristic, else 64/128/256
+  int splits = 0;           // 0 = heuristic, 1 = no split-K
+  void* workspace = nullptr;  // split-K partials + tile counters (may be null -> no split)
+  size_t workspace_bytes = 0;
+};
+
+// Returns 0 or a negative oasis status code.
+int gemm_launch(const GemmProblem& p, cudaStream_t stream);
+
+// Bytes of split-K workspace the heuristic may want for an M x N x K problem.
+size_t gemm_workspace_bytes(int M, int N, int K);
+
+int num_sms();
+
+}  // namespace oasis

@@ -1,0 +1,230 @@
+// Memory-bound kernels of the frame path: LayerNorm (+adaLN modulate or affine),
+// SiLU of the conditioning, the noisy-chunk patch embed, the DDIM update, the
+// DiT->VAE bridge (unpatchify + 1/scaling) and the VAE post-quant projection.
+//
+// All are HBM-bound row/element kernels: fp32 vectorised loads (float4),
+// warp-shuffle reductions, bf16 stores where the consumer is a GEMM operand.
+#include "common.cuh"
+#include "pointwise.cuh"
+#include "status.h"
+
+namespace oasis {
+namespace {
+
+constexpr int D = 1024;  // model width of both the DiT and the VAE decoder
+
+// One warp per output row. x is fp32 [*, 1024]; y is bf16 [rows_out, 1024].
+// Row map (gathers the last frame of each session for the final layer):
+//   in_row = (r / P) * in_group + in_off + r % P
+//   frame  = (r / P) * frame_mul + frame_add
+// Modulated: y = LN(x) * scale1p[frame] + shift[frame] (scale1p holds 1+scale).
+// Affine:    y = LN(x) * w + b.
+__global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y,
+                                                        LayerNormParams p) {
+  const int warp_global = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp_global >= p.rows_out) return;
+  const int r = warp_global;
+  const int grp = r / p.P, within = r - grp * p.P;
+  const long long in_row = (long long)grp * p.in_group + p.in_off + within;
+  const float* xr = x + in_row * D;
+
+  float4 v[8];
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    v[j] = reinterpret_cast<const float4*>(xr)[lane + 32 * j];
+    s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float mean = s * (1.f / D);
+  float q = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float a = v[j].x - mean, b = v[j].y - mean, c = v[j].z - mean, d = v[j].w - mean;
+    q += (a * a + b * b) + (c * c + d * d);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+  const float rstd = rsqrtf(q * (1.f / D) + p.eps);
+
+  const float* mul;
+  const float* add;
+  if (p.affine_w) {
+    mul = p.affine_w;
+    add = p.affine_b;
+  } else {
+    const long long frame = (long long)grp * p.frame_mul + p.frame_add;
+    mul = p.mod + frame * p.ld_mod + p.scale_off;
+    add = p.mod + frame * p.ld_mod + p.shift_off;
+  }
+  __nv_bfloat16* yr = y + (long long)r * D;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int c = 4 * (lane + 32 * j);
+    const float4 m = *reinterpret_cast<const float4*>(mul + c);
+    const float4 a = add ? *reinterpret_cast<const float4*>(add + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const float o0 = (v[j].x - mean) * rstd * m.x + a.x;
+    const float o1 = (v[j].y - mean) * rstd * m.y + a.y;
+    const float o2 = (v[j].z - mean) * rstd * m.z + a.z;
+    const float o3 = (v[j].w - mean) * rstd * m.w + a.w;
+    *reinterpret_cast<uint2*>(yr + c) = make_uint2(pack_bf16x2(o0, o1), pack_bf16x2(o2, o3));
+  }
+}
+
+__global__ void silu_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, long long n4) {
+  long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  for (; i < n4; i += (long long)gridDim.x * blockDim.x) {
+    const float4 a = reinterpret_cast<const float4*>(x)[i];
+    const float s0 = a.x / (1.f + __expf(-a.x));
+    const float s1 = a.y / (1.f + __expf(-a.y));
+    const float s2 = a.z / (1.f + __expf(-a.z));
+    const float s3 = a.w / (1.f + __expf(-a.w));
+    reinterpret_cast<uint2*>(y)[i] = make_uint2(pack_bf16x2(s0, s1), pack_bf16x2(s2, s3));
+  }
+}
+
+// z[out_row, :] = chunk[r, :64] . W[64, 1024] + b, fp32 throughout.
+// Block: 256 threads x 4 columns = one full row width; kRows rows per block.
+constexpr int kEmbedRows = 16;
+__global__ void __launch_bounds__(256) patch_embed_kernel(const float* __restrict__ chunk, const float* __restrict__ w,
+                                                          const float* __restrict__ b, float* __restrict__ z,
+                                                          PatchEmbedParams p) {
+  __shared__ float xs[kEmbedRows][64];
+  const int r0 = blockIdx.x * kEmbedRows;
+  for (int i = threadIdx.x; i < kEmbedRows * 64; i += 256) {
+    const int rr = r0 + i / 64;
+    xs[i / 64][i % 64] = rr < p.rows ? chunk[(long long)rr * 64 + (i % 64)] : 0.f;
+  }
+  __syncthreads();
+  const int c = threadIdx.x * 4;
+  float4 acc[kEmbedRows];
+  const float4 bias = b ? *reinterpret_cast<const float4*>(b + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < kEmbedRows; ++i) acc[i] = bias;
+#pragma unroll 4
+  for (int k = 0; k < 64; ++k) {
+    const float4 wk = __ldg(reinterpret_cast<const float4*>(w + k * D + c));
+#pragma unroll
+    for (int i = 0; i < kEmbedRows; ++i) {
+      const float xv = xs[i][k];
+      acc[i].x = fmaf(xv, wk.x, acc[i].x);
+      acc[i].y = fmaf(xv, wk.y, acc[i].y);
+      acc[i].z = fmaf(xv, wk.z, acc[i].z);
+      acc[i].w = fmaf(xv, wk.w, acc[i].w);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kEmbedRows; ++i) {
+    const int r = r0 + i;
+    if (r >= p.rows) break;
+    const int grp = r / p.P, within = r - grp * p.P;
+    const long long out_row = (long long)grp * p.out_group + p.out_off + within;
+    *reinterpret_cast<float4*>(z + out_row * D + c) = acc[i];
+  }
+}
+
+__global__ void ddim_kernel(float* __restrict__ chunk, const float* __restrict__ v, DdimCoeffs c, long long n) {
+  long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  for (; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const float x = chunk[i];
+    const float x_start = c.at_sqrt * x - c.one_minus_at_sqrt * v[i];
+    const float x_noise = (c.inv_at_sqrt * x - x_start) * c.inv_sigma;
+    chunk[i] = c.an_sqrt * x_start + c.one_minus_an_sqrt * x_noise;
+  }
+}
+
+// chunk [B, 144, 64] in (h, w, p, q, c) order -> latent tokens [B, 576, 16]:
+// latent[b, (2h+p)*32 + (2w+q), c] = chunk[b, h*16+w, p*32 + q*16 + c] * inv_scale.
+__global__ void bridge_kernel(const float* __restrict__ chunk, float* __restrict__ lat, int batch, float inv_scale) {
+  const long long n = (long long)batch * 576 * 16;
+  long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  for (; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const int c = i & 15;
+    const long long t = i >> 4;
+    const int tok = t % 576;
+    const long long bidx = t / 576;
+    const int row = tok >> 5, col = tok & 31;
+    const int h = row >> 1, pp = row & 1, w = col >> 1, qq = col & 1;
+    lat[i] = chunk[(bidx * 144 + h * 16 + w) * 64 + pp * 32 + qq * 16 + c] * inv_scale;
+  }
+}
+
+// z[r, :] = lat[r, :16] . W[16, 1024] + b  (VAE post_quant_conv as a linear map)
+__global__ void __launch_bounds__(256) post_quant_kernel(const float* __restrict__ lat, const float* __restrict__ w,
+                                                         const float* __restrict__ b, float* __restrict__ z, int rows) {
+  const int r = blockIdx.x;
+  if (r >= rows) return;
+  __shared__ float xs[16];
+  if (threadIdx.x < 16) xs[threadIdx.x] = lat[(long long)r * 16 + threadIdx.x];
+  __syncthreads();
+  const int c = threadIdx.x * 4;
+  float4 acc = b ? *reinterpret_cast<const float4*>(b + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    const float4 wk = __ldg(reinterpret_cast<const float4*>(w + k * D + c));
+    acc.x = fmaf(xs[k], wk.x, acc.x);
+    acc.y = fmaf(xs[k], wk.y, acc.y);
+    acc.z = fmaf(xs[k], wk.z, acc.z);
+    acc.w = fmaf(xs[k], wk.w, acc.w);
+  }
+  *reinterpret_cast<float4*>(z + (long long)r * D + c) = acc;
+}
+
+int grid_for(long long n, int threads) {
+  long long g = (n + threads - 1) / threads;
+  const long long cap = (long long)num_sms_cached() * 16;
+  return (int)(g < cap ? (g > 0 ? g : 1) : cap);
+}
+
+}  // namespace
+
+int layernorm_launch(const float* x, __nv_bfloat16* y, const LayerNormParams& p, cudaStream_t s) {
+  OASIS_REQUIRE(x && y, "layernorm: null pointer");
+  OASIS_REQUIRE(p.rows_out >= 0 && p.P > 0, "layernorm: bad row map");
+  OASIS_REQUIRE(p.affine_w || p.mod, "layernorm: need affine weights or a modulation table");
+  if (p.rows_out == 0) return OASIS_OK;
+  const int warps_per_block = 8;
+  const int grid = (p.rows_out + warps_per_block - 1) / warps_per_block;
+  layernorm_kernel<<<grid, 32 * warps_per_block, 0, s>>>(x, y, p);
+  return check_launch("layernorm_kernel");
+}
+
+int silu_bf16_launch(const float* x, __nv_bfloat16* y, long long n, cudaStream_t s) {
+  OASIS_REQUIRE(n % 4 == 0, "silu: n must be a multiple of 4");
+  if (n == 0) return OASIS_OK;
+  silu_bf16_kernel<<<grid_for(n / 4, 256), 256, 0, s>>>(x, y, n / 4);
+  return check_launch("silu_bf16_kernel");
+}
+
+int patch_embed_launch(const float* chunk, const float* w, const float* b, float* z, const PatchEmbedParams& p,
+                       cudaStream_t s) {
+  OASIS_REQUIRE(chunk && w && z, "patch_embed: null pointer");
+  if (p.rows == 0) return OASIS_OK;
+  patch_embed_kernel<<<(p.rows + kEmbedRows - 1) / kEmbedRows, 256, 0, s>>>(chunk, w, b, z, p);
+  return check_launch("patch_embed_kernel");
+}
+
+int ddim_launch(float* chunk, const float* v, const DdimCoeffs& c, long long n, cudaStream_t s) {
+  OASIS_REQUIRE(chunk && v, "ddim: null pointer");
+  if (n == 0) return OASIS_OK;
+  ddim_kernel<<<grid_for(n, 256), 256, 0, s>>>(chunk, v, c, n);
+  return check_launch("ddim_kernel");
+}
+
+int bridge_launch(const float* chunk, float* latent, int batch, float inv_scale, cudaStream_t s) {
+  OASIS_REQUIRE(chunk && latent && batch >= 0, "bridge: bad arguments");
+  if (batch == 0) return OASIS_OK;
+  bridge_kernel<<<grid_for((long long)batch * 576 * 16, 256), 256, 0, s>>>(chunk, latent, batch, inv_scale);
+  return check_launch("bridge_kernel");
+}
+
+int post_quant_launch(const float* lat, const float* w, const float* b, float* z, int rows, cudaStream_t s) {
+  OASIS_REQUIRE(lat && w && z, "post_quant: null pointer");
+  if (rows == 0) return OASIS_OK;
+  post_quant_kernel<<<rows, 256, 0, s>>>(lat, w, b, z, rows);
+  return check_launch("post_quant_kernel");
+}
+
+}  // namespace oasis

@@ -1,0 +1,177 @@
+"""Native frame-generation API over the C ABI.
+
+Functions here take torch tensors only as device-memory handles; all compute is
+in liboasis_b200.so, launched on the current torch CUDA stream. `FrameEngine`
+preallocates every buffer of one frame (B sessions x T frames) and can capture
+the whole frame (4 DDIM steps + bridge + VAE decode) into a CUDA graph, the
+B200 equivalent of the reference's trace capture/replay
+(oasis_inference.py:2125-2148, 2224).
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import _lib
+from . import host as H
+from .weights import DitDeviceWeights, VaeDeviceWeights
+
+
+def _stream(stream=None) -> int:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def _check_cuda(t: torch.Tensor, name: str, dtype=torch.float32):
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if t.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def workspace(nbytes: int, device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+
+
+def dit_workspace_bytes(batch: int, frames: int) -> int:
+    return int(_lib.load().oasis_dit_workspace_size(batch, frames))
+
+
+def step_workspace_bytes(batch: int, frames: int) -> int:
+    return int(_lib.load().oasis_step_workspace_size(batch, frames))
+
+
+def vae_workspace_bytes(batch: int) -> int:
+    return int(_lib.load().oasis_vae_workspace_size(batch))
+
+
+def dit_forward(dw: DitDeviceWeights, z: torch.Tensor, cond: torch.Tensor, v_out: torch.Tensor,
+                ws: torch.Tensor, last_frame_only: bool = True, stream=None) -> torch.Tensor:
+    """z [B, T, 144, 1024] fp32 (overwritten), cond [B, T, 1024] -> v_out."""
+    _check_cuda(z, "z")
+    _check_cuda(cond, "cond")
+    _check_cuda(v_out, "v_out")
+    B, T = z.shape[0], z.shape[1]
+    if tuple(z.shape[2:]) != (H.N_PATCHES, H.D_MODEL) or tuple(cond.shape) != (B, T, H.D_MODEL):
+        raise ValueError(f"bad shapes z={tuple(z.shape)} cond={tuple(cond.shape)}")
+    want = (B, H.N_PATCHES, H.OUT_DIM) if last_frame_only else (B, T, H.N_PATCHES, H.OUT_DIM)
+    if tuple(v_out.shape) != want:
+        raise ValueError(f"v_out must be {want}")
+    a = _lib.OasisDitArgs(B, T, z.data_ptr(), cond.data_ptr(), v_out.data_ptr(), int(last_frame_only),
+                          ws.data_ptr(), ws.numel())
+    _lib.call("oasis_dit_forward", dw.ref(), C.byref(a), _stream(stream))
+    return v_out
+
+
+def ddim_update(chunk: torch.Tensor, v: torch.Tensor, step: H.DdimStep, stream=None) -> torch.Tensor:
+    _check_cuda(chunk, "chunk")
+    _check_cuda(v, "v")
+    if chunk.numel() != v.numel():
+        raise ValueError("chunk and v differ in size")
+    c = _lib.OasisDdimCoeffs(*step.as_tuple())
+    _lib.call("oasis_ddim_update", chunk.data_ptr(), v.data_ptr(), C.byref(c), chunk.numel(), _stream(stream))
+    return chunk
+
+
+def ddim_step(dw: DitDeviceWeights, chunk: torch.Tensor, context_z: torch.Tensor | None, cond: torch.Tensor,
+              step: H.DdimStep, ws: torch.Tensor, stream=None) -> torch.Tensor:
+    """One DDIM step in place on chunk [B, 144, 64] with T-1 context frames."""
+    _check_cuda(chunk, "chunk")
+    _check_cuda(cond, "cond")
+    B, T = cond.shape[0], cond.shape[1]
+    if context_z is not None:
+        _check_cuda(context_z, "context_z")
+        if tuple(context_z.shape) != (B, T - 1, H.N_PATCHES, H.D_MODEL):
+            raise ValueError(f"context_z must be {(B, T - 1, H.N_PATCHES, H.D_MODEL)}")
+    a = _lib.OasisStepArgs(B, T, chunk.data_ptr(), 0 if context_z is None else context_z.data_ptr(),
+                           cond.data_ptr(), _lib.OasisDdimCoeffs(*step.as_tuple()), ws.data_ptr(), ws.numel())
+    _lib.call("oasis_ddim_step", dw.ref(), C.byref(a), _stream(stream))
+    return chunk
+
+
+def patch_embed(dw: DitDeviceWeights, patches: torch.Tensor, z: torch.Tensor, out_group: int, out_off: int,
+                stream=None) -> torch.Tensor:
+    """patches [R, 64] -> rows (r // 144) * out_group + out_off + r % 144 of z."""
+    _check_cuda(patches, "patches")
+    _check_cuda(z, "z")
+    rows = patches.numel() // H.OUT_DIM
+    _lib.call("oasis_patch_embed", dw.ref(), patches.data_ptr(), rows, z.data_ptr(), out_group, out_off,
+              _stream(stream))
+    return z
+
+
+def bridge_unpatchify(chunk: torch.Tensor, latent: torch.Tensor, stream=None) -> torch.Tensor:
+    """chunk [B, 144, 64] -> latent [B, 576, 16] / SCALING_FACTOR."""
+    _check_cuda(chunk, "chunk")
+    _check_cuda(latent, "latent")
+    B = chunk.numel() // (H.N_PATCHES * H.OUT_DIM)
+    if latent.numel() != B * H.VAE_TOKENS * H.VAE_LATENT:
+        raise ValueError("latent must hold B x 576 x 16 values")
+    _lib.call("oasis_bridge_unpatchify", chunk.data_ptr(), latent.data_ptr(), B, _stream(stream))
+    return latent
+
+
+def vae_decode(vw: VaeDeviceWeights, latent: torch.Tensor, image: torch.Tensor, ws: torch.Tensor,
+               stream=None) -> torch.Tensor:
+    """latent [B, 576, 16] -> image [B, 3, 360, 640] in [-1, 1]."""
+    _check_cuda(latent, "latent")
+    _check_cuda(image, "image")
+    B = latent.shape[0]
+    if tuple(image.shape) != (B, 3, H.VAE_H * H.VAE_PATCH, H.VAE_W * H.VAE_PATCH):
+        raise ValueError("image must be [B, 3, 360, 640]")
+    a = _lib.OasisVaeArgs(B, latent.data_ptr(), image.data_ptr(), ws.data_ptr(), ws.numel())
+    _lib.call("oasis_vae_decode", vw.ref(), C.byref(a), _stream(stream))
+    return image
+
+
+class FrameEngine:
+    """All device buffers of one generated frame for B sessions with T-frame
+    context windows, and the launch sequence: 4 DDIM steps (patch embed -> DiT ->
+    DDIM update), bridge, VAE decode. `capture()` records it as a CUDA graph."""
+
+    def __init__(self, dw: DitDeviceWeights, vw: VaeDeviceWeights, batch: int, frames: int,
+                 steps: list[H.DdimStep] | None = None):
+        self.dw, self.vw = dw, vw
+        self.B, self.T = batch, frames
+        self.steps = steps if steps is not None else H.ddim_schedule()
+        dev = dw.device
+        B, T = batch, frames
+        self.chunk = torch.zeros(B, H.N_PATCHES, H.OUT_DIM, device=dev)
+        self.context_z = torch.zeros(B, max(T - 1, 1), H.N_PATCHES, H.D_MODEL, device=dev)
+        self.cond = torch.zeros(len(self.steps), B, T, H.D_MODEL, device=dev)
+        self.latent = torch.zeros(B, H.VAE_TOKENS, H.VAE_LATENT, device=dev)
+        self.image = torch.zeros(B, 3, H.VAE_H * H.VAE_PATCH, H.VAE_W * H.VAE_PATCH, device=dev)
+        self.step_ws = workspace(step_workspace_bytes(B, T), dev)
+        self.vae_ws = workspace(vae_workspace_bytes(B), dev)
+        self.graph = None
+
+    def run_steps(self, stream=None):
+        ctx = self.context_z if self.T > 1 else None
+        for i, st in enumerate(self.steps):
+            ddim_step(self.dw, self.chunk, ctx, self.cond[i], st, self.step_ws, stream)
+
+    def run_decode(self, stream=None):
+        bridge_unpatchify(self.chunk, self.latent, stream)
+        vae_decode(self.vw, self.latent, self.image, self.vae_ws, stream)
+
+    def run(self, stream=None):
+        self.run_steps(stream)
+        self.run_decode(stream)
+
+    def capture(self):
+        """Captures run() into a CUDA graph (launch sequence and pointers fixed)."""
+        self.run()  # warm-up outside capture: sets kernel attributes, resolves the driver entry point
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.run()
+        self.graph = g
+        return g
+
+    def replay(self):
+        if self.graph is None:
+            raise RuntimeError("capture() first")
+        self.graph.replay()

@@ -1,0 +1,94 @@
+"""CPU checks of the C-ABI boundary: the library loads, exports every function the
+header declares, the ctypes mirrors have the C layouts, and argument validation
+fails loudly without touching a GPU."""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+import subprocess
+import tempfile
+
+import pytest
+
+from oasis_b200 import _lib
+from tests.helpers import ROOT
+
+HEADER = os.path.join(ROOT, "include", "oasis_b200.h")
+
+
+def declared_functions() -> list[str]:
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(oasis_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    names = declared_functions()
+    assert len(names) >= 15
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared in oasis_b200.h but not exported"
+    assert set(names) == set(_lib.SIGNATURES), "ctypes signatures and header disagree"
+
+
+STRUCTS = ["OasisDitSubBlock", "OasisDitWeights", "OasisVaeBlock", "OasisVaeWeights", "OasisDitArgs",
+           "OasisDdimCoeffs", "OasisStepArgs", "OasisVaeArgs", "OasisGemmArgs", "OasisLayerNormArgs"]
+
+
+def test_ctypes_layouts_match_c():
+    prog = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{HEADER}"', "int main(void) {"]
+    for s in STRUCTS:
+        prog.append(f'  printf("{s} %zu\\n", sizeof({s}));')
+        for f, _ in getattr(_lib, s)._fields_:
+            prog.append(f'  printf("{s}.{f} %zu\\n", offsetof({s}, {f}));')
+    prog.append("  return 0; }")
+    with tempfile.TemporaryDirectory() as d:
+        c, exe = os.path.join(d, "l.c"), os.path.join(d, "l")
+        open(c, "w").write("\n".join(prog))
+        subprocess.run(["gcc", "-std=c99", c, "-o", exe], check=True)
+        out = subprocess.run([exe], capture_output=True, text=True, check=True).stdout
+    sizes = dict(line.rsplit(" ", 1) for line in out.strip().splitlines())
+    for s in STRUCTS:
+        cls = getattr(_lib, s)
+        assert int(sizes[s]) == C.sizeof(cls), s
+        for f, _ in cls._fields_:
+            assert int(sizes[f"{s}.{f}"]) == getattr(cls, f).offset, f"{s}.{f}"
+
+
+def test_invalid_arguments_are_rejected_without_a_gpu():
+    lib = _lib.load()
+    rc = lib.oasis_gemm(None, None)
+    assert rc == -1 and b"null" in lib.oasis_last_error()
+    args = _lib.OasisGemmArgs()
+    args.a, args.w, args.m, args.n, args.k, args.out = 16, 16, 128, 100, 1024, 16
+    assert lib.oasis_gemm(C.byref(args), None) == -1
+    assert b"multiple of 16" in lib.oasis_last_error()
+    args.n, args.k = 128, 100
+    assert lib.oasis_gemm(C.byref(args), None) == -1
+    assert b"multiple of 64" in lib.oasis_last_error()
+    assert lib.oasis_attention_temporal(16, 16, 1, 33, None) == -1
+    assert b"frames" in lib.oasis_last_error()
+    d = _lib.OasisDitArgs(1, 40, 16, 16, 16, 1, 16, 1 << 30)
+    w = _lib.OasisDitWeights()
+    assert lib.oasis_dit_forward(C.byref(w), C.byref(d), None) == -1
+    d = _lib.OasisDitArgs(1, 2, 16, 16, 16, 1, 0, 0)
+    assert lib.oasis_dit_forward(C.byref(w), C.byref(d), None) == -3  # no workspace
+    assert b"workspace" in lib.oasis_last_error()
+    v = _lib.OasisVaeArgs(0, 16, 16, 16, 1)
+    assert lib.oasis_vae_decode(C.byref(_lib.OasisVaeWeights()), C.byref(v), None) == -1
+
+
+def test_call_raises_with_status_and_message():
+    with pytest.raises(_lib.OasisError) as ei:
+        _lib.call("oasis_attention_temporal", 16, 16, 1, 0, None)
+    assert ei.value.code == -1 and "frames" in str(ei.value)
+
+
+def test_workspace_sizes_scale_with_batch():
+    lib = _lib.load()
+    a = lib.oasis_dit_workspace_size(1, 2)
+    b = lib.oasis_dit_workspace_size(4, 2)
+    assert 0 < a < b
+    assert lib.oasis_step_workspace_size(1, 2) > a
+    assert lib.oasis_vae_workspace_size(2) > lib.oasis_vae_workspace_size(1) > 0

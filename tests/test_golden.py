@@ -1,0 +1,142 @@
+"""Pins the CPU oracle and the product's host-side code to golden vectors made by
+running the reference's own functions (tests/golden/make_golden.py)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from tests.helpers import GOLDEN
+from oracle import oasis_oracle as O
+from oasis_b200 import host as H
+from tests.golden.make_golden import cond_weights, conv_weights
+
+
+@pytest.fixture(scope="module")
+def g():
+    return dict(np.load(GOLDEN))
+
+
+def t(x):
+    return torch.from_numpy(np.asarray(x))
+
+
+def test_timestep_embedding(g):
+    lv = t(g["t_levels"])
+    for fn in (O.timestep_embedding, H.timestep_embedding):
+        np.testing.assert_allclose(fn(lv, 256).numpy(), g["timestep_embedding"], rtol=0, atol=1e-6)
+
+
+def test_sigmoid_schedule(g):
+    np.testing.assert_allclose(H.sigmoid_beta_schedule(1000).numpy(), g["sigmoid_betas"], rtol=0, atol=0)
+    ac_ref = torch.cumprod(1 - t(g["sigmoid_betas"]).float(), 0)
+    np.testing.assert_allclose(O.alphas_cumprod("sigmoid").numpy(), ac_ref.numpy(), rtol=1e-6, atol=1e-7)
+
+
+def test_rope_freq_tables(g):
+    s_f, t_f = t(g["s_freqs"]), t(g["t_freqs"])
+    np.testing.assert_allclose(H.default_spatial_freqs().numpy(), g["s_freqs"], rtol=1e-7)
+    np.testing.assert_allclose(H.default_temporal_freqs().numpy(), g["t_freqs"], rtol=1e-7)
+    np.testing.assert_allclose(O.axial_freqs(s_f, 9, 16).numpy(), g["spatial_rope_freqs"], atol=1e-5)
+    np.testing.assert_allclose(H.spatial_rope_angles(s_f).numpy(), g["spatial_rope_freqs"], atol=1e-5)
+    np.testing.assert_allclose(O.temporal_freqs(t_f, 32).numpy(), g["temporal_rope_freqs"], atol=1e-5)
+    np.testing.assert_allclose(H.temporal_rope_angles(t_f).numpy(), g["temporal_rope_freqs"], atol=1e-5)
+
+
+def test_rope_rotation(g):
+    sp = t(g["spatial_rope_freqs"])
+    np.testing.assert_allclose(O.apply_rotary(sp, t(g["rope_q"])).numpy(), g["rope_q_spatial"], atol=1e-5)
+    tp = t(g["temporal_rope_freqs"])[:8]
+    np.testing.assert_allclose(O.apply_rotary(tp, t(g["rope_qt"])).numpy(), g["rope_qt_temporal"], atol=1e-5)
+
+
+def _rotate_with_pair_table(x: torch.Tensor, tab: torch.Tensor) -> torch.Tensor:
+    """The kernels' rotation: (x0, x1) -> (x0 c - x1 s, x1 c + x0 s) per pair."""
+    x0, x1 = x[..., 0::2], x[..., 1::2]
+    c, s = tab[..., 0], tab[..., 1]
+    out = torch.empty_like(x)
+    out[..., 0::2] = x0 * c - x1 * s
+    out[..., 1::2] = x1 * c + x0 * s
+    return out
+
+
+def test_kernel_rope_table_matches_reference_rotation(g):
+    """The (cos, sin) pair tables the GPU reads reproduce the reference rotation."""
+    tab = H.rope_pair_table(H.spatial_rope_angles(t(g["s_freqs"])))
+    got = _rotate_with_pair_table(t(g["rope_q"]), tab)
+    np.testing.assert_allclose(got.numpy(), g["rope_q_spatial"], atol=2e-5)
+    tab_t = H.rope_pair_table(H.temporal_rope_angles(t(g["t_freqs"])))[:8]
+    got = _rotate_with_pair_table(t(g["rope_qt"]), tab_t)
+    np.testing.assert_allclose(got.numpy(), g["rope_qt_temporal"], atol=2e-5)
+
+
+def test_reference_sin_perm_tables_equal_pair_tables(g):
+    """q cos + swap(q) sin_perm (reference rope_layout) == pair rotation."""
+    tab = H.rope_pair_table(H.spatial_rope_angles(t(g["s_freqs"])))  # (144, 32, 2)
+    cos_ref = t(g["spatial_cos_table"])[:144]
+    sin_ref = t(g["spatial_sin_perm_table"])[:144]
+    np.testing.assert_allclose(cos_ref[:, 0::2].numpy(), tab[..., 0].numpy(), atol=1e-6)
+    np.testing.assert_allclose(sin_ref[:, 1::2].numpy(), tab[..., 1].numpy(), atol=1e-6)
+    np.testing.assert_allclose(sin_ref[:, 0::2].numpy(), -tab[..., 1].numpy(), atol=1e-6)
+    assert np.all(g["spatial_cos_table"][144:] == 0)  # the reference's zeroed pad rows
+
+
+def test_vae_rope_tables(g):
+    tab = H.rope_pair_table(H.vae_rope_angles(t(g["vae_freqs"])))  # (576, 32, 2)
+    cos_ref, sin_ref = t(g["vae_cos_table"]), t(g["vae_sin_perm_table"])
+    # bf16 tables in the reference: compare at bf16 resolution
+    np.testing.assert_allclose(cos_ref[:, 0::2].numpy(), tab[..., 0].numpy(), atol=8e-3)
+    np.testing.assert_allclose(sin_ref[:, 1::2].numpy(), tab[..., 1].numpy(), atol=8e-3)
+    np.testing.assert_allclose(sin_ref[:, 0::2].numpy(), -tab[..., 1].numpy(), atol=8e-3)
+    np.testing.assert_allclose(O.vae_rope_freqs(t(g["vae_freqs"])).numpy()[:, 0::2],
+                               H.vae_rope_angles(t(g["vae_freqs"])).numpy()[:, 0::2], atol=1e-6)
+
+
+def test_patch_layouts(g):
+    lat = t(g["latent"])
+    np.testing.assert_array_equal(O.patchify(lat)[0].numpy(), g["patchified"])
+    np.testing.assert_array_equal(H.patchify(lat)[0].numpy(), g["patchified"])
+    np.testing.assert_array_equal(O.unpatchify(t(g["patchified"])[None]).numpy(), g["unpatchified"])
+    np.testing.assert_array_equal(H.unpatchify(t(g["patchified"])).numpy(), g["unpatchified"][0])
+
+
+def test_patch_embed(g):
+    conv_w, conv_b = conv_weights()
+    sd = {"x_embedder.proj.weight": conv_w, "x_embedder.proj.bias": conv_b}
+    emb = O.patch_embed(t(g["latent"]), sd)[0]
+    np.testing.assert_allclose(emb[::9].numpy(), g["patch_embed_rows"], atol=1e-5)
+    np.testing.assert_allclose(emb.sum(1).numpy(), g["patch_embed_rowsum"], atol=1e-4)
+    # the linear map the GPU uses (W_rt over patch vectors) is the same function
+    lin = t(g["patchified"]) @ H.patch_embed_matrix(conv_w) + conv_b
+    np.testing.assert_allclose(lin[::9].numpy(), g["patch_embed_rows"], atol=1e-5)
+
+
+def test_bridge(g):
+    chunk = t(g["bridge_chunk"])[:144].to(torch.bfloat16).float()
+    ref = t(g["bridge_vae_input"])
+    got = O.bridge(chunk[None])[0]
+    # reference scales by a bf16 mask value (1/0.0784 rounded to bf16) and keeps bf16 operands
+    assert torch.all(ref[:, 16:] == 0)
+    np.testing.assert_allclose(got.numpy(), ref[:, :16].numpy(), rtol=1e-2, atol=1e-2)
+    # exact layout check: the permutation is identical (compare with the bf16-rounded scale)
+    scale_bf16 = float(torch.tensor(1.0 / O.SCALING_FACTOR).to(torch.bfloat16))
+    exact = O.bridge(chunk[None])[0] * O.SCALING_FACTOR * scale_bf16
+    np.testing.assert_allclose(exact.numpy(), ref[:, :16].numpy(), rtol=1e-6, atol=1e-6)
+
+
+def test_vae_unpatchify(g):
+    idx = torch.arange(576 * 1200, dtype=torch.float64).reshape(1, 576, 1200)
+    got = O.vae_unpatchify(idx).reshape(-1).numpy().astype(np.int64)
+    np.testing.assert_array_equal(got, g["vae_unpatchify_index"].astype(np.int64))
+
+
+def test_conditioning(g):
+    dev = cond_weights()
+    sd = {"t_embedder.mlp.0.weight": dev["t_emb_w0_host"].T, "t_embedder.mlp.0.bias": dev["t_emb_b0_host"],
+          "t_embedder.mlp.2.weight": dev["t_emb_w2_host"].T, "t_embedder.mlp.2.bias": dev["t_emb_b2_host"],
+          "external_cond.weight": dev["ext_cond_w_host"].T, "external_cond.bias": dev["ext_cond_b_host"]}
+    act = torch.zeros(1, 25)
+    act[0, 11] = 1
+    for fn in (O.cond_vector, H.compute_cond):
+        np.testing.assert_allclose(fn(torch.tensor([14]), None, sd)[0].numpy(), g["cond_t14_noaction"], atol=1e-5)
+        np.testing.assert_allclose(fn(torch.tensor([999]), act, sd)[0].numpy(), g["cond_t999_walk"], atol=1e-5)

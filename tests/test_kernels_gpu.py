@@ -1,0 +1,285 @@
+"""Per-kernel parity through the C ABI against plain PyTorch fp32 references of
+the same op on the same (bf16-rounded) inputs."""
+from __future__ import annotations
+
+import ctypes as C
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from oasis_b200 import _lib
+from oasis_b200 import host as H
+from tests.helpers import rel_l2
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _s():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def gemm(a, w, mode, out, *, bias=None, resid=None, gate=None, ldg=0, rows_per_frame=1, rope=None,
+         rope_div=1, rope_mod=1, block_n=0, splits=0, ws=None):
+    M, K = a.shape
+    N = w.shape[0]
+    args = _lib.OasisGemmArgs()
+    args.a, args.lda, args.w = a.data_ptr(), K, w.data_ptr()
+    args.m, args.n, args.k, args.mode = M, N, K, mode
+    args.out, args.ldo = out.data_ptr(), (N if mode != 7 else 0)
+    args.bias = _lib.ptr(bias)
+    args.resid, args.ldr = _lib.ptr(resid), N
+    args.gate, args.ldg, args.rows_per_frame = _lib.ptr(gate), ldg, rows_per_frame
+    args.rope, args.rope_div, args.rope_mod = _lib.ptr(rope), rope_div, rope_mod
+    args.block_n, args.splits = block_n, splits
+    if ws is not None:
+        args.workspace, args.workspace_bytes = ws.data_ptr(), ws.numel()
+    _lib.call("oasis_gemm", C.byref(args), _s())
+    torch.cuda.synchronize()
+    return out
+
+
+def rand_bf16(*shape, scale=1.0, seed=0):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    return (torch.randn(*shape, generator=g) * scale).to(DEV, torch.bfloat16)
+
+
+@pytest.mark.parametrize("M,N,K,block_n,splits", [
+    (128, 256, 64, 256, 1), (288, 3072, 1024, 0, 0), (300, 1024, 1024, 64, 4), (1000, 4096, 1024, 256, 1),
+    (577, 1024, 4096, 128, 1), (2, 2048, 1024, 64, 2), (1152, 64, 1024, 64, 1), (4608, 1024, 4096, 0, 0),
+    (73, 1200, 1024, 128, 1), (512, 1024, 1024, 64, 16),
+])
+def test_gemm_f32(M, N, K, block_n, splits):
+    a = rand_bf16(M, K, seed=1)
+    w = rand_bf16(N, K, scale=0.05, seed=2)
+    bias = torch.randn(N, device=DEV)
+    out = torch.full((M, N), float("nan"), device=DEV)
+    ws = torch.empty(64 << 20, dtype=torch.uint8, device=DEV)
+    gemm(a, w, 0, out, bias=bias, block_n=block_n, splits=splits, ws=ws)
+    ref = a.float() @ w.float().T + bias
+    assert rel_l2(out, ref) < 1e-5, rel_l2(out, ref)
+
+
+def test_gemm_splitk_deterministic():
+    a, w = rand_bf16(300, 4096, seed=3), rand_bf16(1024, 4096, scale=0.05, seed=4)
+    ws = torch.empty(64 << 20, dtype=torch.uint8, device=DEV)
+    o1 = torch.empty(300, 1024, device=DEV)
+    o2 = torch.empty(300, 1024, device=DEV)
+    gemm(a, w, 0, o1, block_n=64, splits=8, ws=ws)
+    gemm(a, w, 0, o2, block_n=64, splits=8, ws=ws)
+    assert torch.equal(o1, o2)
+
+
+@pytest.mark.parametrize("mode", [1, 2, 3])
+def test_gemm_bf16_epilogues(mode):
+    M, N, K = 700, 4096, 1024
+    a, w = rand_bf16(M, K, seed=5), rand_bf16(N, K, scale=0.05, seed=6)
+    bias = torch.randn(N, device=DEV) * 0.1
+    out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    gemm(a, w, mode, out, bias=bias)
+    ref = a.float() @ w.float().T + bias
+    if mode == 2:
+        ref = F.gelu(ref, approximate="tanh")
+    elif mode == 3:
+        ref = F.gelu(ref)
+    assert rel_l2(out.float(), ref) < 5e-3
+
+
+@pytest.mark.parametrize("M,block_n,splits", [(288, 0, 0), (1152, 256, 1), (300, 64, 4)])
+def test_gemm_gated_residual(M, block_n, splits):
+    N, K, P = 1024, 1024, 144
+    frames = (M + P - 1) // P
+    a, w = rand_bf16(M, K, seed=7), rand_bf16(N, K, scale=0.05, seed=8)
+    bias = torch.randn(N, device=DEV) * 0.1
+    ld = 6144 * 2 + 2048
+    table = torch.randn(frames, ld, device=DEV)
+    off = 6144 + 2 * 1024
+    resid = torch.randn(M, N, device=DEV)
+    z = resid.clone()
+    ws = torch.empty(64 << 20, dtype=torch.uint8, device=DEV)
+    gemm(a, w, 4, z, bias=bias, resid=z, gate=table[:, off:], ldg=ld, rows_per_frame=P, block_n=block_n,
+         splits=splits, ws=ws)
+    gate = table[torch.arange(M, device=DEV) // P, off:off + N]
+    ref = resid + gate * (a.float() @ w.float().T + bias)
+    assert rel_l2(z, ref) < 1e-5
+
+
+def test_gemm_residual():
+    M, N, K = 576 * 2, 1024, 4096
+    a, w = rand_bf16(M, K, seed=9), rand_bf16(N, K, scale=0.02, seed=10)
+    bias = torch.randn(N, device=DEV)
+    z = torch.randn(M, N, device=DEV)
+    ref = z + a.float() @ w.float().T + bias
+    gemm(a, w, 5, z, bias=bias, resid=z)
+    assert rel_l2(z, ref) < 1e-5
+
+
+def _rope_ref(x, tab, pos):
+    """x [M, 3072] fp32; rotate q/k column pairs with tab[pos[r], pair]."""
+    out = x.clone()
+    c = tab[pos][:, :, 0].repeat(1, 16)  # (M, 512) one entry per pair across 16 heads
+    s = tab[pos][:, :, 1].repeat(1, 16)
+    for sec in range(2):
+        seg = x[:, sec * 1024:(sec + 1) * 1024]
+        x0, x1 = seg[:, 0::2], seg[:, 1::2]
+        out[:, sec * 1024:(sec + 1) * 1024][:, 0::2] = x0 * c - x1 * s
+        out[:, sec * 1024:(sec + 1) * 1024][:, 1::2] = x1 * c + x0 * s
+    return out
+
+
+@pytest.mark.parametrize("kind", ["spatial", "temporal", "vae"])
+def test_gemm_rope(kind):
+    if kind == "spatial":
+        M, tab, div, mod = 2 * 144 * 3, H.rope_pair_table(H.spatial_rope_angles(H.default_spatial_freqs())), 1, 144
+    elif kind == "temporal":
+        T = 8
+        M, tab, div, mod = 2 * T * 144, H.rope_pair_table(H.temporal_rope_angles(H.default_temporal_freqs())), 144, T
+    else:
+        M, tab, div, mod = 2 * 576, H.rope_pair_table(H.vae_rope_angles(H.default_vae_freqs())), 1, 576
+    K, N = 1024, 3072
+    a, w = rand_bf16(M, K, seed=11), rand_bf16(N, K, scale=0.05, seed=12)
+    bias = torch.randn(N, device=DEV) * 0.1 if kind == "vae" else None
+    tab_d = tab.to(DEV)
+    out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    gemm(a, w, 6, out, bias=bias, rope=tab_d, rope_div=div, rope_mod=mod)
+    x = a.float() @ w.float().T + (bias if bias is not None else 0)
+    pos = (torch.arange(M, device=DEV) // div) % mod
+    ref = _rope_ref(x, tab_d, pos)
+    assert rel_l2(out.float(), ref) < 5e-3
+
+
+def test_gemm_image():
+    B = 2
+    M, N, K = B * 576, 1200, 1024
+    a, w = rand_bf16(M, K, seed=13), rand_bf16(N, K, scale=0.05, seed=14)
+    bias = torch.randn(N, device=DEV) * 0.1
+    img = torch.full((B, 3, 360, 640), float("nan"), device=DEV)
+    gemm(a, w, 7, img, bias=bias)
+    pred = (a.float() @ w.float().T + bias).reshape(B, 18, 32, 1200).permute(0, 3, 1, 2)
+    pred = pred.reshape(B, 3, 20, 20, 18, 32).permute(0, 1, 4, 2, 5, 3).reshape(B, 3, 360, 640)
+    ref = pred.clamp(-1, 1)
+    assert not torch.isnan(img).any()
+    assert rel_l2(img, ref) < 1e-5
+
+
+def _ln(args):
+    _lib.call("oasis_layernorm", C.byref(args), _s())
+    torch.cuda.synchronize()
+
+
+def test_layernorm_modulate():
+    B, T, P = 2, 3, 144
+    M = B * T * P
+    x = torch.randn(M, 1024, device=DEV) * 3 + 1
+    ld = 6144 + 2048
+    mod = torch.randn(B * T, ld, device=DEV)
+    y = torch.empty(M, 1024, device=DEV, dtype=torch.bfloat16)
+    a = _lib.OasisLayerNormArgs()
+    a.x, a.y, a.rows_out, a.P, a.in_group = x.data_ptr(), y.data_ptr(), M, P, P
+    a.frame_mul, a.eps, a.mod, a.ld_mod, a.shift_off, a.scale_off = 1, 1e-6, mod.data_ptr(), ld, 3072, 4096
+    _ln(a)
+    fr = torch.arange(M, device=DEV) // P
+    ref = F.layer_norm(x, (1024,), eps=1e-6) * mod[fr, 4096:5120] + mod[fr, 3072:4096]
+    assert rel_l2(y.float(), ref) < 4e-3
+
+
+def test_layernorm_final_gather():
+    B, T, P = 3, 4, 144
+    x = torch.randn(B * T * P, 1024, device=DEV)
+    ld = 2048
+    mod = torch.randn(B * T, ld, device=DEV)
+    y = torch.empty(B * P, 1024, device=DEV, dtype=torch.bfloat16)
+    a = _lib.OasisLayerNormArgs()
+    a.x, a.y, a.rows_out, a.P = x.data_ptr(), y.data_ptr(), B * P, P
+    a.in_group, a.in_off, a.frame_mul, a.frame_add = T * P, (T - 1) * P, T, T - 1
+    a.eps, a.mod, a.ld_mod, a.shift_off, a.scale_off = 1e-6, mod.data_ptr(), ld, 0, 1024
+    _ln(a)
+    xl = x.reshape(B, T, P, 1024)[:, -1].reshape(B * P, 1024)
+    fr = (torch.arange(B * P, device=DEV) // P) * T + T - 1
+    ref = F.layer_norm(xl, (1024,), eps=1e-6) * mod[fr, 1024:] + mod[fr, :1024]
+    assert rel_l2(y.float(), ref) < 4e-3
+
+
+def test_layernorm_affine():
+    M = 576 * 2
+    x = torch.randn(M, 1024, device=DEV) * 2
+    w, b = torch.randn(1024, device=DEV), torch.randn(1024, device=DEV)
+    y = torch.empty(M, 1024, device=DEV, dtype=torch.bfloat16)
+    a = _lib.OasisLayerNormArgs()
+    a.x, a.y, a.rows_out, a.P, a.eps = x.data_ptr(), y.data_ptr(), M, M, 1e-6
+    a.affine_w, a.affine_b = w.data_ptr(), b.data_ptr()
+    _ln(a)
+    ref = F.layer_norm(x, (1024,), w, b, eps=1e-6)
+    assert rel_l2(y.float(), ref) < 4e-3
+
+
+def _attn_ref(q, k, v, mask=None):
+    s = q @ k.transpose(-1, -2) / 8.0
+    if mask is not None:
+        s = s.masked_fill(~mask, float("-inf"))
+    return torch.softmax(s, -1) @ v
+
+
+@pytest.mark.parametrize("groups,seq", [(1, 144), (5, 144), (2, 576), (1, 50), (3, 200)])
+def test_attention_full(groups, seq):
+    qkv = rand_bf16(groups * seq, 3072, seed=groups * 1000 + seq)
+    out = torch.empty(groups * seq, 1024, device=DEV, dtype=torch.bfloat16)
+    _lib.call("oasis_attention_spatial", qkv.data_ptr(), out.data_ptr(), groups, seq, _s())
+    torch.cuda.synchronize()
+    x = qkv.float().reshape(groups, seq, 3, 16, 64).permute(2, 0, 3, 1, 4)  # 3 G H S D
+    ref = _attn_ref(x[0], x[1], x[2]).permute(0, 2, 1, 3).reshape(groups * seq, 1024)
+    assert rel_l2(out.float(), ref) < 1e-2
+
+
+@pytest.mark.parametrize("B,T", [(1, 1), (1, 2), (2, 8), (1, 32), (3, 5)])
+def test_attention_temporal(B, T):
+    P = 144
+    qkv = rand_bf16(B * T * P, 3072, seed=B * 100 + T)
+    out = torch.empty(B * T * P, 1024, device=DEV, dtype=torch.bfloat16)
+    _lib.call("oasis_attention_temporal", qkv.data_ptr(), out.data_ptr(), B, T, _s())
+    torch.cuda.synchronize()
+    x = qkv.float().reshape(B, T, P, 3, 16, 64).permute(3, 0, 2, 4, 1, 5)  # 3 B P H T D
+    mask = torch.tril(torch.ones(T, T, dtype=torch.bool, device=DEV))
+    ref = _attn_ref(x[0], x[1], x[2], mask).permute(0, 3, 1, 2, 4).reshape(B * T * P, 1024)
+    assert rel_l2(out.float(), ref) < 1e-2
+
+
+def test_silu_patch_embed_ddim_bridge_postquant():
+    F_ = 6
+    c = torch.randn(F_, 1024, device=DEV)
+    y = torch.empty(F_, 1024, device=DEV, dtype=torch.bfloat16)
+    _lib.call("oasis_silu_bf16", c.data_ptr(), y.data_ptr(), c.numel(), _s())
+    torch.cuda.synchronize()
+    assert rel_l2(y.float(), F.silu(c)) < 4e-3
+
+    # DDIM update
+    chunk = torch.randn(2, 144, 64, device=DEV)
+    v = torch.randn(2, 144, 64, device=DEV)
+    st = H.ddim_schedule()[1]
+    ref = chunk.clone()
+    at, an = st.at_sqrt ** 2, st.an_sqrt ** 2
+    x0 = math.sqrt(at) * ref - math.sqrt(1 - at) * v
+    eps = (math.sqrt(1 / at) * ref - x0) / math.sqrt(1 / at - 1)
+    ref = math.sqrt(an) * x0 + math.sqrt(1 - an) * eps
+    co = _lib.OasisDdimCoeffs(*st.as_tuple())
+    _lib.call("oasis_ddim_update", chunk.data_ptr(), v.data_ptr(), C.byref(co), chunk.numel(), _s())
+    torch.cuda.synchronize()
+    assert rel_l2(chunk, ref) < 1e-6
+
+    # bridge
+    ch = torch.randn(3, 144, 64, device=DEV)
+    lat = torch.empty(3, 576, 16, device=DEV)
+    _lib.call("oasis_bridge_unpatchify", ch.data_ptr(), lat.data_ptr(), 3, _s())
+    torch.cuda.synchronize()
+    ref = H.unpatchify(ch.cpu()).permute(0, 2, 3, 1).reshape(3, 576, 16) / H.SCALING_FACTOR
+    assert rel_l2(lat, ref) < 1e-6
+
+    # post quant
+    w = torch.randn(16, 1024, device=DEV)
+    b = torch.randn(1024, device=DEV)
+    z = torch.empty(3 * 576, 1024, device=DEV)
+    _lib.call("oasis_post_quant", lat.data_ptr(), w.data_ptr(), b.data_ptr(), z.data_ptr(), 3 * 576, _s())
+    torch.cuda.synchronize()
+    assert rel_l2(z, lat.reshape(-1, 16) @ w + b) < 1e-6

@@ -1,0 +1,147 @@
+"""End-to-end parity of the frame path (DiT forward, DDIM step, bridge, VAE decode,
+full frame) through the C ABI against the CPU fp32 oracle on seeded random-init
+weights. Bar (benchmark spec): relative L2 <= 1e-2 and cosine >= 0.999 on every
+step's v-prediction and on the decoded frame."""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from oracle import oasis_oracle as O
+from oasis_b200 import engine as E
+from oasis_b200 import host as H
+from oasis_b200.weights import DitDeviceWeights, VaeDeviceWeights, init_dit_weights, init_vae_weights
+from tests.helpers import COS_TOL, REL_L2_TOL, cosine, rel_l2
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda")
+
+
+@pytest.fixture(scope="module")
+def dit_small():
+    sd = init_dit_weights(seed=1, n_blocks=2, bias_std=0.02)
+    return sd, DitDeviceWeights(sd, DEV)
+
+
+@pytest.fixture(scope="module")
+def dit_full():
+    sd = init_dit_weights(seed=1)
+    return sd, DitDeviceWeights(sd, DEV)
+
+
+@pytest.fixture(scope="module")
+def vae_full():
+    sd = init_vae_weights(seed=2, bias_std=0.02, norm_std=0.1)
+    return sd, VaeDeviceWeights(sd, DEV)
+
+
+def _inputs(B, T, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    z = torch.randn(B, T, H.N_PATCHES, H.D_MODEL, generator=g)
+    cond = torch.randn(B, T, H.D_MODEL, generator=g)
+    return z, cond
+
+
+@pytest.mark.parametrize("B,T", [(1, 1), (1, 2), (2, 3), (1, 8)])
+def test_dit_forward_small(dit_small, B, T):
+    sd, dw = dit_small
+    z, cond = _inputs(B, T)
+    ref = O.dit_forward(z, cond, sd)
+    zg = z.to(DEV)
+    v = torch.empty(B, T, H.N_PATCHES, H.OUT_DIM, device=DEV)
+    ws = E.workspace(E.dit_workspace_bytes(B, T), DEV)
+    E.dit_forward(dw, zg, cond.to(DEV), v, ws, last_frame_only=False)
+    assert rel_l2(v, ref) < REL_L2_TOL and cosine(v, ref) > COS_TOL, (rel_l2(v, ref), cosine(v, ref))
+    # last-frame-only output is the same rows
+    z2 = z.to(DEV)
+    v2 = torch.empty(B, H.N_PATCHES, H.OUT_DIM, device=DEV)
+    E.dit_forward(dw, z2, cond.to(DEV), v2, ws, last_frame_only=True)
+    assert torch.equal(v2, v[:, -1])
+
+
+def test_dit_forward_full_depth(dit_full):
+    """C2: one 16-block step, B=1, T=2."""
+    sd, dw = dit_full
+    z, cond = _inputs(1, 2, seed=1)
+    ref = O.dit_forward(z, cond, sd)[:, -1]
+    v = torch.empty(1, H.N_PATCHES, H.OUT_DIM, device=DEV)
+    E.dit_forward(dw, z.to(DEV), cond.to(DEV), v, E.workspace(E.dit_workspace_bytes(1, 2), DEV))
+    assert rel_l2(v, ref) < REL_L2_TOL and cosine(v, ref) > COS_TOL, (rel_l2(v, ref), cosine(v, ref))
+
+
+def test_vae_decode_full(vae_full):
+    sd, vw = vae_full
+    g = torch.Generator().manual_seed(5)
+    lat = torch.randn(2, H.VAE_TOKENS, H.VAE_LATENT, generator=g)
+    ref = O.vae_decode(lat, sd)
+    img = torch.empty(2, 3, 360, 640, device=DEV)
+    E.vae_decode(vw, lat.to(DEV), img, E.workspace(E.vae_workspace_bytes(2), DEV))
+    assert rel_l2(img, ref) < REL_L2_TOL and cosine(img, ref) > COS_TOL, (rel_l2(img, ref), cosine(img, ref))
+
+
+def _frame_inputs(sd, B, T, seed):
+    g = torch.Generator().manual_seed(seed)
+    chunk = H.patchify(torch.randn(B, 16, 18, 32, generator=g).clamp(-H.NOISE_ABS_MAX, H.NOISE_ABS_MAX))
+    ctx_lat = torch.randn(B * (T - 1), 16, 18, 32, generator=g)
+    ctx_z = O.patch_embed(ctx_lat, sd).reshape(B, T - 1, H.N_PATCHES, H.D_MODEL)
+    actions = torch.zeros(B, 25)
+    actions[torch.arange(B), torch.randint(0, 25, (B,), generator=g)] = 1
+    steps = H.ddim_schedule()
+    conds = []
+    for st in steps:
+        c_ctx = O.cond_vector(torch.full((B * (T - 1),), H.STABILIZATION_LEVEL - 1), None, sd).reshape(B, T - 1, -1)
+        c_gen = O.cond_vector(torch.full((B,), st.noise_level), actions, sd).reshape(B, 1, -1)
+        conds.append(torch.cat([c_ctx, c_gen], 1))
+    return chunk, ctx_z, conds, steps
+
+
+def test_frame_c3(dit_full, vae_full):
+    """C3: one frame, B=1, T=2: 4 DDIM steps (v checked at every step) + VAE decode."""
+    dsd, dw = dit_full
+    vsd, vw = vae_full
+    B, T = 1, 2
+    chunk, ctx_z, conds, steps = _frame_inputs(dsd, B, T, seed=2)
+    fe = E.FrameEngine(dw, vw, B, T, steps)
+    fe.chunk.copy_(chunk)
+    fe.context_z.copy_(ctx_z)
+    for i, c in enumerate(conds):
+        fe.cond[i].copy_(c)
+    c_ref = chunk.clone()
+    for i, st in enumerate(steps):
+        c_ref, v_ref = O.ddim_step(c_ref, ctx_z, conds[i], st.at_sqrt ** 2, st.an_sqrt ** 2, dsd)
+        E.ddim_step(dw, fe.chunk, fe.context_z, fe.cond[i], st, fe.step_ws)
+        torch.cuda.synchronize()
+        assert rel_l2(fe.chunk, c_ref) < REL_L2_TOL, (i, rel_l2(fe.chunk, c_ref))
+    img_ref = O.vae_decode(O.bridge(c_ref), vsd)
+    fe.run_decode()
+    torch.cuda.synchronize()
+    assert rel_l2(fe.image, img_ref) < REL_L2_TOL and cosine(fe.image, img_ref) > COS_TOL
+
+
+def test_frame_graph_replay_matches_eager(dit_full, vae_full):
+    """The CUDA-graph frame equals the eagerly launched frame bit for bit."""
+    dsd, dw = dit_full
+    vsd, vw = vae_full
+    B, T = 2, 3
+    chunk, ctx_z, conds, steps = _frame_inputs(dsd, B, T, seed=3)
+    fe = E.FrameEngine(dw, vw, B, T, steps)
+    fe.context_z.copy_(ctx_z)
+    for i, c in enumerate(conds):
+        fe.cond[i].copy_(c)
+    fe.chunk.copy_(chunk)
+    fe.run()
+    torch.cuda.synchronize()
+    eager_img, eager_chunk = fe.image.clone(), fe.chunk.clone()
+    fe.chunk.copy_(chunk)
+    fe.capture()  # runs once eagerly as warm-up, then captures
+    fe.chunk.copy_(chunk)
+    fe.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(fe.chunk, eager_chunk)
+    assert torch.equal(fe.image, eager_img)
+
+
+def test_device_error_word_clear():
+    from oasis_b200 import _lib
+
+    assert _lib.load().oasis_device_error(1) == 0
