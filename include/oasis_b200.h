@@ -51,6 +51,9 @@ typedef void* oasis_stream_t; /* cudaStream_t */
 const char* oasis_last_error(void);
 /* Reads (and with reset != 0 clears) the device error word; synchronizes the device. */
 int oasis_device_error(int reset);
+/* Number of kernels this library has launched from the host so far (graph
+ * replays launch without the host and are not counted). */
+unsigned long long oasis_launch_count(void);
 /* Library version string. */
 const char* oasis_version(void);
 

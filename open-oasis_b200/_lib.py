@@ -102,6 +102,7 @@ SIGNATURES = {
     "oasis_last_error": (C.c_char_p, []),
     "oasis_device_error": (C.c_int, [C.c_int]),
     "oasis_version": (C.c_char_p, []),
+    "oasis_launch_count": (C.c_ulonglong, []),
     "oasis_dit_workspace_size": (C.c_size_t, [C.c_int, C.c_int]),
     "oasis_dit_forward": (C.c_int, [C.POINTER(OasisDitWeights), C.POINTER(OasisDitArgs), vp]),
     "oasis_ddim_update": (C.c_int, [fp, fp, C.POINTER(OasisDdimCoeffs), C.c_longlong, vp]),

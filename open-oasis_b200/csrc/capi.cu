@@ -5,6 +5,8 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <atomic>
+
 #include "../../include/oasis_b200.h"
 #include "gemm.cuh"
 #include "pointwise.cuh"
@@ -13,6 +15,9 @@
 namespace oasis {
 
 static thread_local char g_msg[512] = "";
+static std::atomic<unsigned long long> g_launches{0};
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 int set_error(int code, const char* fmt, ...) {
   va_list ap;
@@ -352,6 +357,8 @@ extern "C" {
 const char* oasis_last_error(void) { return g_msg; }
 
 int oasis_device_error(int reset) { return read_device_error(reset); }
+
+unsigned long long oasis_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 const char* oasis_version(void) { return "oasis_b200 0.1 (sm_100a)"; }
 

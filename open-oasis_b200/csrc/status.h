@@ -15,7 +15,11 @@ namespace oasis {
 // Records a printf-style message for oasis_last_error() and returns `code`.
 int set_error(int code, const char* fmt, ...);
 
+// Host-side count of kernels this library has launched (all threads).
+void count_launch();
+
 inline int check_launch(const char* what) {
+  count_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(OASIS_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
   return OASIS_OK;

@@ -162,16 +162,22 @@ class FrameEngine:
         self.run_decode(stream)
 
     def capture(self):
-        """Captures run() into a CUDA graph (launch sequence and pointers fixed)."""
-        self.run()  # warm-up outside capture: sets kernel attributes, resolves the driver entry point
+        """Captures the frame as two CUDA graphs (DDIM steps; bridge + VAE decode)
+        with the launch sequence and pointers fixed. Eagerly runs the frame once
+        first (kernel attributes, driver entry point), which modifies `chunk`."""
+        self.run()
         torch.cuda.synchronize()
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            self.run()
-        self.graph = g
-        return g
+        self.graph_steps = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph_steps):
+            self.run_steps()
+        self.graph_decode = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph_decode):
+            self.run_decode()
+        self.graph = (self.graph_steps, self.graph_decode)
+        return self.graph
 
     def replay(self):
         if self.graph is None:
             raise RuntimeError("capture() first")
-        self.graph.replay()
+        self.graph_steps.replay()
+        self.graph_decode.replay()
