@@ -9,7 +9,8 @@
 // Structure (one CTA per SM, persistent over output tiles):
 //   warp 0      TMA producer: A and W tiles (128B swizzle) into a STAGES-deep ring
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
-//   warps 2..5  epilogue: tcgen05.ld the fp32 accumulator, apply the fused op, store
+//   warps 2..9  epilogue: tcgen05.ld the fp32 accumulator, apply the fused op,
+//               stage 128-byte rows in swizzled shared memory, TMA bulk store
 // Two TMEM accumulators alternate so the epilogue of tile i overlaps the
 // mainloop of tile i+1. Optional split-K: partial tiles go to a workspace and the
 // last-arriving split (tile counter) sums them in split order (deterministic)
@@ -30,7 +31,9 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;                 // two per TMEM lane quarter
+constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer + MMA + epilogue
+constexpr int kStgBytes = 32 * 128;          // per-warp store staging: 32 rows x 128 B
 
 template <int BN>
 struct Cfg {
@@ -39,8 +42,9 @@ struct Cfg {
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;  // two accumulators; 128/256/512 (power of 2)
+  static constexpr int STG_BYTES = kEpiWarps * kStgBytes;
   static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM = 1024 /*align slack*/ + STAGES * STAGE_BYTES + BAR_BYTES;
+  static constexpr int SMEM = 1024 /*align slack*/ + STAGES * STAGE_BYTES + STG_BYTES + BAR_BYTES;
 };
 
 struct SplitK {
@@ -49,108 +53,240 @@ struct SplitK {
   int splits;
 };
 
-// Applies the epilogue to 16 consecutive columns [n, n+16) of row r.
-__device__ __forceinline__ void epilogue16(const EpiParams& e, int r, int n, int N, float (&v)[16]) {
+__host__ __device__ constexpr bool bf16_out(int mode) {
+  return mode == kEpiBF16 || mode == kEpiGeluTanhBF16 || mode == kEpiGeluErfBF16 || mode == kEpiRopeBF16;
+}
+__host__ __device__ constexpr bool reads_resid(int mode) { return mode == kEpiGatedResid || mode == kEpiResid; }
+
+// Residual prefetch for one 32-column group of row r (zeros past the last row).
+__device__ __forceinline__ void load_resid(const EpiParams& e, int r, int nb, int M, float4 (&res)[8]) {
+  if (r < M) {
+    const float4* src = reinterpret_cast<const float4*>(e.resid + (long long)r * e.ldr + nb);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) res[i] = src[i];
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) res[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
+
+// Applies the epilogue to 32 consecutive accumulator columns [nb, nb + 32) of row r, in place.
+__device__ __forceinline__ void epilogue_math(const EpiParams& e, int r, int nb, float (&v)[32],
+                                              const float4 (&res)[8]) {
   if (e.bias) {
 #pragma unroll
-    for (int i = 0; i < 16; i += 4) {
-      float4 b = __ldg(reinterpret_cast<const float4*>(e.bias + n + i));
+    for (int i = 0; i < 32; i += 4) {
+      const float4 b = __ldg(reinterpret_cast<const float4*>(e.bias + nb + i));
       v[i] += b.x; v[i + 1] += b.y; v[i + 2] += b.z; v[i + 3] += b.w;
     }
   }
   switch (e.mode) {
-    case kEpiF32: {
-      float4* o = reinterpret_cast<float4*>(static_cast<float*>(e.out) + (long long)r * e.ldo + n);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) o[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-      break;
-    }
-    case kEpiBF16:
     case kEpiGeluTanhBF16:
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(v[i]);
+      break;
     case kEpiGeluErfBF16:
-    case kEpiRopeBF16: {
-      if (e.mode == kEpiGeluTanhBF16) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = gelu_tanh(v[i]);
-      } else if (e.mode == kEpiGeluErfBF16) {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = gelu_erf(v[i]);
-      } else if (e.mode == kEpiRopeBF16 && n < 2 * e.rope_dim) {
+      for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
+      break;
+    case kEpiRopeBF16:
+      if (nb < 2 * e.rope_dim) {
+        // pairs (2j, 2j+1) of a 64-wide head rotate by the angle of (pos, pair)
         const int pos = (r / e.rope_div) % e.rope_mod;
-        const int pair0 = (n & 63) >> 1;  // 16 columns never straddle a 64-wide head
-        const float2* tab = reinterpret_cast<const float2*>(e.rope) + pos * 32 + pair0;
+        const float4* tab = reinterpret_cast<const float4*>(e.rope + pos * 64 + (nb & 63));
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const float2 cs = __ldg(tab + j);
-          const float x0 = v[2 * j], x1 = v[2 * j + 1];
-          v[2 * j] = x0 * cs.x - x1 * cs.y;
-          v[2 * j + 1] = x1 * cs.x + x0 * cs.y;
+          const float4 cs = __ldg(tab + j);  // (cos, sin) of two consecutive pairs
+          const float x0 = v[4 * j], x1 = v[4 * j + 1], x2 = v[4 * j + 2], x3 = v[4 * j + 3];
+          v[4 * j] = x0 * cs.x - x1 * cs.y;
+          v[4 * j + 1] = x1 * cs.x + x0 * cs.y;
+          v[4 * j + 2] = x2 * cs.z - x3 * cs.w;
+          v[4 * j + 3] = x3 * cs.z + x2 * cs.w;
         }
       }
-      uint4* o = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(e.out) + (long long)r * e.ldo + n);
-      o[0] = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
-                        pack_bf16x2(v[6], v[7]));
-      o[1] = make_uint4(pack_bf16x2(v[8], v[9]), pack_bf16x2(v[10], v[11]),
-                        pack_bf16x2(v[12], v[13]), pack_bf16x2(v[14], v[15]));
       break;
-    }
     case kEpiGatedResid:
-    case kEpiResid: {
-      const float4* rs = reinterpret_cast<const float4*>(e.resid + (long long)r * e.ldr + n);
-      float4 res[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) res[i] = rs[i];
+    case kEpiResid:
       if (e.mode == kEpiGatedResid) {
-        const float4* g = reinterpret_cast<const float4*>(
-            e.gate + (long long)(r / e.rows_per_frame) * e.ldg + n);
+        const float4* g = reinterpret_cast<const float4*>(e.gate + (long long)(r / e.rows_per_frame) * e.ldg + nb);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < 8; ++i) {
           const float4 gg = __ldg(g + i);
           v[4 * i] *= gg.x; v[4 * i + 1] *= gg.y; v[4 * i + 2] *= gg.z; v[4 * i + 3] *= gg.w;
         }
       }
-      float4* o = reinterpret_cast<float4*>(static_cast<float*>(e.out) + (long long)r * e.ldo + n);
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-        o[i] = make_float4(res[i].x + v[4 * i], res[i].y + v[4 * i + 1], res[i].z + v[4 * i + 2],
-                           res[i].w + v[4 * i + 3]);
-      break;
-    }
-    case kEpiImage: {
-      // row r = frame * tokens + (hh * grid_w + ww); column n = ch * P*P + p * P + q
-      const int P = e.img_patch;
-      const int frame = r / e.img_tokens;
-      const int tok = r - frame * e.img_tokens;
-      const int hh = tok / e.img_grid_w, ww = tok - hh * e.img_grid_w;
-      const int grid_h = e.img_tokens / e.img_grid_w;
-      const long long H = (long long)grid_h * P, W = (long long)e.img_grid_w * P;
-      float* img = static_cast<float*>(e.out) + (long long)frame * 3 * H * W;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int nn = n + i;
-        if (nn < N) {
-          const int ch = nn / (P * P);
-          const int rem = nn - ch * P * P;
-          const int p = rem / P, q = rem - p * P;
-          const float x = fminf(1.f, fmaxf(-1.f, v[i]));
-          img[(long long)ch * H * W + (long long)(hh * P + p) * W + (ww * P + q)] = x;
-        }
+      for (int i = 0; i < 8; ++i) {
+        v[4 * i] += res[i].x; v[4 * i + 1] += res[i].y; v[4 * i + 2] += res[i].z; v[4 * i + 3] += res[i].w;
       }
       break;
-    }
     default:
       break;
+  }
+}
+
+// VAE predictor: row r = frame * tokens + (hh * grid_w + ww); column n = ch * P*P + p * P + q.
+__device__ __forceinline__ void store_image(const EpiParams& e, int r, int nb, int N, const float (&v)[32]) {
+  const int P = e.img_patch;
+  const int frame = r / e.img_tokens;
+  const int tok = r - frame * e.img_tokens;
+  const int hh = tok / e.img_grid_w, ww = tok - hh * e.img_grid_w;
+  const int grid_h = e.img_tokens / e.img_grid_w;
+  const long long H = (long long)grid_h * P, Wd = (long long)e.img_grid_w * P;
+  float* img = static_cast<float*>(e.out) + (long long)frame * 3 * H * Wd;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const int nn = nb + i;
+    if (nn < N) {
+      const int ch = nn / (P * P);
+      const int rem = nn - ch * P * P;
+      const int p = rem / P, q = rem - p * P;
+      img[(long long)ch * H * Wd + (long long)(hh * P + p) * Wd + (ww * P + q)] = fminf(1.f, fmaxf(-1.f, v[i]));
+    }
+  }
+}
+
+// The warp's staging tile holds one 32-row x 128-byte box for a TMA store; row
+// `lane` belongs to this thread and its 16-byte chunks are XOR-swizzled by
+// lane % 8 (TMA's 128-byte swizzle), so the writes are bank-conflict free.
+__device__ __forceinline__ void stage_begin(int lane) {
+  if (lane == 0) bulk_wait_read0();  // the previous store from this buffer has read it
+  __syncwarp();
+}
+
+// Writes 32 values at 16-byte chunks [j0, j0 + 8 or 4) of this thread's staging row.
+__device__ __forceinline__ void stage_write(uint8_t* stg, int lane, bool bf16, int j0, const float (&v)[32]) {
+  uint8_t* row = stg + lane * 128;
+  if (bf16) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      *reinterpret_cast<uint4*>(row + (((j0 + j) ^ (lane & 7)) << 4)) =
+          make_uint4(pack_bf16x2(v[8 * j], v[8 * j + 1]), pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
+                     pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      *reinterpret_cast<uint4*>(row + ((j ^ (lane & 7)) << 4)) =
+          make_uint4(__float_as_uint(v[4 * j]), __float_as_uint(v[4 * j + 1]), __float_as_uint(v[4 * j + 2]),
+                     __float_as_uint(v[4 * j + 3]));
+  }
+}
+
+__device__ __forceinline__ void stage_commit(const CUtensorMap* tm_out, uint8_t* stg, int lane, int row0, int nb) {
+  fence_proxy_async();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(tm_out, stg, nb, row0);
+    bulk_commit();
+  }
+}
+
+// Epilogue of one output tile for one warp. A chunk is 128 output bytes per row
+// (32 fp32 or 64 bf16 columns), processed as 32-column groups; the warp takes
+// chunks c = half, half + 2, ...
+__device__ __forceinline__ void epilogue_tile(const EpiParams& e, const SplitK& sk, const CUtensorMap* tm_out,
+                                              uint8_t* stg, uint32_t t_acc, int M, int N, int BN, int m0q, int n0,
+                                              int tile, int split, int quarter, int half, int lane,
+                                              uint64_t* acc_bar, uint32_t acc_parity, bool& ok) {
+  const int r = m0q + lane;
+  const bool bf16 = bf16_out(e.mode);
+  const int W = bf16 ? 64 : 32;
+  const int nchunks = BN / W;
+  const bool resid = reads_resid(e.mode) && sk.splits == 1;  // fp32 modes: W == 32
+  float4 rcur[8];
+  if (resid && half < nchunks && n0 + half * W < N) load_resid(e, r, n0 + half * W, M, rcur);
+  if (!mbar_wait(acc_bar, acc_parity, kDevTimeoutAccFull)) {
+    ok = false;
+    return;
+  }
+  tc_fence_after();
+  float* part = nullptr;
+  if (sk.splits > 1) part = sk.partials + ((long long)tile * sk.splits + split) * (BM * BN) + (quarter * 32 + lane) * BN;
+#pragma unroll 1
+  for (int c = half; c < nchunks; c += 2) {
+    const int nb = n0 + c * W;
+    if (sk.splits == 1 && nb >= N) break;  // warp-uniform
+    float4 rnext[8];
+    if (resid && c + 2 < nchunks && nb + 2 * W < N) load_resid(e, r, nb + 2 * W, M, rnext);
+    if (sk.splits == 1 && e.mode != kEpiImage) stage_begin(lane);
+#pragma unroll 1
+    for (int g = 0; g < W / 32; ++g) {
+      float v[32];
+      __syncwarp();
+      tmem_ld32(t_acc + c * W + g * 32, v);
+      if (sk.splits > 1) {
+        float4* dst = reinterpret_cast<float4*>(part + c * W + g * 32);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) __stcg(dst + i, make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
+      } else {
+        epilogue_math(e, r, nb + g * 32, v, rcur);
+        if (e.mode == kEpiImage) {
+          if (r < M) store_image(e, r, nb, N, v);
+        } else {
+          stage_write(stg, lane, bf16, g * 4, v);
+        }
+      }
+    }
+    if (sk.splits == 1) {
+      if (e.mode != kEpiImage) stage_commit(tm_out, stg, lane, m0q, nb);
+      if (resid) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) rcur[i] = rnext[i];
+      }
+    }
+  }
+}
+
+// Split-K fix-up run by the last split of a tile: sums the partials in split order.
+__device__ __forceinline__ void splitk_reduce(const EpiParams& e, const SplitK& sk, const CUtensorMap* tm_out,
+                                              uint8_t* stg, int M, int N, int BN, int m0q, int n0, int tile,
+                                              int quarter, int half, int lane) {
+  const int r = m0q + lane;
+  const bool bf16 = bf16_out(e.mode);
+  const int W = bf16 ? 64 : 32;
+  const float* base = sk.partials + (long long)tile * sk.splits * (BM * BN) + (quarter * 32 + lane) * BN;
+  const int nchunks = BN / W;
+#pragma unroll 1
+  for (int c = half; c < nchunks; c += 2) {
+    const int nb = n0 + c * W;
+    if (nb >= N) break;
+    if (e.mode != kEpiImage) stage_begin(lane);
+#pragma unroll 1
+    for (int g = 0; g < W / 32; ++g) {
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = 0.f;
+      for (int s2 = 0; s2 < sk.splits; ++s2) {
+        const float4* src = reinterpret_cast<const float4*>(base + (long long)s2 * (BM * BN) + c * W + g * 32);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 y = __ldcg(src + i);
+          v[4 * i] += y.x; v[4 * i + 1] += y.y; v[4 * i + 2] += y.z; v[4 * i + 3] += y.w;
+        }
+      }
+      float4 res[8];
+      if (reads_resid(e.mode)) load_resid(e, r, nb + g * 32, M, res);
+      epilogue_math(e, r, nb + g * 32, v, res);
+      if (e.mode == kEpiImage) {
+        if (r < M) store_image(e, r, nb, N, v);
+      } else {
+        stage_write(stg, lane, bf16, g * 4, v);
+      }
+    }
+    if (e.mode != kEpiImage) stage_commit(tm_out, stg, lane, m0q, nb);
   }
 }
 
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
-                const int M, const int N, const int K, const EpiParams epi, const SplitK sk) {
+                const __grid_constant__ CUtensorMap tmO, const int M, const int N, const int K,
+                const EpiParams epi, const SplitK sk) {
   using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint8_t* staging = smem + C::STAGES * C::STAGE_BYTES;  // 1024-aligned
+  uint64_t* full = reinterpret_cast<uint64_t*>(staging + C::STG_BYTES);
   uint64_t* empty = full + C::STAGES;
   uint64_t* acc_full = empty + C::STAGES;
   uint64_t* acc_empty = acc_full + 2;
@@ -170,13 +306,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmW);
+    if (epi.mode != kEpiImage) prefetch_tmap(&tmO);
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 4);
+      mbar_init(&acc_empty[a], kEpiWarps);
     }
     fence_barrier_init();
   }
@@ -243,82 +380,49 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ---------------- Epilogue (warps 2..5) ----------------
-    const int sub = warp & 3;  // TMEM lane quarter this warp may access
-    const int row_in_tile = sub * 32 + lane;
-    const uint32_t lane_off = (uint32_t)(sub * 32) << 16;
+    // ---------------- Epilogue (warps 2..9) ----------------
+    // Warp w reads TMEM lanes [32 (w % 4), +32) - the rows it may access - and
+    // every other chunk of 128 output bytes per row (half = (w - 2) / 4). Each
+    // thread owns one row; results leave through a swizzled staging tile and a
+    // TMA bulk store, residual inputs are prefetched a chunk ahead.
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    uint8_t* stg = staging + (warp - 2) * kStgBytes;
     const int ep_tid = threadIdx.x - 64;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+    bool ok = true;
+    for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
       const int tile = u / splits, split = u - tile * splits;
-      const int m0 = (tile / n_tiles) * BM, n0 = (tile % n_tiles) * BN;
-      const int r = m0 + row_in_tile;
-      if (!mbar_wait(&acc_full[acc], acc_phase, kDevTimeoutAccFull)) break;
-      tc_fence_after();
+      const int m0q = (tile / n_tiles) * BM + quarter * 32, n0 = (tile % n_tiles) * BN;
       const uint32_t t_acc = tmem_base + lane_off + acc * BN;
-      if (splits == 1) {
-#pragma unroll 1
-        for (int c = 0; c < BN / 16; ++c) {
-          const int n = n0 + c * 16;
-          if (n >= N) break;  // warp-uniform
-          float v[16];
-          __syncwarp();
-          tmem_ld16(t_acc + c * 16, v);
-          if (r < M) epilogue16(epi, r, n, N, v);
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[acc]);
-      } else {
-        float* part = sk.partials + ((long long)tile * splits + split) * (BM * BN) + row_in_tile * BN;
-#pragma unroll 1
-        for (int c = 0; c < BN / 16; ++c) {
-          float v[16];
-          __syncwarp();
-          tmem_ld16(t_acc + c * 16, v);
-          float4* dst = reinterpret_cast<float4*>(part + c * 16);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) __stcg(dst + i, make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[acc]);
+      epilogue_tile(epi, sk, &tmO, stg, t_acc, M, N, BN, m0q, n0, tile, split, quarter, half, lane,
+                    &acc_full[acc], acc_phase, ok);
+      if (!ok) break;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+      if (splits > 1) {
         __threadfence();
-        named_barrier_sync(1, 128);
+        named_barrier_sync(1, 32 * kEpiWarps);
         if (ep_tid == 0) {
           const int prev = atomicAdd(&sk.counters[tile], 1);
           const int last = (prev == splits - 1);
           if (last) sk.counters[tile] = 0;  // every split has arrived: ready for the next launch
           *sk_flag = last;
         }
-        named_barrier_sync(1, 128);
+        named_barrier_sync(1, 32 * kEpiWarps);
         if (*sk_flag) {
           __threadfence();
-          const float* base = sk.partials + (long long)tile * splits * (BM * BN) + row_in_tile * BN;
-#pragma unroll 1
-          for (int c = 0; c < BN / 16; ++c) {
-            const int n = n0 + c * 16;
-            if (n >= N) break;
-            float v[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) v[i] = 0.f;
-            for (int s = 0; s < splits; ++s) {
-              const float4* src = reinterpret_cast<const float4*>(base + (long long)s * (BM * BN) + c * 16);
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const float4 x = __ldcg(src + i);
-                v[4 * i] += x.x; v[4 * i + 1] += x.y; v[4 * i + 2] += x.z; v[4 * i + 3] += x.w;
-              }
-            }
-            if (r < M) epilogue16(epi, r, n, N, v);
-          }
+          splitk_reduce(epi, sk, &tmO, stg, M, N, BN, m0q, n0, tile, quarter, half, lane);
         }
-        named_barrier_sync(1, 128);  // sk_flag is reused by the next tile
+        named_barrier_sync(1, 32 * kEpiWarps);  // sk_flag is reused by the next tile
       }
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
+    if (lane == 0) bulk_wait0();  // stores complete before the staging memory goes away
   }
 
   tc_fence_before();
@@ -361,6 +465,23 @@ int make_map(CUtensorMap* map, const void* ptr, long long rows, long long K, lon
   return OASIS_OK;
 }
 
+// Output store map: dims {N, M}, box {128 bytes of columns, 32 rows}, 128-byte swizzle.
+int make_out_map(CUtensorMap* map, void* ptr, long long M, long long N, long long ld, bool bf16) {
+  OASIS_TRY(get_encoder());
+  const int es = bf16 ? 2 : 4;
+  OASIS_REQUIRE((reinterpret_cast<uintptr_t>(ptr) & 15) == 0, "GEMM output not 16-byte aligned");
+  OASIS_REQUIRE((ld * es) % 16 == 0, "GEMM output row stride not a multiple of 16 bytes");
+  cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)M};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * es)};
+  cuuint32_t box[2] = {(cuuint32_t)(128 / es), 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, ptr, dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(OASIS_ERR_CUDA, "cuTensorMapEncodeTiled (output) failed (%d)", (int)r);
+  return OASIS_OK;
+}
+
 int g_num_sms[64] = {0};
 
 template <int BN>
@@ -374,9 +495,13 @@ int launch_bn(const GemmProblem& p, int splits, cudaStream_t stream) {
     if (e != cudaSuccess) return set_error(OASIS_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     attr_set[dev & 63] = true;
   }
-  CUtensorMap ta, tw;
+  CUtensorMap ta, tw, to;
   OASIS_TRY(make_map(&ta, p.A, p.M, p.K, p.lda, BM));
   OASIS_TRY(make_map(&tw, p.W, p.N, p.K, p.K, BN));
+  if (p.epi.mode == kEpiImage)
+    to = ta;  // unused: the image epilogue scatters directly
+  else
+    OASIS_TRY(make_out_map(&to, p.epi.out, p.M, p.N, p.epi.ldo, bf16_out(p.epi.mode)));
   const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
   SplitK sk{nullptr, nullptr, splits};
   if (splits > 1) {
@@ -392,7 +517,7 @@ int launch_bn(const GemmProblem& p, int splits, cudaStream_t stream) {
   }
   const int units = tiles * splits;
   const int grid = units < num_sms() ? units : num_sms();
-  gemm_kernel<BN><<<grid, kThreads, C::SMEM, stream>>>(ta, tw, p.M, p.N, p.K, p.epi, sk);
+  gemm_kernel<BN><<<grid, kThreads, C::SMEM, stream>>>(ta, tw, to, p.M, p.N, p.K, p.epi, sk);
   return check_launch("gemm_kernel");
 }
 

@@ -1,0 +1,104 @@
+"""Small, self-contained launch cases for ncu captures of single kernels.
+
+    python open-oasis_b200/profile_cases.py gemm --m 16384 --n 4096 --k 1024 --mode 2 [--reps 3]
+    python open-oasis_b200/profile_cases.py attn_spatial --groups 512
+    python open-oasis_b200/profile_cases.py attn_temporal --batch 64 --frames 8
+    python open-oasis_b200/profile_cases.py layernorm --rows 73728
+
+Each case allocates only what the one kernel needs (a few GB at most), runs it
+`reps` times and exits, so an ncu capture with -k/-c ends by itself quickly.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import os
+import sys
+
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+import __graft_entry__  # noqa: E402
+
+__graft_entry__.load_package()
+from oasis_b200 import _lib  # noqa: E402
+
+
+def _st():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def gemm(a):
+    M, N, K = a.m, a.n, a.k
+    A = (torch.randn(M, K, device="cuda") * 0.5).to(torch.bfloat16)
+    W = (torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16)
+    out = torch.empty(M, N, device="cuda", dtype=torch.float32)
+    bias = torch.zeros(N, device="cuda")
+    gate = torch.randn((M + 143) // 144, N, device="cuda")
+    rope = torch.zeros(144, 32, 2, device="cuda")
+    rope[..., 0] = 1
+    args = _lib.OasisGemmArgs()
+    args.a, args.lda, args.w, args.m, args.n, args.k, args.mode = A.data_ptr(), K, W.data_ptr(), M, N, K, a.mode
+    args.out, args.ldo, args.bias = out.data_ptr(), N, bias.data_ptr()
+    args.resid, args.ldr, args.gate, args.ldg, args.rows_per_frame = out.data_ptr(), N, gate.data_ptr(), N, 144
+    args.rope, args.rope_div, args.rope_mod = rope.data_ptr(), 1, 144
+    args.block_n, args.splits = a.block_n, a.splits
+    ws = torch.empty(max(_lib.load().oasis_gemm_workspace_size(M, N, K), 256), dtype=torch.uint8, device="cuda")
+    args.workspace, args.workspace_bytes = ws.data_ptr(), ws.numel()
+    for _ in range(a.reps):
+        _lib.call("oasis_gemm", C.byref(args), _st())
+
+
+def attn_spatial(a):
+    qkv = torch.randn(a.groups * a.seq, 3072, device="cuda").to(torch.bfloat16)
+    out = torch.empty(a.groups * a.seq, 1024, device="cuda", dtype=torch.bfloat16)
+    for _ in range(a.reps):
+        _lib.call("oasis_attention_spatial", qkv.data_ptr(), out.data_ptr(), a.groups, a.seq, _st())
+
+
+def attn_temporal(a):
+    rows = a.batch * a.frames * 144
+    qkv = torch.randn(rows, 3072, device="cuda").to(torch.bfloat16)
+    out = torch.empty(rows, 1024, device="cuda", dtype=torch.bfloat16)
+    for _ in range(a.reps):
+        _lib.call("oasis_attention_temporal", qkv.data_ptr(), out.data_ptr(), a.batch, a.frames, _st())
+
+
+def layernorm(a):
+    x = torch.randn(a.rows, 1024, device="cuda")
+    y = torch.empty(a.rows, 1024, device="cuda", dtype=torch.bfloat16)
+    frames = (a.rows + 143) // 144
+    mod = torch.randn(frames, 2048, device="cuda")
+    args = _lib.OasisLayerNormArgs()
+    args.x, args.y, args.rows_out, args.P, args.in_group = x.data_ptr(), y.data_ptr(), a.rows, 144, 144
+    args.frame_mul, args.eps, args.mod, args.ld_mod, args.shift_off, args.scale_off = 1, 1e-6, mod.data_ptr(), 2048, 0, 1024
+    for _ in range(a.reps):
+        _lib.call("oasis_layernorm", C.byref(args), _st())
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("case", choices=["gemm", "attn_spatial", "attn_temporal", "layernorm"])
+    ap.add_argument("--m", type=int, default=16384)
+    ap.add_argument("--n", type=int, default=4096)
+    ap.add_argument("--k", type=int, default=1024)
+    ap.add_argument("--mode", type=int, default=2)
+    ap.add_argument("--block-n", type=int, default=0)
+    ap.add_argument("--splits", type=int, default=0)
+    ap.add_argument("--groups", type=int, default=512)
+    ap.add_argument("--seq", type=int, default=144)
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--frames", type=int, default=8)
+    ap.add_argument("--rows", type=int, default=73728)
+    ap.add_argument("--reps", type=int, default=3)
+    a = ap.parse_args()
+    globals()[a.case](a)
+    torch.cuda.synchronize()
+    err = _lib.load().oasis_device_error(0)
+    if err:
+        raise SystemExit(f"device error word {err}")
+
+
+if __name__ == "__main__":
+    main()
