@@ -5,13 +5,14 @@
 // reference's separate RoPE/layout kernels and reshapes disappear: a head is a
 // 128-byte column slice of each row.
 //
+// attention_spatial (seq = 144, the DiT spatial case): persistent, one whole
+//   (frame, head) problem per CTA iteration, see below.
 // attention_full: non-causal softmax(q k^T / 8) v within groups of `seq`
-//   consecutive rows (DiT spatial: one frame, seq = 144, exactly 144 keys - the
-//   tail of the last key tile is masked; VAE: one frame, seq = 576).
+//   consecutive rows (VAE: one frame, seq = 576; other lengths: key tail masked).
 //   Flash-style: K/V tiles of 64 keys staged in swizzled shared memory with
 //   cp.async double buffering, online softmax in fp32, bf16 mma.sync m16n8k16.
 // attention_temporal: causal softmax over the T frames of one session, per
-//   (patch, head). One warp per problem, lane = 2 of the 64 head dims, k/v for
+//   (patch, head). One warp per problem, lane = 2 of the 64 head dims, q/k/v for
 //   all frames held in registers, scores reduced with warp shuffles.
 #include "common.cuh"
 #include "pointwise.cuh"
@@ -214,6 +215,133 @@ __global__ void __launch_bounds__(NW * 32) attention_full_kernel(const __nv_bflo
   }
 }
 
+// Spatial attention over exactly 144 tokens: one (frame, head) problem per CTA
+// iteration, persistent over problems. 9 warps x 16 query rows cover all 144
+// queries, so K and V are staged once per problem; the whole 16 x 144 score
+// strip of a warp stays in registers (single-pass softmax, no key tail: 144 =
+// 9 x 16). The next problem's q/k/v slices are prefetched into the other half of
+// a double buffer with cp.async while the current one is computed.
+constexpr int kSpatialSeq = 144;
+constexpr int kSpatialWarps = 9;
+constexpr int kSpatialTile = kSpatialSeq * kDh;  // bf16 elements per q, k or v slice
+
+__device__ __forceinline__ void spatial_prefetch(__nv_bfloat16* buf, const __nv_bfloat16* qkv, int item) {
+  const long long row0 = (long long)(item / kHeads) * kSpatialSeq;
+  const __nv_bfloat16* src = qkv + row0 * kQkvLd + (item % kHeads) * kDh;
+  for (int i = threadIdx.x; i < 3 * kSpatialSeq * 8; i += kSpatialWarps * 32) {
+    const int m = i / (kSpatialSeq * 8), rem = i - m * (kSpatialSeq * 8);
+    const int r = rem >> 3, c = (rem & 7) * 8;
+    cp_async16(buf + m * kSpatialTile + swz(r, c), src + (long long)r * kQkvLd + m * kOutLd + c, true);
+  }
+}
+
+__global__ void __launch_bounds__(kSpatialWarps * 32, 1)
+    attention_spatial_kernel(const __nv_bfloat16* __restrict__ qkv, __nv_bfloat16* __restrict__ out, int items) {
+  extern __shared__ __align__(128) __nv_bfloat16 sm[];  // [2][q | k | v]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const float sc = 0.125f * 1.4426950408889634f;  // 1/sqrt(64) * log2(e)
+  int item = blockIdx.x;
+  if (item >= items) return;
+  spatial_prefetch(sm, qkv, item);
+  cp_async_commit();
+  for (int it = 0; item < items; ++it, item += gridDim.x) {
+    __nv_bfloat16* cur = sm + (it & 1) * 3 * kSpatialTile;
+    const int next = item + gridDim.x;
+    if (next < items) spatial_prefetch(sm + ((it + 1) & 1) * 3 * kSpatialTile, qkv, next);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    const __nv_bfloat16* sQ = cur;
+    const __nv_bfloat16* sK = cur + kSpatialTile;
+    const __nv_bfloat16* sV = cur + 2 * kSpatialTile;
+
+    uint32_t qa[4][4];
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      const int r = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+      ldsm_x4(qa[kk], sQ + swz(r, kk * 16 + (lane >> 4) * 8));
+    }
+    float s[18][4];
+#pragma unroll
+    for (int i = 0; i < 18; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
+#pragma unroll
+    for (int np = 0; np < 9; ++np) {
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        uint32_t b[4];
+        const int m = lane >> 3;
+        ldsm_x4(b, sK + swz(np * 16 + (lane & 7) + (m >> 1) * 8, kk * 16 + (m & 1) * 8));
+        mma_bf16(s[2 * np], qa[kk], b[0], b[1]);
+        mma_bf16(s[2 * np + 1], qa[kk], b[2], b[3]);
+      }
+    }
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 18; ++i) {
+      mx0 = fmaxf(mx0, fmaxf(s[i][0], s[i][1]));
+      mx1 = fmaxf(mx1, fmaxf(s[i][2], s[i][3]));
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float o0 = mx0 * sc, o1 = mx1 * sc;
+    float l0 = 0.f, l1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 18; ++i) {
+      s[i][0] = exp2f(s[i][0] * sc - o0);
+      s[i][1] = exp2f(s[i][1] * sc - o0);
+      s[i][2] = exp2f(s[i][2] * sc - o1);
+      s[i][3] = exp2f(s[i][3] * sc - o1);
+      l0 += s[i][0] + s[i][1];
+      l1 += s[i][2] + s[i][3];
+    }
+    float o[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < 9; ++kk) {
+      uint32_t pa[4];
+      pa[0] = pack_bf16x2(s[2 * kk][0], s[2 * kk][1]);
+      pa[1] = pack_bf16x2(s[2 * kk][2], s[2 * kk][3]);
+      pa[2] = pack_bf16x2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      pa[3] = pack_bf16x2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+      for (int dp = 0; dp < 4; ++dp) {
+        uint32_t b[4];
+        const int m = lane >> 3;
+        ldsm_x4_t(b, sV + swz(kk * 16 + (lane & 7) + (m & 1) * 8, dp * 16 + (m >> 1) * 8));
+        mma_bf16(o[2 * dp], pa, b[0], b[1]);
+        mma_bf16(o[2 * dp + 1], pa, b[2], b[3]);
+      }
+    }
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    const float inv0 = 1.f / l0, inv1 = 1.f / l1;
+    // Stage this warp's 16 output rows in its (no longer needed) rows of the q slice,
+    // then write them out as whole 128-byte rows.
+    __nv_bfloat16* sO = cur;
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int c = i * 8 + 2 * t;
+      *reinterpret_cast<uint32_t*>(sO + swz(warp * 16 + g, c)) = pack_bf16x2(o[i][0] * inv0, o[i][1] * inv0);
+      *reinterpret_cast<uint32_t*>(sO + swz(warp * 16 + g + 8, c)) = pack_bf16x2(o[i][2] * inv1, o[i][3] * inv1);
+    }
+    __syncwarp();
+    __nv_bfloat16* ob = out + (long long)(item / kHeads) * kSpatialSeq * kOutLd + (item % kHeads) * kDh;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int r = warp * 16 + k * 4 + (lane >> 3), c = (lane & 7) * 8;
+      *reinterpret_cast<uint4*>(ob + (long long)r * kOutLd + c) = *reinterpret_cast<const uint4*>(sO + swz(r, c));
+    }
+    __syncthreads();  // this buffer is refilled two iterations from now
+  }
+}
+
 // One warp per (session, patch, head); lane owns head dims 2*lane, 2*lane+1.
 template <int TMAX>
 __global__ void __launch_bounds__(256) attention_temporal_kernel(const __nv_bfloat16* __restrict__ qkv,
@@ -230,11 +358,13 @@ __global__ void __launch_bounds__(256) attention_temporal_kernel(const __nv_bflo
   const long long row0 = b * T * P + p;  // row of frame t = row0 + t * P
   const int col = head * kDh + 2 * lane;
 
-  __nv_bfloat162 kr[TMAX], vr[TMAX];
+  // all loads first: q, k, v of every frame (independent 128-byte row segments)
+  __nv_bfloat162 qr[TMAX], kr[TMAX], vr[TMAX];
 #pragma unroll
   for (int s = 0; s < TMAX; ++s) {
     if (s < T) {
       const __nv_bfloat16* rp = qkv + (row0 + (long long)s * P) * kQkvLd + col;
+      qr[s] = *reinterpret_cast<const __nv_bfloat162*>(rp);
       kr[s] = *reinterpret_cast<const __nv_bfloat162*>(rp + kOutLd);
       vr[s] = *reinterpret_cast<const __nv_bfloat162*>(rp + 2 * kOutLd);
     }
@@ -243,8 +373,7 @@ __global__ void __launch_bounds__(256) attention_temporal_kernel(const __nv_bflo
 #pragma unroll
   for (int tq = 0; tq < TMAX; ++tq) {
     if (tq < T) {
-      const float2 q = __bfloat1622float2(
-          *reinterpret_cast<const __nv_bfloat162*>(qkv + (row0 + (long long)tq * P) * kQkvLd + col));
+      const float2 q = __bfloat1622float2(qr[tq]);
       float sc_[TMAX];
       float mx = -INFINITY;
 #pragma unroll
@@ -277,9 +406,26 @@ int attention_full_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, int grou
   OASIS_REQUIRE(qkv && out, "attention_full: null pointer");
   OASIS_REQUIRE(groups >= 0 && seq > 0, "attention_full: bad shape");
   if (groups == 0) return OASIS_OK;
-  if (seq <= 160) {
-    constexpr int NW = 3;  // 48 query rows per CTA: 144 = 3 x 48
+  if (seq == kSpatialSeq) {
+    constexpr int smem = 2 * 3 * kSpatialTile * 2;
+    static bool attr[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr[dev & 63]) {
+      cudaError_t e = cudaFuncSetAttribute(attention_spatial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e != cudaSuccess) return set_error(OASIS_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      attr[dev & 63] = true;
+    }
+    const int items = groups * kHeads;
+    const int grid = items < num_sms() ? items : num_sms();
+    attention_spatial_kernel<<<grid, kSpatialWarps * 32, smem, s>>>(qkv, out, items);
+  } else if (seq <= 160) {
+    constexpr int NW = 3;  // 48 query rows per CTA
     dim3 grid((seq + NW * 16 - 1) / (NW * 16), kHeads, groups);
+    attention_full_kernel<NW><<<grid, NW * 32, 0, s>>>(qkv, out, seq);
+  } else if (seq % 96 == 0) {
+    constexpr int NW = 6;  // 96 query rows per CTA: 576 = 6 x 96
+    dim3 grid(seq / (NW * 16), kHeads, groups);
     attention_full_kernel<NW><<<grid, NW * 32, 0, s>>>(qkv, out, seq);
   } else {
     constexpr int NW = 4;
