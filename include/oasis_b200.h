@@ -224,6 +224,18 @@ typedef struct OasisGemmArgs {
 int oasis_gemm(const OasisGemmArgs* a, oasis_stream_t stream);
 size_t oasis_gemm_workspace_size(int m, int n, int k);
 
+/* oasis_gemm for callers that cannot allocate device memory (their allocator
+ * belongs to a host framework, or allocation is not allowed where they run): the
+ * split-K scratch comes from a library-owned fixed device array of
+ * oasis_gemm_static_scratch_capacity() bytes (8 MiB, held on every GPU that loads
+ * the library) instead of a->workspace, which is ignored. Problems needing more
+ * scratch fail with OASIS_ERR_WORKSPACE. All calls share the array, so calls
+ * that overlap on the GPU race; the first call on a device looks up the array's
+ * address and should come before any stream capture. This entry point has no
+ * counterpart in the reference. */
+int oasis_gemm_static_scratch(const OasisGemmArgs* a, oasis_stream_t stream);
+size_t oasis_gemm_static_scratch_capacity(void);
+
 /* LayerNorm (eps, no affine) + adaLN modulate, or LayerNorm with affine w/b:
  * y_bf16[r] = LN(x[in_row]) * mul + add, where
  *   in_row = (r / P) * in_group + in_off + r % P

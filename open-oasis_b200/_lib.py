@@ -114,6 +114,8 @@ SIGNATURES = {
     "oasis_vae_decode": (C.c_int, [C.POINTER(OasisVaeWeights), C.POINTER(OasisVaeArgs), vp]),
     "oasis_gemm": (C.c_int, [C.POINTER(OasisGemmArgs), vp]),
     "oasis_gemm_workspace_size": (C.c_size_t, [C.c_int, C.c_int, C.c_int]),
+    "oasis_gemm_static_scratch": (C.c_int, [C.POINTER(OasisGemmArgs), vp]),
+    "oasis_gemm_static_scratch_capacity": (C.c_size_t, []),
     "oasis_layernorm": (C.c_int, [C.POINTER(OasisLayerNormArgs), vp]),
     "oasis_silu_bf16": (C.c_int, [fp, vp, C.c_longlong, vp]),
     "oasis_attention_spatial": (C.c_int, [vp, vp, C.c_int, C.c_int, vp]),

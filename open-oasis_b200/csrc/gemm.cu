@@ -562,6 +562,16 @@ size_t gemm_workspace_bytes(int M, int N, int K) {
   return tiles * pl.splits * BM * pl.bn * sizeof(float) + tiles * sizeof(int);
 }
 
+size_t gemm_splitk_bytes(int M, int N, int K, int block_n, int splits) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  Plan pl = choose_plan(M, N, K);
+  if (block_n) pl.bn = block_n;
+  if (splits) pl.splits = splits;
+  if (pl.splits <= 1) return 0;
+  const size_t tiles = (size_t)((M + BM - 1) / BM) * ((N + pl.bn - 1) / pl.bn);
+  return tiles * pl.splits * BM * pl.bn * sizeof(float) + tiles * sizeof(int);
+}
+
 int gemm_launch(const GemmProblem& p, cudaStream_t stream) {
   OASIS_REQUIRE(p.A && p.W, "GEMM: null operand");
   OASIS_REQUIRE(p.M > 0 && p.N > 0 && p.K > 0, "GEMM: bad shape %d x %d x %d", p.M, p.N, p.K);

@@ -55,6 +55,9 @@ int gemm_launch(const GemmProblem& p, cudaStream_t stream);
 // Bytes of split-K workspace the heuristic may want for an M x N x K problem.
 size_t gemm_workspace_bytes(int M, int N, int K);
 
+// Split-K workspace bytes a launch with these overrides (0 = heuristic) needs.
+size_t gemm_splitk_bytes(int M, int N, int K, int block_n, int splits);
+
 int num_sms();
 
 }  // namespace oasis
