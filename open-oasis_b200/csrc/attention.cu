@@ -75,6 +75,8 @@ __device__ __forceinline__ void load_tile(__nv_bfloat16* dst, const __nv_bfloat1
 template <int NW>
 __global__ void __launch_bounds__(NW * 32) attention_full_kernel(const __nv_bfloat16* __restrict__ qkv,
                                                                  __nv_bfloat16* __restrict__ out, int seq) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int NT = NW * 32;
   constexpr int QROWS = NW * 16;
   __shared__ __align__(128) __nv_bfloat16 sQ[QROWS * kDh];
@@ -237,6 +239,8 @@ __device__ __forceinline__ void spatial_prefetch(__nv_bfloat16* buf, const __nv_
 
 __global__ void __launch_bounds__(kSpatialWarps * 32, 1)
     attention_spatial_kernel(const __nv_bfloat16* __restrict__ qkv, __nv_bfloat16* __restrict__ out, int items) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(128) __nv_bfloat16 sm[];  // [2][q | k | v]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
@@ -347,6 +351,8 @@ template <int TMAX>
 __global__ void __launch_bounds__(256) attention_temporal_kernel(const __nv_bfloat16* __restrict__ qkv,
                                                                  __nv_bfloat16* __restrict__ out, int batch,
                                                                  int T, int P) {
+  pdl_trigger();
+  pdl_wait();
   const long long w = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const long long total = (long long)batch * P * kHeads;
@@ -418,19 +424,19 @@ int attention_full_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, int grou
     }
     const int items = groups * kHeads;
     const int grid = items < num_sms() ? items : num_sms();
-    attention_spatial_kernel<<<grid, kSpatialWarps * 32, smem, s>>>(qkv, out, items);
+    launch_pdl(attention_spatial_kernel, dim3(grid), dim3(kSpatialWarps * 32), smem, s, qkv, out, items);
   } else if (seq <= 160) {
     constexpr int NW = 3;  // 48 query rows per CTA
     dim3 grid((seq + NW * 16 - 1) / (NW * 16), kHeads, groups);
-    attention_full_kernel<NW><<<grid, NW * 32, 0, s>>>(qkv, out, seq);
+    launch_pdl(attention_full_kernel<NW>, dim3(grid), dim3(NW * 32), 0, s, qkv, out, seq);
   } else if (seq % 96 == 0) {
     constexpr int NW = 6;  // 96 query rows per CTA: 576 = 6 x 96
     dim3 grid(seq / (NW * 16), kHeads, groups);
-    attention_full_kernel<NW><<<grid, NW * 32, 0, s>>>(qkv, out, seq);
+    launch_pdl(attention_full_kernel<NW>, dim3(grid), dim3(NW * 32), 0, s, qkv, out, seq);
   } else {
     constexpr int NW = 4;
     dim3 grid((seq + NW * 16 - 1) / (NW * 16), kHeads, groups);
-    attention_full_kernel<NW><<<grid, NW * 32, 0, s>>>(qkv, out, seq);
+    launch_pdl(attention_full_kernel<NW>, dim3(grid), dim3(NW * 32), 0, s, qkv, out, seq);
   }
   return check_launch("attention_full_kernel");
 }
@@ -443,15 +449,15 @@ int attention_temporal_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, int 
   if (warps == 0) return OASIS_OK;
   const int grid = (int)((warps * 32 + 255) / 256);
   if (frames <= 2)
-    attention_temporal_kernel<2><<<grid, 256, 0, s>>>(qkv, out, batch, frames, P);
+    launch_pdl(attention_temporal_kernel<2>, dim3(grid), dim3(256), 0, s, qkv, out, batch, frames, P);
   else if (frames <= 4)
-    attention_temporal_kernel<4><<<grid, 256, 0, s>>>(qkv, out, batch, frames, P);
+    launch_pdl(attention_temporal_kernel<4>, dim3(grid), dim3(256), 0, s, qkv, out, batch, frames, P);
   else if (frames <= 8)
-    attention_temporal_kernel<8><<<grid, 256, 0, s>>>(qkv, out, batch, frames, P);
+    launch_pdl(attention_temporal_kernel<8>, dim3(grid), dim3(256), 0, s, qkv, out, batch, frames, P);
   else if (frames <= 16)
-    attention_temporal_kernel<16><<<grid, 256, 0, s>>>(qkv, out, batch, frames, P);
+    launch_pdl(attention_temporal_kernel<16>, dim3(grid), dim3(256), 0, s, qkv, out, batch, frames, P);
   else
-    attention_temporal_kernel<32><<<grid, 256, 0, s>>>(qkv, out, batch, frames, P);
+    launch_pdl(attention_temporal_kernel<32>, dim3(grid), dim3(256), 0, s, qkv, out, batch, frames, P);
   return check_launch("attention_temporal_kernel");
 }
 

@@ -3,6 +3,7 @@
 // kernel sequence of one sub-block, one step and one decode on a caller stream.
 #include <stdarg.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <atomic>
@@ -28,6 +29,14 @@ int set_error(int code, const char* fmt, ...) {
 }
 
 int read_device_error(int reset);  // gemm.cu
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("OASIS_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
 
 namespace {
 

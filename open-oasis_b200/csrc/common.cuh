@@ -11,7 +11,30 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 namespace oasis {
+
+// Whether kernels are launched with programmatic stream serialization
+// (OASIS_PDL=0 in the environment turns it off; read once per process).
+bool pdl_enabled();
+
+// Launches `kernel` on `s`, with programmatic dependent launch when enabled.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // ---------------------------------------------------------------------------
 // Device error word. Kernels never trap: a wait that gives up records a code
@@ -126,6 +149,11 @@ __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.comm
 // Wait until the source shared memory of all committed bulk stores has been read.
 __device__ __forceinline__ void bulk_wait_read0() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+// Wait until at most one committed bulk store still reads its source.
+__device__ __forceinline__ void bulk_wait_read1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
 }
 
 // Wait until all committed bulk stores have completed.
@@ -248,6 +276,14 @@ __device__ __forceinline__ bool elect_one() {
       : "r"(0xffffffffu));
   return pred != 0;
 }
+
+// Programmatic dependent launch. A kernel launched with launch_pdl may start
+// while the previous kernel on the stream is still running: it triggers its own
+// dependents at entry and must pdl_wait() before reading anything an earlier
+// kernel wrote (or writing anything an earlier kernel may still read). Both are
+// no-ops for a normal launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 __device__ __forceinline__ void named_barrier_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");

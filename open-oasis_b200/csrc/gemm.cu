@@ -37,13 +37,16 @@ constexpr int kStgBytes = 32 * 128;          // per-warp store staging: 32 rows 
 
 template <int BN>
 struct Cfg {
-  static constexpr int STAGES = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
+  // Narrow tiles get two staging buffers per epilogue warp (store of one chunk
+  // overlaps the next; residual tiles are TMA-loaded into them ahead of time).
+  static constexpr int NBUF = BN == 256 ? 1 : 2;
+  static constexpr int STAGES = BN == 256 ? 4 : (BN == 128 ? 5 : 6);
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;  // two accumulators; 128/256/512 (power of 2)
-  static constexpr int STG_BYTES = kEpiWarps * kStgBytes;
-  static constexpr int BAR_BYTES = 256;
+  static constexpr int STG_BYTES = kEpiWarps * kStgBytes * NBUF;
+  static constexpr int BAR_BYTES = 512;
   static constexpr int SMEM = 1024 /*align slack*/ + STAGES * STAGE_BYTES + STG_BYTES + BAR_BYTES;
 };
 
@@ -149,8 +152,14 @@ __device__ __forceinline__ void store_image(const EpiParams& e, int r, int nb, i
 // The warp's staging tile holds one 32-row x 128-byte box for a TMA store; row
 // `lane` belongs to this thread and its 16-byte chunks are XOR-swizzled by
 // lane % 8 (TMA's 128-byte swizzle), so the writes are bank-conflict free.
-__device__ __forceinline__ void stage_begin(int lane) {
-  if (lane == 0) bulk_wait_read0();  // the previous store from this buffer has read it
+__device__ __forceinline__ void stage_begin(int lane, int nbuf) {
+  // the store that last used the buffer about to be written has read it
+  if (lane == 0) {
+    if (nbuf == 2)
+      bulk_wait_read1();
+    else
+      bulk_wait_read0();
+  }
   __syncwarp();
 }
 
@@ -185,9 +194,9 @@ __device__ __forceinline__ void stage_commit(const CUtensorMap* tm_out, uint8_t*
 // (32 fp32 or 64 bf16 columns), processed as 32-column groups; the warp takes
 // chunks c = half, half + 2, ...
 __device__ __forceinline__ void epilogue_tile(const EpiParams& e, const SplitK& sk, const CUtensorMap* tm_out,
-                                              uint8_t* stg, uint32_t t_acc, int M, int N, int BN, int m0q, int n0,
-                                              int tile, int split, int quarter, int half, int lane,
-                                              uint64_t* acc_bar, uint32_t acc_parity, bool& ok) {
+                                              uint8_t* stg, int nbuf, int& sbuf, uint32_t t_acc, int M, int N,
+                                              int BN, int m0q, int n0, int tile, int split, int quarter, int half,
+                                              int lane, uint64_t* acc_bar, uint32_t acc_parity, bool& ok) {
   const int r = m0q + lane;
   const bool bf16 = bf16_out(e.mode);
   const int W = bf16 ? 64 : 32;
@@ -208,7 +217,8 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& e, const SplitK& 
     if (sk.splits == 1 && nb >= N) break;  // warp-uniform
     float4 rnext[8];
     if (resid && c + 2 < nchunks && nb + 2 * W < N) load_resid(e, r, nb + 2 * W, M, rnext);
-    if (sk.splits == 1 && e.mode != kEpiImage) stage_begin(lane);
+    uint8_t* buf = stg + sbuf * kStgBytes;
+    if (sk.splits == 1 && e.mode != kEpiImage) stage_begin(lane, nbuf);
 #pragma unroll 1
     for (int g = 0; g < W / 32; ++g) {
       float v[32];
@@ -223,17 +233,71 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& e, const SplitK& 
         if (e.mode == kEpiImage) {
           if (r < M) store_image(e, r, nb, N, v);
         } else {
-          stage_write(stg, lane, bf16, g * 4, v);
+          stage_write(buf, lane, bf16, g * 4, v);
         }
       }
     }
     if (sk.splits == 1) {
-      if (e.mode != kEpiImage) stage_commit(tm_out, stg, lane, m0q, nb);
+      if (e.mode != kEpiImage) {
+        stage_commit(tm_out, buf, lane, m0q, nb);
+        if (nbuf == 2) sbuf ^= 1;
+      }
       if (resid) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) rcur[i] = rnext[i];
       }
     }
+  }
+}
+
+// Epilogue of a residual tile (fp32 in and out, no split-K) on a kernel with two
+// staging buffers per warp: the warp's (at most two) 32-column residual boxes are
+// TMA-loaded into its buffers before the accumulator is ready, the result is
+// computed in place and TMA-stored from the same buffer.
+__device__ __forceinline__ void epilogue_tile_resid(const EpiParams& e, const CUtensorMap* tm_out,
+                                                    const CUtensorMap* tm_res, uint8_t* stg, uint64_t* rbar,
+                                                    uint32_t& rphase, uint32_t t_acc, int M, int N, int BN, int m0q,
+                                                    int n0, int half, int lane, uint64_t* acc_bar,
+                                                    uint32_t acc_parity, bool& ok) {
+  const int r = m0q + lane;
+  const int nchunks = BN / 32;
+  if (lane == 0) {
+    bulk_wait_read0();  // earlier stores no longer read the buffers
+    for (int i = 0; i < 2; ++i) {
+      const int c = half + 2 * i;
+      if (c < nchunks && n0 + c * 32 < N) {
+        mbar_arrive_expect_tx(&rbar[i], kStgBytes);
+        tma_load_2d(stg + i * kStgBytes, tm_res, &rbar[i], n0 + c * 32, m0q);
+      }
+    }
+  }
+  __syncwarp();
+  if (!mbar_wait(acc_bar, acc_parity, kDevTimeoutAccFull)) {
+    ok = false;
+    return;
+  }
+  tc_fence_after();
+#pragma unroll 1
+  for (int i = 0; i < 2; ++i) {
+    const int c = half + 2 * i;
+    const int nb = n0 + c * 32;
+    if (c >= nchunks || nb >= N) break;  // warp-uniform
+    uint8_t* buf = stg + i * kStgBytes;
+    if (!mbar_wait(&rbar[i], (rphase >> i) & 1, kDevTimeoutAccFull)) {
+      ok = false;
+      return;
+    }
+    rphase ^= 1u << i;
+    float v[32];
+    __syncwarp();
+    tmem_ld32(t_acc + c * 32, v);
+    uint8_t* row = buf + lane * 128;
+    float4 res[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) res[j] = *reinterpret_cast<const float4*>(row + ((j ^ (lane & 7)) << 4));
+    epilogue_math(e, r, nb, v, res);
+    stage_write(buf, lane, false, 0, v);
+    stage_commit(tm_out, buf, lane, m0q, nb);
   }
 }
 
@@ -250,7 +314,7 @@ __device__ __forceinline__ void splitk_reduce(const EpiParams& e, const SplitK& 
   for (int c = half; c < nchunks; c += 2) {
     const int nb = n0 + c * W;
     if (nb >= N) break;
-    if (e.mode != kEpiImage) stage_begin(lane);
+    if (e.mode != kEpiImage) stage_begin(lane, 1);
 #pragma unroll 1
     for (int g = 0; g < W / 32; ++g) {
       float v[32];
@@ -280,7 +344,8 @@ __device__ __forceinline__ void splitk_reduce(const EpiParams& e, const SplitK& 
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
-                const __grid_constant__ CUtensorMap tmO, const int M, const int N, const int K,
+                const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR, const int M,
+                const int N, const int K,
                 const EpiParams epi, const SplitK sk) {
   using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
@@ -292,9 +357,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   int* sk_flag = reinterpret_cast<int*>(tmem_base_slot + 1);
+  uint64_t* rbar = reinterpret_cast<uint64_t*>(tmem_base_slot + 4);  // [kEpiWarps][2], 8-byte aligned
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  pdl_trigger();
 
   const int m_tiles = (M + BM - 1) / BM;
   const int n_tiles = (N + BN - 1) / BN;
@@ -307,6 +374,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmW);
     if (epi.mode != kEpiImage) prefetch_tmap(&tmO);
+    if (reads_resid(epi.mode)) prefetch_tmap(&tmR);
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -315,6 +383,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&acc_full[a], 1);
       mbar_init(&acc_empty[a], kEpiWarps);
     }
+    for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&rbar[i], 1);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -325,6 +394,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_base_slot;
+  if (warp != 0) pdl_wait();  // the producer waits after prefetching weights
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -332,16 +402,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      // Weights are never written by an earlier kernel: start streaming the first
+      // stages' W tiles before waiting for the upstream kernel (programmatic
+      // dependent launch), then add the A tiles once its output is visible.
+      int pre = 0;
+      if ((int)blockIdx.x < units) {
+        const int tile = blockIdx.x / splits, split = blockIdx.x - tile * splits;
+        const int n0 = (tile % n_tiles) * BN, kb0 = split * kb_per_split;
+        pre = kb_per_split < C::STAGES ? kb_per_split : C::STAGES;
+        for (int i = 0; i < pre; ++i) {
+          mbar_arrive_expect_tx(&full[i], C::STAGE_BYTES);
+          tma_load_2d(smem + i * C::STAGE_BYTES + C::A_BYTES, &tmW, &full[i], (kb0 + i) * BK, n0);
+        }
+      }
+      pdl_wait();
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
         const int tile = u / splits, split = u - tile * splits;
         const int m0 = (tile / n_tiles) * BM, n0 = (tile % n_tiles) * BN;
         const int kb0 = split * kb_per_split;
         for (int kb = kb0; kb < kb0 + kb_per_split; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, kDevTimeoutSmemEmpty)) { ok = false; break; }
           uint8_t* sa = smem + stage * C::STAGE_BYTES;
-          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
-          tma_load_2d(sa, &tmA, &full[stage], kb * BK, m0);
-          tma_load_2d(sa + C::A_BYTES, &tmW, &full[stage], kb * BK, n0);
+          if (u == (int)blockIdx.x && kb - kb0 < pre) {
+            tma_load_2d(sa, &tmA, &full[stage], kb * BK, m0);  // W already in flight
+          } else {
+            if (!mbar_wait(&empty[stage], phase ^ 1, kDevTimeoutSmemEmpty)) { ok = false; break; }
+            mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+            tma_load_2d(sa, &tmA, &full[stage], kb * BK, m0);
+            tma_load_2d(sa + C::A_BYTES, &tmW, &full[stage], kb * BK, n0);
+          }
           if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
         }
       }
@@ -388,7 +476,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    uint8_t* stg = staging + (warp - 2) * kStgBytes;
+    uint8_t* stg = staging + (warp - 2) * kStgBytes * C::NBUF;
+    uint64_t* my_rbar = rbar + 2 * (warp - 2);
+    const bool resid_tma = C::NBUF == 2 && reads_resid(epi.mode) && splits == 1;
+    int sbuf = 0;
+    uint32_t rphase = 0;
     const int ep_tid = threadIdx.x - 64;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -397,8 +489,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int tile = u / splits, split = u - tile * splits;
       const int m0q = (tile / n_tiles) * BM + quarter * 32, n0 = (tile % n_tiles) * BN;
       const uint32_t t_acc = tmem_base + lane_off + acc * BN;
-      epilogue_tile(epi, sk, &tmO, stg, t_acc, M, N, BN, m0q, n0, tile, split, quarter, half, lane,
-                    &acc_full[acc], acc_phase, ok);
+      if (resid_tma)
+        epilogue_tile_resid(epi, &tmO, &tmR, stg, my_rbar, rphase, t_acc, M, N, BN, m0q, n0, half, lane,
+                            &acc_full[acc], acc_phase, ok);
+      else
+        epilogue_tile(epi, sk, &tmO, stg, C::NBUF, sbuf, t_acc, M, N, BN, m0q, n0, tile, split, quarter, half,
+                      lane, &acc_full[acc], acc_phase, ok);
       if (!ok) break;
       tc_fence_before();
       __syncwarp();
@@ -495,13 +591,17 @@ int launch_bn(const GemmProblem& p, int splits, cudaStream_t stream) {
     if (e != cudaSuccess) return set_error(OASIS_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     attr_set[dev & 63] = true;
   }
-  CUtensorMap ta, tw, to;
+  CUtensorMap ta, tw, to, tr;
   OASIS_TRY(make_map(&ta, p.A, p.M, p.K, p.lda, BM));
   OASIS_TRY(make_map(&tw, p.W, p.N, p.K, p.K, BN));
   if (p.epi.mode == kEpiImage)
     to = ta;  // unused: the image epilogue scatters directly
   else
     OASIS_TRY(make_out_map(&to, p.epi.out, p.M, p.N, p.epi.ldo, bf16_out(p.epi.mode)));
+  if (reads_resid(p.epi.mode))
+    OASIS_TRY(make_out_map(&tr, const_cast<float*>(p.epi.resid), p.M, p.N, p.epi.ldr, false));  // same box as the output
+  else
+    tr = to;
   const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
   SplitK sk{nullptr, nullptr, splits};
   if (splits > 1) {
@@ -517,7 +617,7 @@ int launch_bn(const GemmProblem& p, int splits, cudaStream_t stream) {
   }
   const int units = tiles * splits;
   const int grid = units < num_sms() ? units : num_sms();
-  gemm_kernel<BN><<<grid, kThreads, C::SMEM, stream>>>(ta, tw, to, p.M, p.N, p.K, p.epi, sk);
+  launch_pdl(gemm_kernel<BN>, dim3(grid), dim3(kThreads), C::SMEM, stream, ta, tw, to, tr, p.M, p.N, p.K, p.epi, sk);
   return check_launch("gemm_kernel");
 }
 
@@ -533,13 +633,11 @@ Plan choose_plan(int M, int N, int K) {
   if (t256 >= sms && N % 256 == 0) return {256, 1};
   const int t128 = mt * ((N + 127) / 128);
   if (t128 >= sms) return {128, 1};
-  // Small problems (a handful of sessions): narrow tiles, then split K until
-  // there is roughly one work unit per SM so the weight stream uses all of HBM.
-  const int t64 = mt * ((N + 63) / 64);
-  const int kb = K / BK;
-  int splits = 1;
-  while (t64 * splits * 2 <= sms && kb % (splits * 2) == 0 && kb / (splits * 2) >= 4) splits *= 2;
-  return {64, splits};
+  // Small problems (a handful of sessions): narrow tiles so most SMs stream a
+  // slice of the weights. Split-K is not chosen: measured on B200 at M = 288-576,
+  // its fix-up pass costs more than the extra parallelism returns.
+  (void)K;
+  return {t128 >= sms / 2 ? 128 : 64, 1};
 }
 
 }  // namespace
@@ -584,6 +682,10 @@ int gemm_launch(const GemmProblem& p, cudaStream_t stream) {
   if (p.epi.mode == kEpiGatedResid) OASIS_REQUIRE(p.epi.gate && p.epi.rows_per_frame > 0, "GEMM: gate missing");
   if (p.epi.mode == kEpiRopeBF16) OASIS_REQUIRE(p.epi.rope && p.epi.rope_mod > 0 && p.epi.rope_div > 0, "GEMM: rope table missing");
   Plan pl = choose_plan(p.M, p.N, p.K);
+  // Residual epilogues stream fp32 in and out: narrower tiles have the staging
+  // room to prefetch the residual with TMA (kept only where K is short enough
+  // for the epilogue to dominate; at K = 4096 the wider mainloop wins).
+  if (pl.bn == 256 && reads_resid(p.epi.mode) && p.K <= 1024) pl.bn = 128;
   if (p.block_n) pl.bn = p.block_n;
   if (p.splits) pl.splits = p.splits;
   if (pl.splits > 1 && !p.workspace) pl.splits = 1;

@@ -21,6 +21,8 @@ constexpr int D = 1024;  // model width of both the DiT and the VAE decoder
 // Affine:    y = LN(x) * w + b.
 __global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y,
                                                         LayerNormParams p) {
+  pdl_trigger();
+  pdl_wait();
   const int warp_global = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp_global >= p.rows_out) return;
@@ -74,6 +76,8 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict_
 }
 
 __global__ void silu_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, long long n4) {
+  pdl_trigger();
+  pdl_wait();
   long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
   for (; i < n4; i += (long long)gridDim.x * blockDim.x) {
     const float4 a = reinterpret_cast<const float4*>(x)[i];
@@ -91,6 +95,8 @@ constexpr int kEmbedRows = 16;
 __global__ void __launch_bounds__(256) patch_embed_kernel(const float* __restrict__ chunk, const float* __restrict__ w,
                                                           const float* __restrict__ b, float* __restrict__ z,
                                                           PatchEmbedParams p) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float xs[kEmbedRows][64];
   const int r0 = blockIdx.x * kEmbedRows;
   for (int i = threadIdx.x; i < kEmbedRows * 64; i += 256) {
@@ -126,6 +132,8 @@ __global__ void __launch_bounds__(256) patch_embed_kernel(const float* __restric
 }
 
 __global__ void ddim_kernel(float* __restrict__ chunk, const float* __restrict__ v, DdimCoeffs c, long long n) {
+  pdl_trigger();
+  pdl_wait();
   long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
   for (; i < n; i += (long long)gridDim.x * blockDim.x) {
     const float x = chunk[i];
@@ -138,6 +146,8 @@ __global__ void ddim_kernel(float* __restrict__ chunk, const float* __restrict__
 // chunk [B, 144, 64] in (h, w, p, q, c) order -> latent tokens [B, 576, 16]:
 // latent[b, (2h+p)*32 + (2w+q), c] = chunk[b, h*16+w, p*32 + q*16 + c] * inv_scale.
 __global__ void bridge_kernel(const float* __restrict__ chunk, float* __restrict__ lat, int batch, float inv_scale) {
+  pdl_trigger();
+  pdl_wait();
   const long long n = (long long)batch * 576 * 16;
   long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
   for (; i < n; i += (long long)gridDim.x * blockDim.x) {
@@ -154,6 +164,8 @@ __global__ void bridge_kernel(const float* __restrict__ chunk, float* __restrict
 // z[r, :] = lat[r, :16] . W[16, 1024] + b  (VAE post_quant_conv as a linear map)
 __global__ void __launch_bounds__(256) post_quant_kernel(const float* __restrict__ lat, const float* __restrict__ w,
                                                          const float* __restrict__ b, float* __restrict__ z, int rows) {
+  pdl_trigger();
+  pdl_wait();
   const int r = blockIdx.x;
   if (r >= rows) return;
   __shared__ float xs[16];
@@ -187,14 +199,14 @@ int layernorm_launch(const float* x, __nv_bfloat16* y, const LayerNormParams& p,
   if (p.rows_out == 0) return OASIS_OK;
   const int warps_per_block = 8;
   const int grid = (p.rows_out + warps_per_block - 1) / warps_per_block;
-  layernorm_kernel<<<grid, 32 * warps_per_block, 0, s>>>(x, y, p);
+  launch_pdl(layernorm_kernel, dim3(grid), dim3(32 * warps_per_block), 0, s, x, y, p);
   return check_launch("layernorm_kernel");
 }
 
 int silu_bf16_launch(const float* x, __nv_bfloat16* y, long long n, cudaStream_t s) {
   OASIS_REQUIRE(n % 4 == 0, "silu: n must be a multiple of 4");
   if (n == 0) return OASIS_OK;
-  silu_bf16_kernel<<<grid_for(n / 4, 256), 256, 0, s>>>(x, y, n / 4);
+  launch_pdl(silu_bf16_kernel, dim3(grid_for(n / 4, 256)), dim3(256), 0, s, x, y, n / 4);
   return check_launch("silu_bf16_kernel");
 }
 
@@ -202,28 +214,28 @@ int patch_embed_launch(const float* chunk, const float* w, const float* b, float
                        cudaStream_t s) {
   OASIS_REQUIRE(chunk && w && z, "patch_embed: null pointer");
   if (p.rows == 0) return OASIS_OK;
-  patch_embed_kernel<<<(p.rows + kEmbedRows - 1) / kEmbedRows, 256, 0, s>>>(chunk, w, b, z, p);
+  launch_pdl(patch_embed_kernel, dim3((p.rows + kEmbedRows - 1) / kEmbedRows), dim3(256), 0, s, chunk, w, b, z, p);
   return check_launch("patch_embed_kernel");
 }
 
 int ddim_launch(float* chunk, const float* v, const DdimCoeffs& c, long long n, cudaStream_t s) {
   OASIS_REQUIRE(chunk && v, "ddim: null pointer");
   if (n == 0) return OASIS_OK;
-  ddim_kernel<<<grid_for(n, 256), 256, 0, s>>>(chunk, v, c, n);
+  launch_pdl(ddim_kernel, dim3(grid_for(n, 256)), dim3(256), 0, s, chunk, v, c, n);
   return check_launch("ddim_kernel");
 }
 
 int bridge_launch(const float* chunk, float* latent, int batch, float inv_scale, cudaStream_t s) {
   OASIS_REQUIRE(chunk && latent && batch >= 0, "bridge: bad arguments");
   if (batch == 0) return OASIS_OK;
-  bridge_kernel<<<grid_for((long long)batch * 576 * 16, 256), 256, 0, s>>>(chunk, latent, batch, inv_scale);
+  launch_pdl(bridge_kernel, dim3(grid_for((long long)batch * 576 * 16, 256)), dim3(256), 0, s, chunk, latent, batch, inv_scale);
   return check_launch("bridge_kernel");
 }
 
 int post_quant_launch(const float* lat, const float* w, const float* b, float* z, int rows, cudaStream_t s) {
   OASIS_REQUIRE(lat && w && z, "post_quant: null pointer");
   if (rows == 0) return OASIS_OK;
-  post_quant_kernel<<<rows, 256, 0, s>>>(lat, w, b, z, rows);
+  launch_pdl(post_quant_kernel, dim3(rows), dim3(256), 0, s, lat, w, b, z, rows);
   return check_launch("post_quant_kernel");
 }
 

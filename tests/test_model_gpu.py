@@ -83,7 +83,7 @@ def _frame_inputs(sd, B, T, seed):
     g = torch.Generator().manual_seed(seed)
     chunk = H.patchify(torch.randn(B, 16, 18, 32, generator=g).clamp(-H.NOISE_ABS_MAX, H.NOISE_ABS_MAX))
     ctx_lat = torch.randn(B * (T - 1), 16, 18, 32, generator=g)
-    ctx_z = O.patch_embed(ctx_lat, sd).reshape(B, T - 1, H.N_PATCHES, H.D_MODEL)
+    ctx_z = O.patch_embed(ctx_lat, sd).reshape(B, T - 1, H.N_PATCHES, H.D_MODEL).contiguous()
     actions = torch.zeros(B, 25)
     actions[torch.arange(B), torch.randint(0, 25, (B,), generator=g)] = 1
     steps = H.ddim_schedule()
@@ -145,3 +145,10 @@ def test_device_error_word_clear():
     from oasis_b200 import _lib
 
     assert _lib.load().oasis_device_error(1) == 0
+
+
+def test_graft_smoke():
+    """The driver's smoke check (one small DDIM step + VAE decode vs the oracle)."""
+    import __graft_entry__
+
+    __graft_entry__.smoke()
