@@ -37,10 +37,11 @@ constexpr int kStgBytes = 32 * 128;          // per-warp store staging: 32 rows 
 
 template <int BN>
 struct Cfg {
-  // Narrow tiles get two staging buffers per epilogue warp (store of one chunk
-  // overlaps the next; residual tiles are TMA-loaded into them ahead of time).
-  static constexpr int NBUF = BN == 256 ? 1 : 2;
-  static constexpr int STAGES = BN == 256 ? 4 : (BN == 128 ? 5 : 6);
+  // Two staging buffers per epilogue warp (the store of one chunk overlaps the
+  // next; residual tiles are TMA-loaded into them ahead of time). Measured on
+  // B200: worth a pipeline stage even at BN = 256.
+  static constexpr int NBUF = 2;
+  static constexpr int STAGES = BN == 256 ? 3 : (BN == 128 ? 5 : 6);
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -250,10 +251,10 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& e, const SplitK& 
   }
 }
 
-// Epilogue of a residual tile (fp32 in and out, no split-K) on a kernel with two
-// staging buffers per warp: the warp's (at most two) 32-column residual boxes are
-// TMA-loaded into its buffers before the accumulator is ready, the result is
-// computed in place and TMA-stored from the same buffer.
+// Epilogue of a residual tile (fp32 in and out, no split-K): the warp's 32-column
+// residual boxes are TMA-loaded into its two staging buffers (the first two before
+// the accumulator is ready, later ones as soon as a buffer's store has read it),
+// the result is computed in place and TMA-stored from the same buffer.
 __device__ __forceinline__ void epilogue_tile_resid(const EpiParams& e, const CUtensorMap* tm_out,
                                                     const CUtensorMap* tm_res, uint8_t* stg, uint64_t* rbar,
                                                     uint32_t& rphase, uint32_t t_acc, int M, int N, int BN, int m0q,
@@ -261,14 +262,13 @@ __device__ __forceinline__ void epilogue_tile_resid(const EpiParams& e, const CU
                                                     uint32_t acc_parity, bool& ok) {
   const int r = m0q + lane;
   const int nchunks = BN / 32;
+  int mine = 0;  // this warp's chunks: c = half + 2 i, i < mine
+  while (half + 2 * mine < nchunks && n0 + (half + 2 * mine) * 32 < N) ++mine;
   if (lane == 0) {
     bulk_wait_read0();  // earlier stores no longer read the buffers
-    for (int i = 0; i < 2; ++i) {
-      const int c = half + 2 * i;
-      if (c < nchunks && n0 + c * 32 < N) {
-        mbar_arrive_expect_tx(&rbar[i], kStgBytes);
-        tma_load_2d(stg + i * kStgBytes, tm_res, &rbar[i], n0 + c * 32, m0q);
-      }
+    for (int i = 0; i < 2 && i < mine; ++i) {
+      mbar_arrive_expect_tx(&rbar[i], kStgBytes);
+      tma_load_2d(stg + i * kStgBytes, tm_res, &rbar[i], n0 + (half + 2 * i) * 32, m0q);
     }
   }
   __syncwarp();
@@ -278,16 +278,16 @@ __device__ __forceinline__ void epilogue_tile_resid(const EpiParams& e, const CU
   }
   tc_fence_after();
 #pragma unroll 1
-  for (int i = 0; i < 2; ++i) {
+  for (int i = 0; i < mine; ++i) {
+    const int b = i & 1;
     const int c = half + 2 * i;
     const int nb = n0 + c * 32;
-    if (c >= nchunks || nb >= N) break;  // warp-uniform
-    uint8_t* buf = stg + i * kStgBytes;
-    if (!mbar_wait(&rbar[i], (rphase >> i) & 1, kDevTimeoutAccFull)) {
+    uint8_t* buf = stg + b * kStgBytes;
+    if (!mbar_wait(&rbar[b], (rphase >> b) & 1, kDevTimeoutAccFull)) {
       ok = false;
       return;
     }
-    rphase ^= 1u << i;
+    rphase ^= 1u << b;
     float v[32];
     __syncwarp();
     tmem_ld32(t_acc + c * 32, v);
@@ -298,6 +298,14 @@ __device__ __forceinline__ void epilogue_tile_resid(const EpiParams& e, const CU
     epilogue_math(e, r, nb, v, res);
     stage_write(buf, lane, false, 0, v);
     stage_commit(tm_out, buf, lane, m0q, nb);
+    if (i + 2 < mine) {  // refill this buffer with chunk i + 2 once the store has read it
+      if (lane == 0) {
+        bulk_wait_read0();
+        mbar_arrive_expect_tx(&rbar[b], kStgBytes);
+        tma_load_2d(buf, tm_res, &rbar[b], n0 + (c + 4) * 32, m0q);
+      }
+      __syncwarp();
+    }
   }
 }
 
@@ -682,10 +690,6 @@ int gemm_launch(const GemmProblem& p, cudaStream_t stream) {
   if (p.epi.mode == kEpiGatedResid) OASIS_REQUIRE(p.epi.gate && p.epi.rows_per_frame > 0, "GEMM: gate missing");
   if (p.epi.mode == kEpiRopeBF16) OASIS_REQUIRE(p.epi.rope && p.epi.rope_mod > 0 && p.epi.rope_div > 0, "GEMM: rope table missing");
   Plan pl = choose_plan(p.M, p.N, p.K);
-  // Residual epilogues stream fp32 in and out: narrower tiles have the staging
-  // room to prefetch the residual with TMA (kept only where K is short enough
-  // for the epilogue to dominate; at K = 4096 the wider mainloop wins).
-  if (pl.bn == 256 && reads_resid(p.epi.mode) && p.K <= 1024) pl.bn = 128;
   if (p.block_n) pl.bn = p.block_n;
   if (p.splits) pl.splits = p.splits;
   if (pl.splits > 1 && !p.workspace) pl.splits = 1;
