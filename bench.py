@@ -291,6 +291,7 @@ def latency_extras(dw, vw, peaks):
     torch.cuda.synchronize()
     k = 20
     ms_frame = time_graph(fe.replay, k) / k
+    fe.capture(breakdown=True)
     ms_steps = time_graph(fe.graph_steps.replay, k) / k
     # weights read per DiT step (the B=1 HBM floor): 606.2 M params bf16
     dit_bytes = sum(t.numel() * t.element_size() for blk in dw.tensors.values() for t in blk.values())
@@ -328,6 +329,7 @@ def main():
     n0 = _lib.load().oasis_launch_count()
     fe.capture()
     launches_per_frame = (_lib.load().oasis_launch_count() - n0) // 2  # eager frame + captured frame
+    fe.capture(breakdown=True)  # steps-only and decode-only graphs for the timing split
 
     def frame():
         fe.replay()
@@ -346,8 +348,7 @@ def main():
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
     ev[0].record()
     for _ in range(args.steps):
-        fe.graph_steps.replay()
-        fe.graph_decode.replay()
+        fe.replay()
     ev[1].record()
     barrier()
     ms = ev[0].elapsed_time(ev[1])

@@ -191,6 +191,33 @@ typedef struct OasisVaeArgs {
 size_t oasis_vae_workspace_size(int batch);
 int oasis_vae_decode(const OasisVaeWeights* w, const OasisVaeArgs* a, oasis_stream_t stream);
 
+/* One generated frame for B sessions (run_full_frame, oasis_inference.py:2175-2232):
+ * `steps` DDIM steps through the DiT, then the bridge and the VAE decode. The
+ * adaLN tables of all steps come from one GEMM, so the stacked adaLN weights are
+ * read once per frame instead of once per step.
+ *   chunk     [B, 144, 64] fp32 noise patches in, final latent patches out
+ *   context_z [B, T-1, 144, 1024] fp32 embedded context frames (NULL if T == 1)
+ *   cond      [steps, B, T, 1024] fp32 conditioning of every step (pre-SiLU)
+ *   coeffs    HOST array of `steps` DDIM coefficient sets, highest noise first
+ *   image     [B, 3, 360, 640] fp32 in [-1, 1]; skip_decode != 0 stops after the steps */
+typedef struct OasisFrameArgs {
+  int batch;
+  int frames;
+  int steps;
+  float* chunk;
+  const float* context_z;
+  const float* cond;
+  const OasisDdimCoeffs* coeffs;
+  float* image;
+  int skip_decode;
+  void* workspace;
+  size_t workspace_bytes;
+} OasisFrameArgs;
+
+size_t oasis_frame_workspace_size(int batch, int frames, int steps);
+int oasis_generate_frame(const OasisDitWeights* w, const OasisVaeWeights* vw, const OasisFrameArgs* a,
+                         oasis_stream_t stream);
+
 /* ------------------------------------------------------------ op level --- */
 
 /* tcgen05 GEMM: acc = A[M,K] . W[N,K]^T (bf16 in, fp32 accumulate) + bias, then

@@ -82,6 +82,12 @@ class OasisVaeArgs(C.Structure):
                 ("workspace_bytes", C.c_size_t)]
 
 
+class OasisFrameArgs(C.Structure):
+    _fields_ = [("batch", C.c_int), ("frames", C.c_int), ("steps", C.c_int), ("chunk", fp), ("context_z", fp),
+                ("cond", fp), ("coeffs", C.POINTER(OasisDdimCoeffs)), ("image", fp), ("skip_decode", C.c_int),
+                ("workspace", vp), ("workspace_bytes", C.c_size_t)]
+
+
 class OasisGemmArgs(C.Structure):
     _fields_ = [("a", vp), ("lda", C.c_longlong), ("w", vp), ("m", C.c_int), ("n", C.c_int), ("k", C.c_int),
                 ("mode", C.c_int), ("out", vp), ("ldo", C.c_longlong), ("bias", fp), ("resid", fp),
@@ -112,6 +118,9 @@ SIGNATURES = {
     "oasis_bridge_unpatchify": (C.c_int, [fp, fp, C.c_int, vp]),
     "oasis_vae_workspace_size": (C.c_size_t, [C.c_int]),
     "oasis_vae_decode": (C.c_int, [C.POINTER(OasisVaeWeights), C.POINTER(OasisVaeArgs), vp]),
+    "oasis_frame_workspace_size": (C.c_size_t, [C.c_int, C.c_int, C.c_int]),
+    "oasis_generate_frame": (C.c_int, [C.POINTER(OasisDitWeights), C.POINTER(OasisVaeWeights),
+                                       C.POINTER(OasisFrameArgs), vp]),
     "oasis_gemm": (C.c_int, [C.POINTER(OasisGemmArgs), vp]),
     "oasis_gemm_workspace_size": (C.c_size_t, [C.c_int, C.c_int, C.c_int]),
     "oasis_gemm_static_scratch": (C.c_int, [C.POINTER(OasisGemmArgs), vp]),

@@ -89,11 +89,11 @@ struct DitScratch {
   size_t splitk_bytes;
 };
 
-size_t carve_dit(Carve& c, int B, int T, DitScratch* s) {
+size_t carve_dit(Carve& c, int B, int T, DitScratch* s, bool with_adaln = true) {
   const size_t F = (size_t)B * T, M = F * kP;
   DitScratch d;
-  d.silu = c.take<__nv_bfloat16>(F * kD);
-  d.adaln = c.take<float>(F * OASIS_ADALN_ROWS);
+  d.silu = with_adaln ? c.take<__nv_bfloat16>(F * kD) : nullptr;
+  d.adaln = with_adaln ? c.take<float>(F * OASIS_ADALN_ROWS) : nullptr;
   d.xn = c.take<__nv_bfloat16>(M * kD);
   d.qkv = c.take<__nv_bfloat16>(M * 3 * kD);
   d.attn = c.take<__nv_bfloat16>(M * kD);
@@ -117,32 +117,28 @@ GemmProblem gemm(const void* A, const void* W, int M, int N, int K, void* ws, si
   return p;
 }
 
-int dit_forward_impl(const OasisDitWeights* w, const OasisDitArgs* a, cudaStream_t st) {
-  OASIS_REQUIRE(w && a, "dit_forward: null argument");
-  const int B = a->batch, T = a->frames;
-  OASIS_REQUIRE(B > 0 && T > 0 && T <= 32, "dit_forward: batch=%d frames=%d (need frames in [1, 32])", B, T);
-  OASIS_REQUIRE(a->z && a->cond && a->v_out, "dit_forward: null tensor");
-  Carve c(a->workspace, a->workspace_bytes);
-  DitScratch s;
-  carve_dit(c, B, T, &s);
-  if (!a->workspace || !c.ok())
-    return set_error(OASIS_ERR_WORKSPACE, "dit_forward: workspace %zu bytes < %zu", a->workspace_bytes, c.used);
+// adaLN parameters of every sub-block and the final layer for `rows` frames:
+// silu(cond) then ONE GEMM against the stacked adaLN weights.
+int compute_adaln(const OasisDitWeights* w, const float* cond, int rows, __nv_bfloat16* silu, float* adaln,
+                  void* splitk, size_t splitk_bytes, cudaStream_t st) {
+  const long long ldm = (long long)w->num_subblocks * OASIS_ADALN_WIDTH + 2 * kD;
+  OASIS_TRY(silu_bf16_launch(cond, silu, (long long)rows * kD, st));
+  GemmProblem p = gemm(silu, w->adaln_w, rows, (int)ldm, kD, splitk, splitk_bytes);
+  p.epi.mode = kEpiF32;
+  p.epi.out = adaln;
+  p.epi.ldo = ldm;
+  p.epi.bias = w->adaln_b;
+  return gemm_launch(p, st);
+}
+
+// The 32 sub-blocks and the final layer for B sessions x T frames, given the
+// adaLN table [B T, ldm] of this step.
+int dit_blocks(const OasisDitWeights* w, int B, int T, float* z, const float* adaln, float* v_out,
+               int last_frame_only, const DitScratch& s, cudaStream_t st) {
   const int F = B * T, M = F * kP;
   const int nsub = w->num_subblocks;
-  OASIS_REQUIRE(nsub >= 0 && nsub <= OASIS_DIT_SUBBLOCKS, "dit_forward: num_subblocks=%d", nsub);
   const long long ldm = (long long)nsub * OASIS_ADALN_WIDTH + 2 * kD;
-
-  // adaLN parameters of every sub-block and the final layer, all frames, one GEMM.
-  OASIS_TRY(silu_bf16_launch(a->cond, s.silu, (long long)F * kD, st));
-  {
-    GemmProblem p = gemm(s.silu, w->adaln_w, F, (int)ldm, kD, s.splitk, s.splitk_bytes);
-    p.epi.mode = kEpiF32;
-    p.epi.out = s.adaln;
-    p.epi.ldo = ldm;
-    p.epi.bias = w->adaln_b;
-    OASIS_TRY(gemm_launch(p, st));
-  }
-
+  float* const ad = const_cast<float*>(adaln);
   for (int i = 0; i < nsub; ++i) {
     const OasisDitSubBlock& sb = w->sub[i];
     const bool spatial = (i % 2) == 0;
@@ -151,11 +147,11 @@ int dit_forward_impl(const OasisDitWeights* w, const OasisDitArgs* a, cudaStream
     ln.rows_out = M;
     ln.P = kP;
     ln.in_group = kP;
-    ln.mod = s.adaln;
+    ln.mod = ad;
     ln.ld_mod = ldm;
     ln.shift_off = off;
     ln.scale_off = off + kD;
-    OASIS_TRY(layernorm_launch(a->z, s.xn, ln, st));
+    OASIS_TRY(layernorm_launch(z, s.xn, ln, st));
     {
       GemmProblem p = gemm(s.xn, sb.qkv_w, M, 3 * kD, kD, s.splitk, s.splitk_bytes);
       p.epi.mode = kEpiRopeBF16;
@@ -173,19 +169,19 @@ int dit_forward_impl(const OasisDitWeights* w, const OasisDitArgs* a, cudaStream
     {
       GemmProblem p = gemm(s.attn, sb.out_w, M, kD, kD, s.splitk, s.splitk_bytes);
       p.epi.mode = kEpiGatedResid;
-      p.epi.out = a->z;
+      p.epi.out = z;
       p.epi.ldo = kD;
-      p.epi.resid = a->z;
+      p.epi.resid = z;
       p.epi.ldr = kD;
       p.epi.bias = sb.out_b;
-      p.epi.gate = s.adaln + off + 2 * kD;
+      p.epi.gate = ad + off + 2 * kD;
       p.epi.ldg = ldm;
       p.epi.rows_per_frame = kP;
       OASIS_TRY(gemm_launch(p, st));
     }
     ln.shift_off = off + 3 * kD;
     ln.scale_off = off + 4 * kD;
-    OASIS_TRY(layernorm_launch(a->z, s.xn, ln, st));
+    OASIS_TRY(layernorm_launch(z, s.xn, ln, st));
     {
       GemmProblem p = gemm(s.xn, sb.fc1_w, M, kMlp, kD, s.splitk, s.splitk_bytes);
       p.epi.mode = kEpiGeluTanhBF16;
@@ -197,12 +193,12 @@ int dit_forward_impl(const OasisDitWeights* w, const OasisDitArgs* a, cudaStream
     {
       GemmProblem p = gemm(s.h, sb.fc2_w, M, kD, kMlp, s.splitk, s.splitk_bytes);
       p.epi.mode = kEpiGatedResid;
-      p.epi.out = a->z;
+      p.epi.out = z;
       p.epi.ldo = kD;
-      p.epi.resid = a->z;
+      p.epi.resid = z;
       p.epi.ldr = kD;
       p.epi.bias = sb.fc2_b;
-      p.epi.gate = s.adaln + off + 5 * kD;
+      p.epi.gate = ad + off + 5 * kD;
       p.epi.ldg = ldm;
       p.epi.rows_per_frame = kP;
       OASIS_TRY(gemm_launch(p, st));
@@ -213,11 +209,11 @@ int dit_forward_impl(const OasisDitWeights* w, const OasisDitArgs* a, cudaStream
   const long long foff = (long long)nsub * OASIS_ADALN_WIDTH;
   LayerNormParams ln;
   ln.P = kP;
-  ln.mod = s.adaln;
+  ln.mod = ad;
   ln.ld_mod = ldm;
   ln.shift_off = foff;
   ln.scale_off = foff + kD;
-  if (a->last_frame_only) {
+  if (last_frame_only) {
     ln.rows_out = B * kP;
     ln.in_group = (long long)T * kP;
     ln.in_off = (long long)(T - 1) * kP;
@@ -227,13 +223,29 @@ int dit_forward_impl(const OasisDitWeights* w, const OasisDitArgs* a, cudaStream
     ln.rows_out = M;
     ln.in_group = kP;
   }
-  OASIS_TRY(layernorm_launch(a->z, s.xn, ln, st));
+  OASIS_TRY(layernorm_launch(z, s.xn, ln, st));
   GemmProblem p = gemm(s.xn, w->final_w, ln.rows_out, kOut, kD, s.splitk, s.splitk_bytes);
   p.epi.mode = kEpiF32;
-  p.epi.out = a->v_out;
+  p.epi.out = v_out;
   p.epi.ldo = kOut;
   p.epi.bias = w->final_b;
   return gemm_launch(p, st);
+}
+
+int dit_forward_impl(const OasisDitWeights* w, const OasisDitArgs* a, cudaStream_t st) {
+  OASIS_REQUIRE(w && a, "dit_forward: null argument");
+  const int B = a->batch, T = a->frames;
+  OASIS_REQUIRE(B > 0 && T > 0 && T <= 32, "dit_forward: batch=%d frames=%d (need frames in [1, 32])", B, T);
+  OASIS_REQUIRE(a->z && a->cond && a->v_out, "dit_forward: null tensor");
+  OASIS_REQUIRE(w->num_subblocks >= 0 && w->num_subblocks <= OASIS_DIT_SUBBLOCKS, "dit_forward: num_subblocks=%d",
+                w->num_subblocks);
+  Carve c(a->workspace, a->workspace_bytes);
+  DitScratch s;
+  carve_dit(c, B, T, &s);
+  if (!a->workspace || !c.ok())
+    return set_error(OASIS_ERR_WORKSPACE, "dit_forward: workspace %zu bytes < %zu", a->workspace_bytes, c.used);
+  OASIS_TRY(compute_adaln(w, a->cond, B * T, s.silu, s.adaln, s.splitk, s.splitk_bytes, st));
+  return dit_blocks(w, B, T, a->z, s.adaln, a->v_out, a->last_frame_only, s, st);
 }
 
 size_t step_ws(int B, int T, DitScratch* s, float** z, float** v, void* base, size_t cap) {
@@ -356,6 +368,82 @@ int vae_decode_impl(const OasisVaeWeights* w, const OasisVaeArgs* a, cudaStream_
   return gemm_launch(p, st);
 }
 
+
+constexpr int kMaxFrameSteps = 64;
+
+struct FrameScratch {
+  __nv_bfloat16* silu;  // [steps B T, 1024]
+  float* adaln;         // [steps B T, 6144 S + 2048]
+  float* z;             // [B T 144, 1024]
+  float* v;             // [B 144, 64]
+  float* latent;        // [B, 576, 16]
+  void* shared;         // DiT step scratch, later reused by the VAE decode
+  size_t shared_bytes;
+};
+
+size_t carve_frame(Carve& c, int B, int T, int S, FrameScratch* f) {
+  const size_t F = (size_t)B * T;
+  FrameScratch d;
+  d.silu = c.take<__nv_bfloat16>((size_t)S * F * kD);
+  d.adaln = c.take<float>((size_t)S * F * OASIS_ADALN_ROWS);
+  d.z = c.take<float>(F * kP * kD);
+  d.v = c.take<float>((size_t)B * kP * kOut);
+  d.latent = c.take<float>((size_t)B * kVaeTok * 16);
+  Carve dit(nullptr, 0), vae(nullptr, 0);
+  carve_dit(dit, B, T, nullptr, false);
+  carve_vae(vae, B, nullptr);
+  d.shared_bytes = (dit.used > vae.used ? dit.used : vae.used) + 256;
+  d.shared = c.take<uint8_t>(d.shared_bytes);
+  if (f) *f = d;
+  return c.used;
+}
+
+int generate_frame_impl(const OasisDitWeights* w, const OasisVaeWeights* vw, const OasisFrameArgs* a,
+                        cudaStream_t st) {
+  OASIS_REQUIRE(w && a, "generate_frame: null argument");
+  const int B = a->batch, T = a->frames, S = a->steps;
+  OASIS_REQUIRE(B > 0 && T > 0 && T <= 32, "generate_frame: batch=%d frames=%d", B, T);
+  OASIS_REQUIRE(S > 0 && S <= kMaxFrameSteps, "generate_frame: steps=%d outside [1, %d]", S, kMaxFrameSteps);
+  OASIS_REQUIRE(a->chunk && a->cond && a->coeffs, "generate_frame: null tensor");
+  OASIS_REQUIRE(T == 1 || a->context_z, "generate_frame: frames > 1 needs context_z");
+  OASIS_REQUIRE(a->skip_decode || (vw && a->image), "generate_frame: decoding needs VAE weights and an image");
+  OASIS_REQUIRE(w->num_subblocks >= 0 && w->num_subblocks <= OASIS_DIT_SUBBLOCKS, "generate_frame: num_subblocks");
+  Carve c(a->workspace, a->workspace_bytes);
+  FrameScratch f;
+  carve_frame(c, B, T, S, &f);
+  if (!a->workspace || !c.ok())
+    return set_error(OASIS_ERR_WORKSPACE, "generate_frame: workspace %zu bytes < %zu", a->workspace_bytes, c.used);
+  Carve dc(f.shared, f.shared_bytes);
+  DitScratch s;
+  carve_dit(dc, B, T, &s, false);
+  const int F = B * T;
+  const long long ldm = (long long)w->num_subblocks * OASIS_ADALN_WIDTH + 2 * kD;
+  // adaLN tables of all steps at once: the stacked weights stream from HBM once per frame.
+  OASIS_TRY(compute_adaln(w, a->cond, S * F, f.silu, f.adaln, s.splitk, s.splitk_bytes, st));
+  for (int i = 0; i < S; ++i) {
+    if (T > 1) {
+      const size_t ctx_bytes = (size_t)(T - 1) * kP * kD * sizeof(float);
+      cudaError_t e = cudaMemcpy2DAsync(f.z, (size_t)T * kP * kD * sizeof(float), a->context_z, ctx_bytes,
+                                        ctx_bytes, B, cudaMemcpyDeviceToDevice, st);
+      if (e != cudaSuccess) return set_error(OASIS_ERR_CUDA, "generate_frame: context copy: %s", cudaGetErrorString(e));
+    }
+    PatchEmbedParams pe;
+    pe.rows = B * kP;
+    pe.P = kP;
+    pe.out_group = (long long)T * kP;
+    pe.out_off = (long long)(T - 1) * kP;
+    OASIS_TRY(patch_embed_launch(a->chunk, w->embed_w, w->embed_b, f.z, pe, st));
+    OASIS_TRY(dit_blocks(w, B, T, f.z, f.adaln + (size_t)i * F * ldm, f.v, 1, s, st));
+    const OasisDdimCoeffs& k = a->coeffs[i];
+    DdimCoeffs dk{k.at_sqrt, k.one_minus_at_sqrt, k.inv_at_sqrt, k.inv_sigma, k.an_sqrt, k.one_minus_an_sqrt};
+    OASIS_TRY(ddim_launch(a->chunk, f.v, dk, (long long)B * kP * kOut, st));
+  }
+  if (a->skip_decode) return OASIS_OK;
+  OASIS_TRY(bridge_launch(a->chunk, f.latent, B, 1.0f / kScalingFactor, st));
+  OasisVaeArgs va{B, f.latent, a->image, f.shared, f.shared_bytes};
+  return vae_decode_impl(vw, &va, st);
+}
+
 }  // namespace
 }  // namespace oasis
 
@@ -446,6 +534,17 @@ size_t oasis_vae_workspace_size(int batch) {
 int oasis_vae_decode(const OasisVaeWeights* w, const OasisVaeArgs* a, oasis_stream_t stream) {
   g_msg[0] = 0;
   return vae_decode_impl(w, a, S(stream));
+}
+
+size_t oasis_frame_workspace_size(int batch, int frames, int steps) {
+  Carve c(nullptr, 0);
+  return carve_frame(c, batch, frames, steps, nullptr) + 256;
+}
+
+int oasis_generate_frame(const OasisDitWeights* w, const OasisVaeWeights* vw, const OasisFrameArgs* a,
+                         oasis_stream_t stream) {
+  g_msg[0] = 0;
+  return generate_frame_impl(w, vw, a, S(stream));
 }
 
 int oasis_gemm(const OasisGemmArgs* a, oasis_stream_t stream) {

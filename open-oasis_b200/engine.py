@@ -127,10 +127,40 @@ def vae_decode(vw: VaeDeviceWeights, latent: torch.Tensor, image: torch.Tensor, 
     return image
 
 
+def frame_workspace_bytes(batch: int, frames: int, steps: int) -> int:
+    return int(_lib.load().oasis_frame_workspace_size(batch, frames, steps))
+
+
+def generate_frame(dw: DitDeviceWeights, vw: VaeDeviceWeights | None, chunk: torch.Tensor,
+                   context_z: torch.Tensor | None, cond: torch.Tensor, steps: list[H.DdimStep],
+                   image: torch.Tensor | None, ws: torch.Tensor, skip_decode: bool = False, stream=None):
+    """One frame for B sessions: len(steps) DDIM steps (chunk updated in place),
+    then bridge + VAE decode into image [B, 3, 360, 640] unless skip_decode."""
+    _check_cuda(chunk, "chunk")
+    _check_cuda(cond, "cond")
+    S, B, T = cond.shape[0], cond.shape[1], cond.shape[2]
+    if S != len(steps) or tuple(chunk.shape) != (B, H.N_PATCHES, H.OUT_DIM):
+        raise ValueError("cond must be [steps, B, T, 1024] and chunk [B, 144, 64]")
+    if context_z is not None:
+        _check_cuda(context_z, "context_z")
+        if tuple(context_z.shape) != (B, T - 1, H.N_PATCHES, H.D_MODEL):
+            raise ValueError(f"context_z must be {(B, T - 1, H.N_PATCHES, H.D_MODEL)}")
+    if not skip_decode:
+        _check_cuda(image, "image")
+    coeffs = (_lib.OasisDdimCoeffs * S)(*[_lib.OasisDdimCoeffs(*st.as_tuple()) for st in steps])
+    a = _lib.OasisFrameArgs(B, T, S, chunk.data_ptr(), 0 if context_z is None else context_z.data_ptr(),
+                            cond.data_ptr(), coeffs, 0 if image is None else image.data_ptr(), int(skip_decode),
+                            ws.data_ptr(), ws.numel())
+    _lib.call("oasis_generate_frame", dw.ref(), None if vw is None else vw.ref(), C.byref(a), _stream(stream))
+    return chunk
+
+
 class FrameEngine:
     """All device buffers of one generated frame for B sessions with T-frame
-    context windows, and the launch sequence: 4 DDIM steps (patch embed -> DiT ->
-    DDIM update), bridge, VAE decode. `capture()` records it as a CUDA graph."""
+    context windows. `run()` issues the whole frame through oasis_generate_frame
+    (4 DDIM steps with all adaLN tables from one GEMM, bridge, VAE decode);
+    `capture()` records it (and, for timing breakdowns, the steps alone and the
+    decode alone) as CUDA graphs."""
 
     def __init__(self, dw: DitDeviceWeights, vw: VaeDeviceWeights, batch: int, frames: int,
                  steps: list[H.DdimStep] | None = None):
@@ -144,40 +174,56 @@ class FrameEngine:
         self.cond = torch.zeros(len(self.steps), B, T, H.D_MODEL, device=dev)
         self.latent = torch.zeros(B, H.VAE_TOKENS, H.VAE_LATENT, device=dev)
         self.image = torch.zeros(B, 3, H.VAE_H * H.VAE_PATCH, H.VAE_W * H.VAE_PATCH, device=dev)
-        self.step_ws = workspace(step_workspace_bytes(B, T), dev)
-        self.vae_ws = workspace(vae_workspace_bytes(B), dev)
+        self.frame_ws = workspace(frame_workspace_bytes(B, T, len(self.steps)), dev)
+        self.step_ws = None
+        self.vae_ws = None
         self.graph = None
 
+    def _ctx(self):
+        return self.context_z if self.T > 1 else None
+
+    def run(self, stream=None):
+        generate_frame(self.dw, self.vw, self.chunk, self._ctx(), self.cond, self.steps, self.image, self.frame_ws,
+                       stream=stream)
+
     def run_steps(self, stream=None):
-        ctx = self.context_z if self.T > 1 else None
-        for i, st in enumerate(self.steps):
-            ddim_step(self.dw, self.chunk, ctx, self.cond[i], st, self.step_ws, stream)
+        generate_frame(self.dw, None, self.chunk, self._ctx(), self.cond, self.steps, None, self.frame_ws,
+                       skip_decode=True, stream=stream)
 
     def run_decode(self, stream=None):
+        if self.vae_ws is None:
+            self.vae_ws = workspace(vae_workspace_bytes(self.B), self.dw.device)
         bridge_unpatchify(self.chunk, self.latent, stream)
         vae_decode(self.vw, self.latent, self.image, self.vae_ws, stream)
 
-    def run(self, stream=None):
-        self.run_steps(stream)
-        self.run_decode(stream)
+    def run_steps_separately(self, stream=None):
+        """The same steps through oasis_ddim_step (adaLN per step)."""
+        if self.step_ws is None:
+            self.step_ws = workspace(step_workspace_bytes(self.B, self.T), self.dw.device)
+        for i, st in enumerate(self.steps):
+            ddim_step(self.dw, self.chunk, self._ctx(), self.cond[i], st, self.step_ws, stream)
 
-    def capture(self):
-        """Captures the frame as two CUDA graphs (DDIM steps; bridge + VAE decode)
-        with the launch sequence and pointers fixed. Eagerly runs the frame once
-        first (kernel attributes, driver entry point), which modifies `chunk`."""
+    def capture(self, breakdown: bool = False):
+        """Captures the frame as a CUDA graph (launch sequence and pointers fixed);
+        with breakdown=True also the steps alone and the decode alone. Runs the
+        frame eagerly once first, which modifies `chunk`."""
         self.run()
-        torch.cuda.synchronize()
-        self.graph_steps = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.graph_steps):
-            self.run_steps()
-        self.graph_decode = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.graph_decode):
+        if breakdown:
             self.run_decode()
-        self.graph = (self.graph_steps, self.graph_decode)
+        torch.cuda.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.run()
+        if breakdown:
+            self.graph_steps = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph_steps):
+                self.run_steps()
+            self.graph_decode = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph_decode):
+                self.run_decode()
         return self.graph
 
     def replay(self):
         if self.graph is None:
             raise RuntimeError("capture() first")
-        self.graph_steps.replay()
-        self.graph_decode.replay()
+        self.graph.replay()

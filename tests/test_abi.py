@@ -33,7 +33,7 @@ def test_library_exports_every_declared_symbol():
 
 
 STRUCTS = ["OasisDitSubBlock", "OasisDitWeights", "OasisVaeBlock", "OasisVaeWeights", "OasisDitArgs",
-           "OasisDdimCoeffs", "OasisStepArgs", "OasisVaeArgs", "OasisGemmArgs", "OasisLayerNormArgs"]
+           "OasisDdimCoeffs", "OasisStepArgs", "OasisFrameArgs", "OasisVaeArgs", "OasisGemmArgs", "OasisLayerNormArgs"]
 
 
 def test_ctypes_layouts_match_c():

@@ -107,9 +107,10 @@ def test_frame_c3(dit_full, vae_full):
     for i, c in enumerate(conds):
         fe.cond[i].copy_(c)
     c_ref = chunk.clone()
+    step_ws = E.workspace(E.step_workspace_bytes(B, T), DEV)
     for i, st in enumerate(steps):
         c_ref, v_ref = O.ddim_step(c_ref, ctx_z, conds[i], st.at_sqrt ** 2, st.an_sqrt ** 2, dsd)
-        E.ddim_step(dw, fe.chunk, fe.context_z, fe.cond[i], st, fe.step_ws)
+        E.ddim_step(dw, fe.chunk, fe.context_z, fe.cond[i], st, step_ws)
         torch.cuda.synchronize()
         assert rel_l2(fe.chunk, c_ref) < REL_L2_TOL, (i, rel_l2(fe.chunk, c_ref))
     img_ref = O.vae_decode(O.bridge(c_ref), vsd)
@@ -152,3 +153,32 @@ def test_graft_smoke():
     import __graft_entry__
 
     __graft_entry__.smoke()
+
+
+def test_generate_frame_matches_per_step_path(dit_full, vae_full):
+    """oasis_generate_frame (all adaLN tables from one GEMM) equals the frame built
+    from oasis_ddim_step calls + bridge + decode, and the oracle."""
+    dsd, dw = dit_full
+    vsd, vw = vae_full
+    B, T = 2, 3
+    chunk, ctx_z, conds, steps = _frame_inputs(dsd, B, T, seed=4)
+    fe = E.FrameEngine(dw, vw, B, T, steps)
+    fe.context_z.copy_(ctx_z)
+    for i, c in enumerate(conds):
+        fe.cond[i].copy_(c)
+    fe.chunk.copy_(chunk)
+    fe.run()
+    torch.cuda.synchronize()
+    frame_chunk, frame_img = fe.chunk.clone(), fe.image.clone()
+    fe.chunk.copy_(chunk)
+    fe.run_steps_separately()
+    fe.run_decode()
+    torch.cuda.synchronize()
+    assert rel_l2(frame_chunk, fe.chunk) < 1e-5
+    assert rel_l2(frame_img, fe.image) < 1e-5
+    c_ref = chunk.clone()
+    for i, st in enumerate(steps):
+        c_ref, _ = O.ddim_step(c_ref, ctx_z, conds[i], st.at_sqrt ** 2, st.an_sqrt ** 2, dsd)
+    img_ref = O.vae_decode(O.bridge(c_ref), vsd)
+    assert rel_l2(frame_chunk, c_ref) < REL_L2_TOL
+    assert rel_l2(frame_img, img_ref) < REL_L2_TOL and cosine(frame_img, img_ref) > COS_TOL
