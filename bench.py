@@ -39,10 +39,11 @@ SESSIONS = 64
 FRAMES_T = 8
 METRIC = "frames_per_sec (4 DDIM steps + VAE decode per frame, 64 sessions)"
 UNIT = "frames/s"
-# DRAM traffic of one FC1 gemm_kernel launch at the bench shape (M=73728, N=4096,
-# K=1024), from the ncu capture summarised in profiles/gemm_kernel_fc1.md
-# (smaller case scaled by rows); None until that capture exists.
-GEMM_TRAFFIC_BYTES_PER_LAUNCH = None
+# DRAM traffic (read + write during the launch) of one FC1 gemm_kernel launch at
+# the bench shape (M=73728, N=4096, K=1024): the ncu capture at M=16384 in
+# profiles/gemm_kernel_fc1.md (42.0 MB read, 79.0 MB written) scaled by rows for
+# the M-proportional parts (A, output); W (8.4 MB) is read once either way.
+GEMM_TRAFFIC_BYTES_PER_LAUNCH = int((42.04e6 - 8.39e6) * 4.5 + 8.39e6 + 78.99e6 * 4.5)
 
 
 def parse():
@@ -271,12 +272,14 @@ def gemm_roofline(M, reps, peaks):
         per[name] = {"ms": round(ms, 4), "tflops": round(f / ms / 1e9, 1)}
         total_f += f
         total_ms += ms
-    achieved = total_f / total_ms / 1e9  # TFLOP/s
+    achieved = 2.0 * M * 4096 * 1024 / per["fc1"]["ms"] / 1e9  # TFLOP/s of the FC1 launch
     del a, w, out, resid
     return {"bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
             "frac": round(achieved / peaks["bf16_tflops"], 3), "traffic": GEMM_TRAFFIC_BYTES_PER_LAUNCH,
-            "kernel": "gemm_kernel (tcgen05, DiT QKV/O/FC1/FC2 at the bench M, FLOP-weighted)",
-            "peak_source": f"bf16_tflops (burst) of {peaks['source']}", "per_shape": per, "M": M}
+            "kernel": f"gemm_kernel<256> FC1+GELU launch, M={M} N=4096 K=1024 (2MNK FLOP / CUDA-event time, "
+                      "avg of 10 launches)",
+            "peak_source": f"bf16_tflops (burst, kernel timed alone) of {peaks['source']}",
+            "all_dit_shapes_tflops": round(total_f / total_ms / 1e9, 1), "per_shape": per, "M": M}
 
 
 def latency_extras(dw, vw, peaks):
