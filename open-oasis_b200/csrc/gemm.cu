@@ -76,7 +76,7 @@ __device__ __forceinline__ void load_resid(const EpiParams& e, int r, int nb, in
 
 // Applies the epilogue to 32 consecutive accumulator columns [nb, nb + 32) of row r, in place.
 __device__ __forceinline__ void epilogue_math(const EpiParams& e, int r, int nb, float (&v)[32],
-                                              const float4 (&res)[8]) {
+                                              const float4 (&res)[8], const float4* gpre = nullptr) {
   if (e.bias) {
 #pragma unroll
     for (int i = 0; i < 32; i += 4) {
@@ -115,7 +115,7 @@ __device__ __forceinline__ void epilogue_math(const EpiParams& e, int r, int nb,
         const float4* g = reinterpret_cast<const float4*>(e.gate + (long long)(r / e.rows_per_frame) * e.ldg + nb);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const float4 gg = __ldg(g + i);
+          const float4 gg = gpre ? gpre[i] : __ldg(g + i);
           v[4 * i] *= gg.x; v[4 * i + 1] *= gg.y; v[4 * i + 2] *= gg.z; v[4 * i + 3] *= gg.w;
         }
       }
@@ -283,6 +283,12 @@ __device__ __forceinline__ void epilogue_tile_resid(const EpiParams& e, const CU
     const int c = half + 2 * i;
     const int nb = n0 + c * 32;
     uint8_t* buf = stg + b * kStgBytes;
+    float4 gate[8];  // issued before the waits so its latency overlaps them
+    if (e.mode == kEpiGatedResid) {
+      const float4* g = reinterpret_cast<const float4*>(e.gate + (long long)((r < M ? r : M - 1) / e.rows_per_frame) * e.ldg + nb);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) gate[j] = __ldg(g + j);
+    }
     if (!mbar_wait(&rbar[b], (rphase >> b) & 1, kDevTimeoutAccFull)) {
       ok = false;
       return;
@@ -295,7 +301,7 @@ __device__ __forceinline__ void epilogue_tile_resid(const EpiParams& e, const CU
     float4 res[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) res[j] = *reinterpret_cast<const float4*>(row + ((j ^ (lane & 7)) << 4));
-    epilogue_math(e, r, nb, v, res);
+    epilogue_math(e, r, nb, v, res, e.mode == kEpiGatedResid ? gate : nullptr);
     stage_write(buf, lane, false, 0, v);
     stage_commit(tm_out, buf, lane, m0q, nb);
     if (i + 2 < mine) {  // refill this buffer with chunk i + 2 once the store has read it

@@ -31,26 +31,6 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict_
   const long long in_row = (long long)grp * p.in_group + p.in_off + within;
   const float* xr = x + in_row * D;
 
-  float4 v[8];
-  float s = 0.f;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    v[j] = reinterpret_cast<const float4*>(xr)[lane + 32 * j];
-    s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  const float mean = s * (1.f / D);
-  float q = 0.f;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const float a = v[j].x - mean, b = v[j].y - mean, c = v[j].z - mean, d = v[j].w - mean;
-    q += (a * a + b * b) + (c * c + d * d);
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
-  const float rstd = rsqrtf(q * (1.f / D) + p.eps);
-
   const float* mul;
   const float* add;
   if (p.affine_w) {
@@ -61,16 +41,40 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict_
     mul = p.mod + frame * p.ld_mod + p.scale_off;
     add = p.mod + frame * p.ld_mod + p.shift_off;
   }
+  float4 v[8], m[8], a[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) v[j] = reinterpret_cast<const float4*>(xr)[lane + 32 * j];
+  // the modulation (or affine) vectors do not depend on the row statistics:
+  // fetch them now so their latency overlaps the reduction
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int c = 4 * (lane + 32 * j);
+    m[j] = __ldg(reinterpret_cast<const float4*>(mul + c));
+    a[j] = add ? __ldg(reinterpret_cast<const float4*>(add + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float mean = s * (1.f / D);
+  float q = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float a0 = v[j].x - mean, b0 = v[j].y - mean, c0 = v[j].z - mean, d0 = v[j].w - mean;
+    q += (a0 * a0 + b0 * b0) + (c0 * c0 + d0 * d0);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+  const float rstd = rsqrtf(q * (1.f / D) + p.eps);
   __nv_bfloat16* yr = y + (long long)r * D;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const int c = 4 * (lane + 32 * j);
-    const float4 m = *reinterpret_cast<const float4*>(mul + c);
-    const float4 a = add ? *reinterpret_cast<const float4*>(add + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-    const float o0 = (v[j].x - mean) * rstd * m.x + a.x;
-    const float o1 = (v[j].y - mean) * rstd * m.y + a.y;
-    const float o2 = (v[j].z - mean) * rstd * m.z + a.z;
-    const float o3 = (v[j].w - mean) * rstd * m.w + a.w;
+    const float o0 = (v[j].x - mean) * rstd * m[j].x + a[j].x;
+    const float o1 = (v[j].y - mean) * rstd * m[j].y + a[j].y;
+    const float o2 = (v[j].z - mean) * rstd * m[j].z + a[j].z;
+    const float o3 = (v[j].w - mean) * rstd * m[j].w + a[j].w;
     *reinterpret_cast<uint2*>(yr + c) = make_uint2(pack_bf16x2(o0, o1), pack_bf16x2(o2, o3));
   }
 }

@@ -46,23 +46,23 @@ def gemm(a):
     args.block_n, args.splits = a.block_n, a.splits
     ws = torch.empty(max(_lib.load().oasis_gemm_workspace_size(M, N, K), 256), dtype=torch.uint8, device="cuda")
     args.workspace, args.workspace_bytes = ws.data_ptr(), ws.numel()
-    for _ in range(a.reps):
-        _lib.call("oasis_gemm", C.byref(args), _st())
+    a._keep = (A, W, out, bias, gate, rope, ws, args)
+    return lambda: _lib.call("oasis_gemm", C.byref(args), _st())
 
 
 def attn_spatial(a):
     qkv = torch.randn(a.groups * a.seq, 3072, device="cuda").to(torch.bfloat16)
     out = torch.empty(a.groups * a.seq, 1024, device="cuda", dtype=torch.bfloat16)
-    for _ in range(a.reps):
-        _lib.call("oasis_attention_spatial", qkv.data_ptr(), out.data_ptr(), a.groups, a.seq, _st())
+    a._keep = (qkv, out)
+    return lambda: _lib.call("oasis_attention_spatial", qkv.data_ptr(), out.data_ptr(), a.groups, a.seq, _st())
 
 
 def attn_temporal(a):
     rows = a.batch * a.frames * 144
     qkv = torch.randn(rows, 3072, device="cuda").to(torch.bfloat16)
     out = torch.empty(rows, 1024, device="cuda", dtype=torch.bfloat16)
-    for _ in range(a.reps):
-        _lib.call("oasis_attention_temporal", qkv.data_ptr(), out.data_ptr(), a.batch, a.frames, _st())
+    a._keep = (qkv, out)
+    return lambda: _lib.call("oasis_attention_temporal", qkv.data_ptr(), out.data_ptr(), a.batch, a.frames, _st())
 
 
 def layernorm(a):
@@ -73,8 +73,8 @@ def layernorm(a):
     args = _lib.OasisLayerNormArgs()
     args.x, args.y, args.rows_out, args.P, args.in_group = x.data_ptr(), y.data_ptr(), a.rows, 144, 144
     args.frame_mul, args.eps, args.mod, args.ld_mod, args.shift_off, args.scale_off = 1, 1e-6, mod.data_ptr(), 2048, 0, 1024
-    for _ in range(a.reps):
-        _lib.call("oasis_layernorm", C.byref(args), _st())
+    a._keep = (x, y, mod, args)
+    return lambda: _lib.call("oasis_layernorm", C.byref(args), _st())
 
 
 def main():
@@ -92,8 +92,23 @@ def main():
     ap.add_argument("--frames", type=int, default=8)
     ap.add_argument("--rows", type=int, default=73728)
     ap.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--time", action="store_true", help="print the mean time per launch (CUDA events)")
     a = ap.parse_args()
-    globals()[a.case](a)
+    launch = globals()[a.case](a)
+    if a.time:
+        for _ in range(3):
+            launch()
+        torch.cuda.synchronize()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        ev[0].record()
+        for _ in range(a.reps):
+            launch()
+        ev[1].record()
+        ev[1].synchronize()
+        print(f"{a.case}: {ev[0].elapsed_time(ev[1]) * 1000 / a.reps:.2f} us per launch")
+    else:
+        for _ in range(a.reps):
+            launch()
     torch.cuda.synchronize()
     err = _lib.load().oasis_device_error(0)
     if err:
