@@ -58,22 +58,6 @@ def parse():
     return ap.parse_args()
 
 
-def dist_setup():
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world > 1 and not dist.is_initialized():
-        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        if torch.cuda.is_available():
-            torch.cuda.set_device(local)
-            dist.init_process_group("nccl", device_id=torch.device("cuda", local))
-        else:
-            dist.init_process_group("gloo")
-    elif torch.cuda.is_available():
-        torch.cuda.set_device(local)
-    return rank, world, local
-
-
 def measured_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -310,7 +294,9 @@ def latency_extras(dw, vw, peaks):
 
 def main():
     args = parse()
-    rank, world, local = dist_setup()
+    from oasis_b200 import parallel as PAR
+
+    rank, world, local = PAR.init_from_env()
     if args.impl == "reference":
         run_reference(args, rank, world)
         if dist.is_initialized():
@@ -322,13 +308,14 @@ def main():
 
     if args.sessions % world:
         raise SystemExit(f"--sessions {args.sessions} not divisible by {world} GPUs")
-    B, T = args.sessions // world, args.frames
+    sess0, B = PAR.shard_sessions(args.sessions, world, rank)
+    T = args.frames
     dev = torch.device("cuda", local)
     peaks = measured_peaks()
     dw = DitDeviceWeights(init_dit_weights(seed=0), dev)
     vw = VaeDeviceWeights(init_vae_weights(seed=0), dev)
     fe = E.FrameEngine(dw, vw, B, T)
-    chunk0, ctx0, conds0 = make_inputs(fe, dw, rank * B, B, T)
+    chunk0, ctx0, conds0 = make_inputs(fe, dw, sess0, B, T)
     n0 = _lib.load().oasis_launch_count()
     fe.capture()
     launches_per_frame = (_lib.load().oasis_launch_count() - n0) // 2  # eager frame + captured frame
@@ -341,11 +328,7 @@ def main():
         frame()
     torch.cuda.synchronize()
 
-    def barrier():
-        if dist.is_initialized():
-            dist.barrier()
-        torch.cuda.synchronize()
-
+    barrier = PAR.barrier
     clocks = ClockSampler(local) if rank == 0 else None
     barrier()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
@@ -356,10 +339,7 @@ def main():
     barrier()
     ms = ev[0].elapsed_time(ev[1])
     clk = clocks.stop() if clocks else None
-    t = torch.tensor([ms], device=dev)
-    if dist.is_initialized():
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+    ms_max = PAR.max_over_ranks(ms)
     value = args.sessions * args.steps / (ms_max / 1000.0)
 
     # split: DiT steps vs decode (device time, this rank)
@@ -387,10 +367,7 @@ def main():
         e2e_frame()
     ev[2].record()
     barrier()
-    t = torch.tensor([ev[0].elapsed_time(ev[2])], device=dev)
-    if dist.is_initialized():
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_value = args.sessions * args.steps / (float(t.item()) / 1000.0)
+    e2e_value = args.sessions * args.steps / (PAR.max_over_ranks(ev[0].elapsed_time(ev[2])) / 1000.0)
 
     roof = gemm_roofline(B * T * 144, 10, peaks)
     extras, cpu = {}, None
