@@ -228,7 +228,7 @@ int oasis_generate_frame(const OasisDitWeights* w, const OasisVaeWeights* vw, co
  *   3 GELU_ERF     out_bf16 = gelu_erf(acc)           (VAE FC1)
  *   4 GATED_RESID  out_f32 = resid + gate[r / rows_per_frame, n] * acc   (O / FC2)
  *   5 RESID        out_f32 = resid + acc              (VAE proj / FC2)
- *   6 ROPE         out_bf16 = acc with interleaved RoPE on columns [0, 2048)
+ *   6 ROPE         out_bf16 = acc with interleaved RoPE on columns [0, 2 rope_dim)
  *                  at position (r / rope_div) % rope_mod    (QKV + rope_layout)
  *   7 IMAGE        VAE predictor: scatter 20x20x3 patches into [frames, 3, 360, 640],
  *                  clamped to [-1, 1]
@@ -246,6 +246,7 @@ typedef struct OasisGemmArgs {
   int block_n; /* 0 = heuristic, else 64 / 128 / 256 */
   int splits;  /* 0 = heuristic, 1 = none */
   void* workspace; size_t workspace_bytes;
+  int rope_dim; /* ROPE: width of the q (and k) section; 0 = 1024 (16 heads) */
 } OasisGemmArgs;
 
 int oasis_gemm(const OasisGemmArgs* a, oasis_stream_t stream);
@@ -285,14 +286,22 @@ int oasis_layernorm(const OasisLayerNormArgs* a, oasis_stream_t stream);
 int oasis_silu_bf16(const float* x, void* y, long long n, oasis_stream_t stream);
 
 /* Spatial / VAE attention: non-causal within groups of `seq` rows of a packed
- * qkv [rows, 3072] bf16; out [rows, 1024] bf16. Replaces sdpa_spatial
- * (src/sdpa.py:27-113, but over exactly `seq` keys) and the VAE ttnn SDPA. */
-int oasis_attention_spatial(const void* qkv, void* out, int groups, int seq, oasis_stream_t stream);
+ * qkv [rows, 3 heads 64] bf16 (q | k | v); out [rows, heads 64] bf16; heads is 16
+ * for the full model, 16 / n on a rank of n-way tensor parallelism. Replaces
+ * sdpa_spatial (src/sdpa.py:27-113, but over exactly `seq` keys) and the VAE ttnn SDPA. */
+int oasis_attention_spatial(const void* qkv, void* out, int groups, int seq, int heads, oasis_stream_t stream);
 
 /* Causal temporal attention per (session, patch, head) over T frames; token row
  * of (b, t, p) = (b T + t) 144 + p. Replaces sdpa_temporal_causal
  * (src/sdpa_causal.py:17-100) and its block-diagonal packing. */
-int oasis_attention_temporal(const void* qkv, void* out, int batch, int frames, oasis_stream_t stream);
+int oasis_attention_temporal(const void* qkv, void* out, int batch, int frames, int heads, oasis_stream_t stream);
+
+/* z[r, :1024] += gate[(r / rows_per_frame) ldg + :] * (x[r, :] + bias), gate NULL =
+ * plain residual. Applies the bias, adaLN gate and residual after the all-reduce of a
+ * row-parallel projection (tensor parallelism: `ttnn.all_reduce` then `ttnn.add` and
+ * `ttnn.addcmul`, oasis_inference.py:1153-1165, 1191-1201). */
+int oasis_gated_residual(float* z, const float* x, const float* bias, const float* gate, long long ldg,
+                         int rows_per_frame, int rows, oasis_stream_t stream);
 
 /* VAE post_quant_conv as a linear map: z[r] = latent[r, :16] . w + b. */
 int oasis_post_quant(const float* latent, const float* w, const float* b, float* z, int rows,

@@ -93,7 +93,7 @@ class OasisGemmArgs(C.Structure):
                 ("mode", C.c_int), ("out", vp), ("ldo", C.c_longlong), ("bias", fp), ("resid", fp),
                 ("ldr", C.c_longlong), ("gate", fp), ("ldg", C.c_longlong), ("rows_per_frame", C.c_int),
                 ("rope", fp), ("rope_div", C.c_int), ("rope_mod", C.c_int), ("block_n", C.c_int),
-                ("splits", C.c_int), ("workspace", vp), ("workspace_bytes", C.c_size_t)]
+                ("splits", C.c_int), ("workspace", vp), ("workspace_bytes", C.c_size_t), ("rope_dim", C.c_int)]
 
 
 class OasisLayerNormArgs(C.Structure):
@@ -127,8 +127,9 @@ SIGNATURES = {
     "oasis_gemm_static_scratch_capacity": (C.c_size_t, []),
     "oasis_layernorm": (C.c_int, [C.POINTER(OasisLayerNormArgs), vp]),
     "oasis_silu_bf16": (C.c_int, [fp, vp, C.c_longlong, vp]),
-    "oasis_attention_spatial": (C.c_int, [vp, vp, C.c_int, C.c_int, vp]),
-    "oasis_attention_temporal": (C.c_int, [vp, vp, C.c_int, C.c_int, vp]),
+    "oasis_attention_spatial": (C.c_int, [vp, vp, C.c_int, C.c_int, C.c_int, vp]),
+    "oasis_attention_temporal": (C.c_int, [vp, vp, C.c_int, C.c_int, C.c_int, vp]),
+    "oasis_gated_residual": (C.c_int, [fp, fp, fp, fp, C.c_longlong, C.c_int, C.c_int, vp]),
     "oasis_post_quant": (C.c_int, [fp, fp, fp, fp, C.c_int, vp]),
 }
 

@@ -21,10 +21,9 @@
 namespace oasis {
 namespace {
 
-constexpr int kHeads = 16;
 constexpr int kDh = 64;
-constexpr int kQkvLd = 3 * kHeads * kDh;  // 3072
-constexpr int kOutLd = kHeads * kDh;      // 1024
+// Head count H is a runtime argument (16 for the full model, 16 / n per rank
+// under n-way tensor parallelism): a qkv row is 3 H 64 wide, an output row H 64.
 constexpr int kKeyTile = 64;
 
 __device__ __forceinline__ int swz(int row, int col) {
@@ -64,17 +63,18 @@ __device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], 
 // Loads `rows` rows (64 bf16 each) of one head slice into a swizzled tile; rows past
 // `valid` are zero-filled.
 template <int NT>
-__device__ __forceinline__ void load_tile(__nv_bfloat16* dst, const __nv_bfloat16* src, int rows, int valid) {
+__device__ __forceinline__ void load_tile(__nv_bfloat16* dst, const __nv_bfloat16* src, int rows, int valid,
+                                          int ld) {
   for (int i = threadIdx.x; i < rows * 8; i += NT) {
     const int r = i >> 3, c = (i & 7) * 8;
     const bool ok = r < valid;
-    cp_async16(dst + swz(r, c), src + (long long)(ok ? r : 0) * kQkvLd + c, ok);
+    cp_async16(dst + swz(r, c), src + (long long)(ok ? r : 0) * ld + c, ok);
   }
 }
 
 template <int NW>
 __global__ void __launch_bounds__(NW * 32) attention_full_kernel(const __nv_bfloat16* __restrict__ qkv,
-                                                                 __nv_bfloat16* __restrict__ out, int seq) {
+                                                                 __nv_bfloat16* __restrict__ out, int seq, int H) {
   pdl_trigger();
   pdl_wait();
   constexpr int NT = NW * 32;
@@ -86,6 +86,7 @@ __global__ void __launch_bounds__(NW * 32) attention_full_kernel(const __nv_bflo
   const int q0 = blockIdx.x * QROWS;
   const int head = blockIdx.y;
   const long long grp_row = (long long)blockIdx.z * seq;
+  const int kQkvLd = 3 * H * kDh, kOutLd = H * kDh;
   const __nv_bfloat16* qb = qkv + grp_row * kQkvLd + head * kDh;
   const __nv_bfloat16* kb = qb + kOutLd;
   const __nv_bfloat16* vb = qb + 2 * kOutLd;
@@ -94,9 +95,9 @@ __global__ void __launch_bounds__(NW * 32) attention_full_kernel(const __nv_bflo
   const int g = lane >> 2, t = lane & 3;
   const int ntiles = (seq + kKeyTile - 1) / kKeyTile;
 
-  load_tile<NT>(sQ, qb + (long long)q0 * kQkvLd, QROWS, seq - q0);
-  load_tile<NT>(sK[0], kb, kKeyTile, seq);
-  load_tile<NT>(sV[0], vb, kKeyTile, seq);
+  load_tile<NT>(sQ, qb + (long long)q0 * kQkvLd, QROWS, seq - q0, kQkvLd);
+  load_tile<NT>(sK[0], kb, kKeyTile, seq, kQkvLd);
+  load_tile<NT>(sV[0], vb, kKeyTile, seq, kQkvLd);
   cp_async_commit();
 
   uint32_t qa[4][4];
@@ -110,8 +111,8 @@ __global__ void __launch_bounds__(NW * 32) attention_full_kernel(const __nv_bflo
     const int buf = j & 1;
     if (j + 1 < ntiles) {
       const int k0n = (j + 1) * kKeyTile;
-      load_tile<NT>(sK[buf ^ 1], kb + (long long)k0n * kQkvLd, kKeyTile, seq - k0n);
-      load_tile<NT>(sV[buf ^ 1], vb + (long long)k0n * kQkvLd, kKeyTile, seq - k0n);
+      load_tile<NT>(sK[buf ^ 1], kb + (long long)k0n * kQkvLd, kKeyTile, seq - k0n, kQkvLd);
+      load_tile<NT>(sV[buf ^ 1], vb + (long long)k0n * kQkvLd, kKeyTile, seq - k0n, kQkvLd);
     }
     cp_async_commit();
     cp_async_wait<1>();
@@ -227,9 +228,10 @@ constexpr int kSpatialSeq = 144;
 constexpr int kSpatialWarps = 9;
 constexpr int kSpatialTile = kSpatialSeq * kDh;  // bf16 elements per q, k or v slice
 
-__device__ __forceinline__ void spatial_prefetch(__nv_bfloat16* buf, const __nv_bfloat16* qkv, int item) {
-  const long long row0 = (long long)(item / kHeads) * kSpatialSeq;
-  const __nv_bfloat16* src = qkv + row0 * kQkvLd + (item % kHeads) * kDh;
+__device__ __forceinline__ void spatial_prefetch(__nv_bfloat16* buf, const __nv_bfloat16* qkv, int item, int H) {
+  const int kQkvLd = 3 * H * kDh, kOutLd = H * kDh;
+  const long long row0 = (long long)(item / H) * kSpatialSeq;
+  const __nv_bfloat16* src = qkv + row0 * kQkvLd + (item % H) * kDh;
   for (int i = threadIdx.x; i < 3 * kSpatialSeq * 8; i += kSpatialWarps * 32) {
     const int m = i / (kSpatialSeq * 8), rem = i - m * (kSpatialSeq * 8);
     const int r = rem >> 3, c = (rem & 7) * 8;
@@ -238,7 +240,7 @@ __device__ __forceinline__ void spatial_prefetch(__nv_bfloat16* buf, const __nv_
 }
 
 __global__ void __launch_bounds__(kSpatialWarps * 32, 1)
-    attention_spatial_kernel(const __nv_bfloat16* __restrict__ qkv, __nv_bfloat16* __restrict__ out, int items) {
+    attention_spatial_kernel(const __nv_bfloat16* __restrict__ qkv, __nv_bfloat16* __restrict__ out, int items, int H) {
   pdl_trigger();
   pdl_wait();
   extern __shared__ __align__(128) __nv_bfloat16 sm[];  // [2][q | k | v]
@@ -247,12 +249,12 @@ __global__ void __launch_bounds__(kSpatialWarps * 32, 1)
   const float sc = 0.125f * 1.4426950408889634f;  // 1/sqrt(64) * log2(e)
   int item = blockIdx.x;
   if (item >= items) return;
-  spatial_prefetch(sm, qkv, item);
+  spatial_prefetch(sm, qkv, item, H);
   cp_async_commit();
   for (int it = 0; item < items; ++it, item += gridDim.x) {
     __nv_bfloat16* cur = sm + (it & 1) * 3 * kSpatialTile;
     const int next = item + gridDim.x;
-    if (next < items) spatial_prefetch(sm + ((it + 1) & 1) * 3 * kSpatialTile, qkv, next);
+    if (next < items) spatial_prefetch(sm + ((it + 1) & 1) * 3 * kSpatialTile, qkv, next, H);
     cp_async_commit();
     cp_async_wait<1>();
     __syncthreads();
@@ -336,7 +338,8 @@ __global__ void __launch_bounds__(kSpatialWarps * 32, 1)
       *reinterpret_cast<uint32_t*>(sO + swz(warp * 16 + g + 8, c)) = pack_bf16x2(o[i][2] * inv1, o[i][3] * inv1);
     }
     __syncwarp();
-    __nv_bfloat16* ob = out + (long long)(item / kHeads) * kSpatialSeq * kOutLd + (item % kHeads) * kDh;
+    const int kOutLd = H * kDh;
+    __nv_bfloat16* ob = out + (long long)(item / H) * kSpatialSeq * kOutLd + (item % H) * kDh;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const int r = warp * 16 + k * 4 + (lane >> 3), c = (lane & 7) * 8;
@@ -350,15 +353,16 @@ __global__ void __launch_bounds__(kSpatialWarps * 32, 1)
 template <int TMAX>
 __global__ void __launch_bounds__(256) attention_temporal_kernel(const __nv_bfloat16* __restrict__ qkv,
                                                                  __nv_bfloat16* __restrict__ out, int batch,
-                                                                 int T, int P) {
+                                                                 int T, int P, int H) {
   pdl_trigger();
   pdl_wait();
   const long long w = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  const long long total = (long long)batch * P * kHeads;
+  const int kQkvLd = 3 * H * kDh, kOutLd = H * kDh;
+  const long long total = (long long)batch * P * H;
   if (w >= total) return;
-  const int head = w % kHeads;
-  const long long bp = w / kHeads;
+  const int head = w % H;
+  const long long bp = w / H;
   const int p = bp % P;
   const long long b = bp / P;
   const long long row0 = b * T * P + p;  // row of frame t = row0 + t * P
@@ -408,9 +412,10 @@ __global__ void __launch_bounds__(256) attention_temporal_kernel(const __nv_bflo
 
 }  // namespace
 
-int attention_full_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, int groups, int seq, cudaStream_t s) {
+int attention_full_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, int groups, int seq, int H, cudaStream_t s) {
   OASIS_REQUIRE(qkv && out, "attention_full: null pointer");
   OASIS_REQUIRE(groups >= 0 && seq > 0, "attention_full: bad shape");
+  OASIS_REQUIRE(H >= 1 && H <= 16, "attention_full: heads=%d outside [1, 16]", H);
   if (groups == 0) return OASIS_OK;
   if (seq == kSpatialSeq) {
     constexpr int smem = 2 * 3 * kSpatialTile * 2;
@@ -422,42 +427,43 @@ int attention_full_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, int grou
       if (e != cudaSuccess) return set_error(OASIS_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
       attr[dev & 63] = true;
     }
-    const int items = groups * kHeads;
+    const int items = groups * H;
     const int grid = items < num_sms() ? items : num_sms();
-    launch_pdl(attention_spatial_kernel, dim3(grid), dim3(kSpatialWarps * 32), smem, s, qkv, out, items);
+    launch_pdl(attention_spatial_kernel, dim3(grid), dim3(kSpatialWarps * 32), smem, s, qkv, out, items, H);
   } else if (seq <= 160) {
     constexpr int NW = 3;  // 48 query rows per CTA
-    dim3 grid((seq + NW * 16 - 1) / (NW * 16), kHeads, groups);
-    launch_pdl(attention_full_kernel<NW>, dim3(grid), dim3(NW * 32), 0, s, qkv, out, seq);
+    dim3 grid((seq + NW * 16 - 1) / (NW * 16), H, groups);
+    launch_pdl(attention_full_kernel<NW>, dim3(grid), dim3(NW * 32), 0, s, qkv, out, seq, H);
   } else if (seq % 96 == 0) {
     constexpr int NW = 6;  // 96 query rows per CTA: 576 = 6 x 96
-    dim3 grid(seq / (NW * 16), kHeads, groups);
-    launch_pdl(attention_full_kernel<NW>, dim3(grid), dim3(NW * 32), 0, s, qkv, out, seq);
+    dim3 grid(seq / (NW * 16), H, groups);
+    launch_pdl(attention_full_kernel<NW>, dim3(grid), dim3(NW * 32), 0, s, qkv, out, seq, H);
   } else {
     constexpr int NW = 4;
-    dim3 grid((seq + NW * 16 - 1) / (NW * 16), kHeads, groups);
-    launch_pdl(attention_full_kernel<NW>, dim3(grid), dim3(NW * 32), 0, s, qkv, out, seq);
+    dim3 grid((seq + NW * 16 - 1) / (NW * 16), H, groups);
+    launch_pdl(attention_full_kernel<NW>, dim3(grid), dim3(NW * 32), 0, s, qkv, out, seq, H);
   }
   return check_launch("attention_full_kernel");
 }
 
-int attention_temporal_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, int batch, int frames, int P,
+int attention_temporal_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, int batch, int frames, int P, int H,
                               cudaStream_t s) {
   OASIS_REQUIRE(qkv && out, "attention_temporal: null pointer");
   OASIS_REQUIRE(frames >= 1 && frames <= 32, "attention_temporal: frames=%d outside [1, 32]", frames);
-  const long long warps = (long long)batch * P * kHeads;
+  OASIS_REQUIRE(H >= 1 && H <= 16, "attention_temporal: heads=%d outside [1, 16]", H);
+  const long long warps = (long long)batch * P * H;
   if (warps == 0) return OASIS_OK;
   const int grid = (int)((warps * 32 + 255) / 256);
   if (frames <= 2)
-    launch_pdl(attention_temporal_kernel<2>, dim3(grid), dim3(256), 0, s, qkv, out, batch, frames, P);
+    launch_pdl(attention_temporal_kernel<2>, dim3(grid), dim3(256), 0, s, qkv, out, batch, frames, P, H);
   else if (frames <= 4)
-    launch_pdl(attention_temporal_kernel<4>, dim3(grid), dim3(256), 0, s, qkv, out, batch, frames, P);
+    launch_pdl(attention_temporal_kernel<4>, dim3(grid), dim3(256), 0, s, qkv, out, batch, frames, P, H);
   else if (frames <= 8)
-    launch_pdl(attention_temporal_kernel<8>, dim3(grid), dim3(256), 0, s, qkv, out, batch, frames, P);
+    launch_pdl(attention_temporal_kernel<8>, dim3(grid), dim3(256), 0, s, qkv, out, batch, frames, P, H);
   else if (frames <= 16)
-    launch_pdl(attention_temporal_kernel<16>, dim3(grid), dim3(256), 0, s, qkv, out, batch, frames, P);
+    launch_pdl(attention_temporal_kernel<16>, dim3(grid), dim3(256), 0, s, qkv, out, batch, frames, P, H);
   else
-    launch_pdl(attention_temporal_kernel<32>, dim3(grid), dim3(256), 0, s, qkv, out, batch, frames, P);
+    launch_pdl(attention_temporal_kernel<32>, dim3(grid), dim3(256), 0, s, qkv, out, batch, frames, P, H);
   return check_launch("attention_temporal_kernel");
 }
 

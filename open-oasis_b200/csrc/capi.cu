@@ -163,9 +163,9 @@ int dit_blocks(const OasisDitWeights* w, int B, int T, float* z, const float* ad
       OASIS_TRY(gemm_launch(p, st));
     }
     if (spatial)
-      OASIS_TRY(attention_full_launch(s.qkv, s.attn, F, kP, st));
+      OASIS_TRY(attention_full_launch(s.qkv, s.attn, F, kP, 16, st));
     else
-      OASIS_TRY(attention_temporal_launch(s.qkv, s.attn, B, T, kP, st));
+      OASIS_TRY(attention_temporal_launch(s.qkv, s.attn, B, T, kP, 16, st));
     {
       GemmProblem p = gemm(s.attn, sb.out_w, M, kD, kD, s.splitk, s.splitk_bytes);
       p.epi.mode = kEpiGatedResid;
@@ -322,7 +322,7 @@ int vae_decode_impl(const OasisVaeWeights* w, const OasisVaeArgs* a, cudaStream_
       p.epi.rope_mod = kVaeTok;
       OASIS_TRY(gemm_launch(p, st));
     }
-    OASIS_TRY(attention_full_launch(s.qkv, s.attn, B, kVaeTok, st));
+    OASIS_TRY(attention_full_launch(s.qkv, s.attn, B, kVaeTok, 16, st));
     {
       GemmProblem p = gemm(s.attn, b.proj_w, R, kD, kD, s.splitk, s.splitk_bytes);
       p.epi.mode = kEpiResid;
@@ -568,6 +568,7 @@ int oasis_gemm(const OasisGemmArgs* a, oasis_stream_t stream) {
   p.epi.rope = a->rope;
   p.epi.rope_div = a->rope_div > 0 ? a->rope_div : 1;
   p.epi.rope_mod = a->rope_mod > 0 ? a->rope_mod : 1;
+  p.epi.rope_dim = a->rope_dim > 0 ? a->rope_dim : 1024;
   p.block_n = a->block_n;
   p.splits = a->splits;
   p.workspace = a->workspace;
@@ -601,14 +602,19 @@ int oasis_silu_bf16(const float* x, void* y, long long n, oasis_stream_t stream)
   return silu_bf16_launch(x, static_cast<__nv_bfloat16*>(y), n, S(stream));
 }
 
-int oasis_attention_spatial(const void* qkv, void* out, int groups, int seq, oasis_stream_t stream) {
+int oasis_attention_spatial(const void* qkv, void* out, int groups, int seq, int heads, oasis_stream_t stream) {
   return attention_full_launch(static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out), groups,
-                               seq, S(stream));
+                               seq, heads, S(stream));
 }
 
-int oasis_attention_temporal(const void* qkv, void* out, int batch, int frames, oasis_stream_t stream) {
+int oasis_attention_temporal(const void* qkv, void* out, int batch, int frames, int heads, oasis_stream_t stream) {
   return attention_temporal_launch(static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out), batch,
-                                   frames, kP, S(stream));
+                                   frames, kP, heads, S(stream));
+}
+
+int oasis_gated_residual(float* z, const float* x, const float* bias, const float* gate, long long ldg,
+                         int rows_per_frame, int rows, oasis_stream_t stream) {
+  return gated_residual_launch(z, x, bias, gate, ldg, rows_per_frame, rows, S(stream));
 }
 
 int oasis_post_quant(const float* latent, const float* w, const float* b, float* z, int rows, oasis_stream_t stream) {

@@ -194,7 +194,45 @@ int grid_for(long long n, int threads) {
   return (int)(g < cap ? (g > 0 ? g : 1) : cap);
 }
 
+// z[r, :] += gate[r / rows_per_frame, :] * (x[r, :] + bias)   (gate NULL: plain residual)
+// x is the all-reduced output of a row-parallel projection (tensor parallelism).
+__global__ void __launch_bounds__(256) gated_residual_kernel(float* __restrict__ z, const float* __restrict__ x,
+                                                             const float* __restrict__ bias,
+                                                             const float* __restrict__ gate, long long ldg,
+                                                             int rows_per_frame, long long n4) {
+  pdl_trigger();
+  pdl_wait();
+  long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  for (; i < n4; i += (long long)gridDim.x * blockDim.x) {
+    const long long e = i * 4;
+    const long long r = e / D;
+    const int c = (int)(e - r * D);
+    float4 v = reinterpret_cast<const float4*>(x)[i];
+    if (bias) {
+      const float4 b = __ldg(reinterpret_cast<const float4*>(bias + c));
+      v.x += b.x; v.y += b.y; v.z += b.z; v.w += b.w;
+    }
+    if (gate) {
+      const float4 g = __ldg(reinterpret_cast<const float4*>(gate + (r / rows_per_frame) * ldg + c));
+      v.x *= g.x; v.y *= g.y; v.z *= g.z; v.w *= g.w;
+    }
+    float4 o = reinterpret_cast<float4*>(z)[i];
+    o.x += v.x; o.y += v.y; o.z += v.z; o.w += v.w;
+    reinterpret_cast<float4*>(z)[i] = o;
+  }
+}
+
 }  // namespace
+
+int gated_residual_launch(float* z, const float* x, const float* bias, const float* gate, long long ldg,
+                          int rows_per_frame, int rows, cudaStream_t s) {
+  OASIS_REQUIRE(z && x && rows >= 0, "gated_residual: bad arguments");
+  OASIS_REQUIRE(!gate || rows_per_frame > 0, "gated_residual: rows_per_frame");
+  const long long n4 = (long long)rows * D / 4;
+  if (n4 == 0) return OASIS_OK;
+  launch_pdl(gated_residual_kernel, dim3(grid_for(n4, 256)), dim3(256), 0, s, z, x, bias, gate, ldg, rows_per_frame, n4);
+  return check_launch("gated_residual_kernel");
+}
 
 int layernorm_launch(const float* x, __nv_bfloat16* y, const LayerNormParams& p, cudaStream_t s) {
   OASIS_REQUIRE(x && y, "layernorm: null pointer");

@@ -47,14 +47,16 @@ int patch_embed_launch(const float* chunk, const float* w, const float* b, float
                        cudaStream_t s);
 int ddim_launch(float* chunk, const float* v, const DdimCoeffs& c, long long n, cudaStream_t s);
 int bridge_launch(const float* chunk, float* latent, int batch, float inv_scale, cudaStream_t s);
+int gated_residual_launch(float* z, const float* x, const float* bias, const float* gate, long long ldg,
+                          int rows_per_frame, int rows, cudaStream_t s);
 int post_quant_launch(const float* lat, const float* w, const float* b, float* z, int rows, cudaStream_t s);
 
 // Attention over a packed qkv buffer [rows, 3 * 1024] bf16 (q | k | v, 16 heads x 64).
 // Full (non-causal) attention within groups of `seq` consecutive rows.
-int attention_full_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, int groups, int seq, cudaStream_t s);
+int attention_full_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, int groups, int seq, int H, cudaStream_t s);
 // Causal attention across the T frames of each session, per (patch, head):
 // row of (b, t, p) = (b * T + t) * P + p.
-int attention_temporal_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, int batch, int frames, int P,
+int attention_temporal_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, int batch, int frames, int P, int H,
                               cudaStream_t s);
 
 }  // namespace oasis

@@ -54,7 +54,7 @@ def attn_spatial(a):
     qkv = torch.randn(a.groups * a.seq, 3072, device="cuda").to(torch.bfloat16)
     out = torch.empty(a.groups * a.seq, 1024, device="cuda", dtype=torch.bfloat16)
     a._keep = (qkv, out)
-    return lambda: _lib.call("oasis_attention_spatial", qkv.data_ptr(), out.data_ptr(), a.groups, a.seq, _st())
+    return lambda: _lib.call("oasis_attention_spatial", qkv.data_ptr(), out.data_ptr(), a.groups, a.seq, 16, _st())
 
 
 def attn_temporal(a):
@@ -62,7 +62,7 @@ def attn_temporal(a):
     qkv = torch.randn(rows, 3072, device="cuda").to(torch.bfloat16)
     out = torch.empty(rows, 1024, device="cuda", dtype=torch.bfloat16)
     a._keep = (qkv, out)
-    return lambda: _lib.call("oasis_attention_temporal", qkv.data_ptr(), out.data_ptr(), a.batch, a.frames, _st())
+    return lambda: _lib.call("oasis_attention_temporal", qkv.data_ptr(), out.data_ptr(), a.batch, a.frames, 16, _st())
 
 
 def layernorm(a):

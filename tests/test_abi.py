@@ -67,7 +67,7 @@ def test_invalid_arguments_are_rejected_without_a_gpu():
     args.n, args.k = 128, 100
     assert lib.oasis_gemm(C.byref(args), None) == -1
     assert b"multiple of 64" in lib.oasis_last_error()
-    assert lib.oasis_attention_temporal(16, 16, 1, 33, None) == -1
+    assert lib.oasis_attention_temporal(16, 16, 1, 33, 16, None) == -1
     assert b"frames" in lib.oasis_last_error()
     d = _lib.OasisDitArgs(1, 40, 16, 16, 16, 1, 16, 1 << 30)
     w = _lib.OasisDitWeights()
@@ -81,7 +81,7 @@ def test_invalid_arguments_are_rejected_without_a_gpu():
 
 def test_call_raises_with_status_and_message():
     with pytest.raises(_lib.OasisError) as ei:
-        _lib.call("oasis_attention_temporal", 16, 16, 1, 0, None)
+        _lib.call("oasis_attention_temporal", 16, 16, 1, 0, 16, None)
     assert ei.value.code == -1 and "frames" in str(ei.value)
 
 

@@ -226,7 +226,7 @@ def _attn_ref(q, k, v, mask=None):
 def test_attention_full(groups, seq):
     qkv = rand_bf16(groups * seq, 3072, seed=groups * 1000 + seq)
     out = torch.empty(groups * seq, 1024, device=DEV, dtype=torch.bfloat16)
-    _lib.call("oasis_attention_spatial", qkv.data_ptr(), out.data_ptr(), groups, seq, _s())
+    _lib.call("oasis_attention_spatial", qkv.data_ptr(), out.data_ptr(), groups, seq, 16, _s())
     torch.cuda.synchronize()
     x = qkv.float().reshape(groups, seq, 3, 16, 64).permute(2, 0, 3, 1, 4)  # 3 G H S D
     ref = _attn_ref(x[0], x[1], x[2]).permute(0, 2, 1, 3).reshape(groups * seq, 1024)
@@ -238,7 +238,7 @@ def test_attention_temporal(B, T):
     P = 144
     qkv = rand_bf16(B * T * P, 3072, seed=B * 100 + T)
     out = torch.empty(B * T * P, 1024, device=DEV, dtype=torch.bfloat16)
-    _lib.call("oasis_attention_temporal", qkv.data_ptr(), out.data_ptr(), B, T, _s())
+    _lib.call("oasis_attention_temporal", qkv.data_ptr(), out.data_ptr(), B, T, 16, _s())
     torch.cuda.synchronize()
     x = qkv.float().reshape(B, T, P, 3, 16, 64).permute(3, 0, 2, 4, 1, 5)  # 3 B P H T D
     mask = torch.tril(torch.ones(T, T, dtype=torch.bool, device=DEV))
