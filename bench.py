@@ -29,6 +29,8 @@ import time
 import torch
 import torch.distributed as dist
 
+# stdout carries exactly one JSON line: keep NCCL's version banner off it
+os.environ["NCCL_DEBUG"] = "WARN"
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 import __graft_entry__  # noqa: E402
@@ -292,6 +294,52 @@ def latency_extras(dw, vw, peaks):
     return out
 
 
+def c5_compare(rank, world, dev, PAR, reps=3):
+    """BASELINE C5 (16 sessions, T=32, seed 3): one DiT step (all 16 sessions)
+    under n-way tensor parallelism vs session data parallelism on the same GPUs."""
+    from oasis_b200 import engine as E
+    from oasis_b200 import host as H
+    from oasis_b200 import tensor_parallel as TP
+    from oasis_b200.weights import DitDeviceWeights, init_dit_weights
+
+    S, T = 16, 32
+    sd = init_dit_weights(seed=3)
+    g = torch.Generator().manual_seed(3)
+    z0 = torch.randn(S, T, H.N_PATCHES, H.D_MODEL, generator=g).to(dev)
+    cond = torch.randn(S, T, H.D_MODEL, generator=g).to(dev)
+    out = {"sessions": S, "frames_T": T, "n_gpus": world}
+
+    def timed(fn):
+        fn()
+        PAR.barrier()
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        e[0].record()
+        for _ in range(reps):
+            fn()
+        e[1].record()
+        PAR.barrier()
+        return PAR.max_over_ranks(e[0].elapsed_time(e[1]) / reps)
+
+    # data parallel: this rank's 16 / n sessions with full weights
+    s0, b = PAR.shard_sessions(S, world, rank)
+    dw = DitDeviceWeights(sd, dev)
+    zb = z0[s0:s0 + b].clone()
+    v = torch.empty(b, H.N_PATCHES, H.OUT_DIM, device=dev)
+    ws = E.workspace(E.dit_workspace_bytes(b, T), dev)
+    out["dp_ms_per_dit_step"] = round(timed(lambda: E.dit_forward(dw, zb.copy_(z0[s0:s0 + b]), cond[s0:s0 + b], v, ws)), 3)
+    del ws, dw
+    if world > 1 and 16 % world == 0:
+        tpw = TP.TPDitWeights(sd, world, rank, dev)
+        sc = TP.TPScratch(tpw, S, T, dev)
+        zt = z0.clone()
+        vt = torch.empty(S, H.N_PATCHES, H.OUT_DIM, device=dev)
+        out["tp_ms_per_dit_step"] = round(timed(lambda: TP.dit_forward_tp(tpw, zt.copy_(z0), cond, vt, sc)), 3)
+        out["tp_allreduce"] = "NCCL, fp32 partials [73728, 1024] after O and FC2 (64 per step)"
+        del tpw, sc
+    torch.cuda.empty_cache()
+    return out
+
+
 def main():
     args = parse()
     from oasis_b200 import parallel as PAR
@@ -370,6 +418,7 @@ def main():
     e2e_value = args.sessions * args.steps / (PAR.max_over_ranks(ev[0].elapsed_time(ev[2])) / 1000.0)
 
     roof = gemm_roofline(B * T * 144, 10, peaks)
+    c5 = None if args.no_extras else c5_compare(rank, world, dev, PAR)
     extras, cpu = {}, None
     if rank == 0 and world == 1 and not args.no_extras:
         extras = latency_extras(dw, vw, peaks)
@@ -393,7 +442,7 @@ def main():
             "clocks": clk,
             "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": int(launches_per_frame * args.steps),
-            "roofline": roof, "cpu_baseline": cpu, **extras,
+            "roofline": roof, "cpu_baseline": cpu, **extras, "c5_tp_vs_dp": c5,
         }
         print(json.dumps(line), flush=True)
     if dist.is_initialized():
