@@ -29,8 +29,10 @@ import time
 import torch
 import torch.distributed as dist
 
-# stdout carries exactly one JSON line: keep NCCL's version banner off it
-os.environ["NCCL_DEBUG"] = "WARN"
+# stdout carries exactly one JSON line: NCCL's messages (its version banner
+# included) go to stderr
+os.environ.setdefault("NCCL_DEBUG", "WARN")
+os.environ["NCCL_DEBUG_FILE"] = "/dev/stderr"
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 import __graft_entry__  # noqa: E402
