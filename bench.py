@@ -29,10 +29,6 @@ import time
 import torch
 import torch.distributed as dist
 
-# stdout carries exactly one JSON line: NCCL's messages (its version banner
-# included) go to stderr
-os.environ.setdefault("NCCL_DEBUG", "WARN")
-os.environ["NCCL_DEBUG_FILE"] = "/dev/stderr"
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 import __graft_entry__  # noqa: E402
@@ -179,7 +175,7 @@ def run_reference(args, rank, world):
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # --------------------------------------------------------------------------- GPU arm
@@ -342,7 +338,26 @@ def c5_compare(rank, world, dev, PAR, reps=3):
     return out
 
 
+_RESULT_FD = None
+
+
+def emit(line: dict) -> None:
+    """Writes the one JSON result line to the process's original stdout."""
+    data = (json.dumps(line) + "\n").encode()
+    if _RESULT_FD is None:
+        sys.stdout.write(data.decode())
+        sys.stdout.flush()
+    else:
+        os.write(_RESULT_FD, data)
+
+
 def main():
+    global _RESULT_FD
+    # stdout carries exactly one JSON line: everything else written to fd 1 while
+    # the benchmark runs (NCCL's version banner, library prints) goes to stderr
+    sys.stdout.flush()
+    _RESULT_FD = os.dup(1)
+    os.dup2(2, 1)
     args = parse()
     from oasis_b200 import parallel as PAR
 
@@ -446,7 +461,7 @@ def main():
             "gpu_launches": int(launches_per_frame * args.steps),
             "roofline": roof, "cpu_baseline": cpu, **extras, "c5_tp_vs_dp": c5,
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
     if dist.is_initialized():
         dist.destroy_process_group()
 
