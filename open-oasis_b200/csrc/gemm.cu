@@ -41,9 +41,14 @@ struct Cfg {
   // next; residual tiles are TMA-loaded into them ahead of time). Measured on
   // B200: worth a pipeline stage even at BN = 256.
   static constexpr int NBUF = 2;
-  static constexpr int STAGES = BN == 256 ? 3 : (BN == 128 ? 5 : 6);
-  static constexpr int A_BYTES = BM * BK * 2;
-  static constexpr int B_BYTES = BN * BK * 2;
+  // Narrow tiles load two 64-wide K atoms per TMA instruction (a stage covers
+  // K = 128): the per-instruction cost, not bytes, bounds small-M GEMMs.
+  static constexpr int KA = BN <= 128 ? 2 : 1;
+  static constexpr int STAGES = BN == 256 ? 3 : (BN == 128 ? 2 : (BN == 64 ? 3 : 4));
+  static constexpr int A_ATOM = BM * BK * 2;  // bytes of one 64-wide K atom of the A tile
+  static constexpr int B_ATOM = BN * BK * 2;
+  static constexpr int A_BYTES = A_ATOM * KA;
+  static constexpr int B_BYTES = B_ATOM * KA;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;  // two accumulators; 128/256/512 (power of 2)
   static constexpr int STG_BYTES = kEpiWarps * kStgBytes * NBUF;
@@ -381,7 +386,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n_tiles = (N + BN - 1) / BN;
   const int splits = sk.splits;
   const int units = m_tiles * n_tiles * splits;
-  const int kb_total = K / BK;
+  const int kb_total = K / (BK * C::KA);  // stages of K
   const int kb_per_split = kb_total / splits;  // host guarantees divisibility
 
   if (warp == 0 && lane == 0) {
@@ -412,6 +417,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
+    // stage kb covers K atoms [kb KA, kb KA + KA)
+    auto load_a = [&](void* dst, uint64_t* bar, int kb, int m0) {
+      if constexpr (C::KA == 1) tma_load_2d(dst, &tmA, bar, kb * BK, m0);
+      else tma_load_3d(dst, &tmA, bar, 0, m0, kb * C::KA);
+    };
+    auto load_w = [&](void* dst, uint64_t* bar, int kb, int n0) {
+      if constexpr (C::KA == 1) tma_load_2d(dst, &tmW, bar, kb * BK, n0);
+      else tma_load_3d(dst, &tmW, bar, 0, n0, kb * C::KA);
+    };
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
@@ -426,7 +440,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         pre = kb_per_split < C::STAGES ? kb_per_split : C::STAGES;
         for (int i = 0; i < pre; ++i) {
           mbar_arrive_expect_tx(&full[i], C::STAGE_BYTES);
-          tma_load_2d(smem + i * C::STAGE_BYTES + C::A_BYTES, &tmW, &full[i], (kb0 + i) * BK, n0);
+          load_w(smem + i * C::STAGE_BYTES + C::A_BYTES, &full[i], kb0 + i, n0);
         }
       }
       pdl_wait();
@@ -437,12 +451,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kb = kb0; kb < kb0 + kb_per_split; ++kb) {
           uint8_t* sa = smem + stage * C::STAGE_BYTES;
           if (u == (int)blockIdx.x && kb - kb0 < pre) {
-            tma_load_2d(sa, &tmA, &full[stage], kb * BK, m0);  // W already in flight
+            load_a(sa, &full[stage], kb, m0);  // W already in flight
           } else {
             if (!mbar_wait(&empty[stage], phase ^ 1, kDevTimeoutSmemEmpty)) { ok = false; break; }
             mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
-            tma_load_2d(sa, &tmA, &full[stage], kb * BK, m0);
-            tma_load_2d(sa + C::A_BYTES, &tmW, &full[stage], kb * BK, n0);
+            load_a(sa, &full[stage], kb, m0);
+            load_w(sa + C::A_BYTES, &full[stage], kb, n0);
           }
           if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
         }
@@ -465,13 +479,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!mbar_wait(&full[stage], phase, kDevTimeoutTmaFull)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smem + stage * C::STAGE_BYTES);
-          const uint64_t adesc = smem_desc_sw128(a_addr);
-          const uint64_t bdesc = smem_desc_sw128(a_addr + C::A_BYTES);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            // +32 bytes per 16-element K step inside the 128-byte swizzle atom
-            tc_mma_bf16(d_tmem, adesc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2), idesc,
-                        (kb > 0 || k > 0) ? 1u : 0u);
+          for (int at = 0; at < C::KA; ++at) {
+            const uint64_t adesc = smem_desc_sw128(a_addr + at * C::A_ATOM);
+            const uint64_t bdesc = smem_desc_sw128(a_addr + C::A_BYTES + at * C::B_ATOM);
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k) {
+              // +32 bytes per 16-element K step inside the 128-byte swizzle atom
+              tc_mma_bf16(d_tmem, adesc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2), idesc,
+                          (kb > 0 || at > 0 || k > 0) ? 1u : 0u);
+            }
           }
           tc_commit(&empty[stage]);
           if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
@@ -560,17 +577,31 @@ int get_encoder() {
 }
 
 // K-major bf16 tile map: dims {K, rows}, box {64, box_rows}, 128-byte swizzle, OOB -> 0.
-int make_map(CUtensorMap* map, const void* ptr, long long rows, long long K, long long ld, int box_rows) {
+int make_map(CUtensorMap* map, const void* ptr, long long rows, long long K, long long ld, int box_rows,
+             int atoms = 1) {
   OASIS_TRY(get_encoder());
   OASIS_REQUIRE((reinterpret_cast<uintptr_t>(ptr) & 15) == 0, "GEMM operand not 16-byte aligned");
   OASIS_REQUIRE((ld * 2) % 16 == 0, "GEMM operand row stride not a multiple of 16 bytes");
-  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
-  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides,
-                        box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r;
+  if (atoms == 1) {
+    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+    cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    // {64, rows, K / 64} view: one box = `atoms` consecutive 64-wide K atoms of
+    // box_rows rows, laid out atom after atom (each atom the 128B-swizzled tile).
+    cuuint64_t dims[3] = {(cuuint64_t)BK, (cuuint64_t)rows, (cuuint64_t)(K / BK)};
+    cuuint64_t strides[2] = {(cuuint64_t)(ld * 2), (cuuint64_t)(BK * 2)};
+    cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)box_rows, (cuuint32_t)atoms};
+    cuuint32_t estr[3] = {1, 1, 1};
+    r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
   if (r != CUDA_SUCCESS) return set_error(OASIS_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return OASIS_OK;
 }
@@ -606,8 +637,8 @@ int launch_bn(const GemmProblem& p, int splits, cudaStream_t stream) {
     attr_set[dev & 63] = true;
   }
   CUtensorMap ta, tw, to, tr;
-  OASIS_TRY(make_map(&ta, p.A, p.M, p.K, p.lda, BM));
-  OASIS_TRY(make_map(&tw, p.W, p.N, p.K, p.K, BN));
+  OASIS_TRY(make_map(&ta, p.A, p.M, p.K, p.lda, BM, C::KA));
+  OASIS_TRY(make_map(&tw, p.W, p.N, p.K, p.K, BN, C::KA));
   if (p.epi.mode == kEpiImage)
     to = ta;  // unused: the image epilogue scatters directly
   else
@@ -679,6 +710,7 @@ size_t gemm_splitk_bytes(int M, int N, int K, int block_n, int splits) {
   Plan pl = choose_plan(M, N, K);
   if (block_n) pl.bn = block_n;
   if (splits) pl.splits = splits;
+  if (pl.bn <= 128 && K % (2 * BK)) pl.bn = 256;  // as gemm_launch
   if (pl.splits <= 1) return 0;
   const size_t tiles = (size_t)((M + BM - 1) / BM) * ((N + pl.bn - 1) / pl.bn);
   return tiles * pl.splits * BM * pl.bn * sizeof(float) + tiles * sizeof(int);
@@ -696,11 +728,20 @@ int gemm_launch(const GemmProblem& p, cudaStream_t stream) {
   if (p.epi.mode == kEpiGatedResid) OASIS_REQUIRE(p.epi.gate && p.epi.rows_per_frame > 0, "GEMM: gate missing");
   if (p.epi.mode == kEpiRopeBF16) OASIS_REQUIRE(p.epi.rope && p.epi.rope_mod > 0 && p.epi.rope_div > 0, "GEMM: rope table missing");
   Plan pl = choose_plan(p.M, p.N, p.K);
+  // fp32-output epilogues (32-column chunks) can use 32-wide tiles: at a few
+  // hundred rows and N = 1024 that doubles the SMs streaming the weights.
+  if (pl.bn == 64 && !bf16_out(p.epi.mode) && p.epi.mode != kEpiImage &&
+      ((p.M + BM - 1) / BM) * ((p.N + 63) / 64) < num_sms() / 2)
+    pl.bn = 32;
   if (p.block_n) pl.bn = p.block_n;
   if (p.splits) pl.splits = p.splits;
   if (pl.splits > 1 && !p.workspace) pl.splits = 1;
-  OASIS_REQUIRE((p.K / BK) % pl.splits == 0, "GEMM: splits=%d must divide K/64=%d", pl.splits, p.K / BK);
+  OASIS_REQUIRE(pl.bn != 32 || !bf16_out(p.epi.mode), "GEMM: block_n=32 needs an fp32 epilogue");
+  if (pl.bn <= 128 && p.K % (2 * BK)) pl.bn = 256;  // narrower tiles stage K in 128-wide steps
+  const int k_stages = p.K / (pl.bn <= 128 ? 2 * BK : BK);
+  OASIS_REQUIRE(k_stages % pl.splits == 0, "GEMM: splits=%d must divide the %d K stages", pl.splits, k_stages);
   switch (pl.bn) {
+    case 32: return launch_bn<32>(p, pl.splits, stream);
     case 64: return launch_bn<64>(p, pl.splits, stream);
     case 128: return launch_bn<128>(p, pl.splits, stream);
     case 256: return launch_bn<256>(p, pl.splits, stream);

@@ -49,7 +49,8 @@ def rand_bf16(*shape, scale=1.0, seed=0):
 @pytest.mark.parametrize("M,N,K,block_n,splits", [
     (128, 256, 64, 256, 1), (288, 3072, 1024, 0, 0), (300, 1024, 1024, 64, 4), (1000, 4096, 1024, 256, 1),
     (577, 1024, 4096, 128, 1), (2, 2048, 1024, 64, 2), (1152, 64, 1024, 64, 1), (4608, 1024, 4096, 0, 0),
-    (73, 1200, 1024, 128, 1), (512, 1024, 1024, 64, 16),
+    (73, 1200, 1024, 128, 1), (512, 1024, 1024, 64, 8), (300, 1024, 4096, 32, 2), (300, 1024, 1024, 32, 1),
+    (300, 1216, 192, 64, 1), (130, 1024, 4096, 64, 1),
 ])
 def test_gemm_f32(M, N, K, block_n, splits):
     a = rand_bf16(M, K, seed=1)
