@@ -218,6 +218,36 @@ size_t oasis_frame_workspace_size(int batch, int frames, int steps);
 int oasis_generate_frame(const OasisDitWeights* w, const OasisVaeWeights* vw, const OasisFrameArgs* a,
                          oasis_stream_t stream);
 
+/* ---------------------------------------------------- context caching --- */
+/* The context frames attend only to earlier frames (causal temporal attention)
+ * and keep the same conditioning at every DDIM step, so their rows can be run
+ * once per generated frame and only the generated frame's rows per step
+ * (oasis_inference.py:1218-1403, default path :1934-1960; the reference does
+ * this for one context frame, here for any T - 1 <= 31).
+ *
+ * KV cache: for each of the 16 temporal sub-blocks, the packed RoPE'd QKV rows
+ * of the context frames, bf16 [16][B, T-1, 144, 3072]. */
+size_t oasis_kv_cache_size(int batch, int past_frames);
+
+/* Replaces precompute_past_state (oasis_inference.py:1354-1369). a->frames =
+ * T - 1 context frames; a->z [B, T-1, 144, 1024] fp32 is overwritten; a->cond
+ * [B, T-1, 1024]; a->v_out is not used. Workspace: oasis_dit_workspace_size(B, T-1). */
+int oasis_dit_precompute_past(const OasisDitWeights* w, const OasisDitArgs* a, void* kv_cache, size_t kv_cache_bytes,
+                              oasis_stream_t stream);
+
+/* Replaces dit_forward_currentonly (oasis_inference.py:1372-1403). a->frames = 1;
+ * a->z [B, 144, 1024] fp32 generated frame (overwritten); a->cond [B, 1024];
+ * a->v_out [B, 144, 64]. The generated frame sits at temporal position
+ * past_frames. Workspace: oasis_dit_workspace_size(B, 1). */
+int oasis_dit_forward_current(const OasisDitWeights* w, const OasisDitArgs* a, const void* kv_cache,
+                              size_t kv_cache_bytes, int past_frames, oasis_stream_t stream);
+
+/* oasis_generate_frame with the context rows run once (same arguments and
+ * results up to rounding; the KV cache lives in the workspace). */
+size_t oasis_frame_kv_workspace_size(int batch, int frames, int steps);
+int oasis_generate_frame_kv(const OasisDitWeights* w, const OasisVaeWeights* vw, const OasisFrameArgs* a,
+                            oasis_stream_t stream);
+
 /* ------------------------------------------------------------ op level --- */
 
 /* tcgen05 GEMM: acc = A[M,K] . W[N,K]^T (bf16 in, fp32 accumulate) + bias, then
@@ -295,6 +325,11 @@ int oasis_attention_spatial(const void* qkv, void* out, int groups, int seq, int
  * of (b, t, p) = (b T + t) 144 + p. Replaces sdpa_temporal_causal
  * (src/sdpa_causal.py:17-100) and its block-diagonal packing. */
 int oasis_attention_temporal(const void* qkv, void* out, int batch, int frames, int heads, oasis_stream_t stream);
+/* The generated frame's query per (session, patch, head) against the cached
+ * context keys/values plus its own: past_qkv [B, Tp, 144, 3 H 64], cur_qkv
+ * [B, 144, 3 H 64], out [B, 144, H 64]. */
+int oasis_attention_temporal_cached(const void* past_qkv, const void* cur_qkv, void* out, int batch, int past_frames,
+                                    int heads, oasis_stream_t stream);
 
 /* z[r, :1024] += gate[(r / rows_per_frame) ldg + :] * (x[r, :] + bias), gate NULL =
  * plain residual. Applies the bias, adaLN gate and residual after the all-reduce of a

@@ -121,6 +121,13 @@ SIGNATURES = {
     "oasis_frame_workspace_size": (C.c_size_t, [C.c_int, C.c_int, C.c_int]),
     "oasis_generate_frame": (C.c_int, [C.POINTER(OasisDitWeights), C.POINTER(OasisVaeWeights),
                                        C.POINTER(OasisFrameArgs), vp]),
+    "oasis_kv_cache_size": (C.c_size_t, [C.c_int, C.c_int]),
+    "oasis_dit_precompute_past": (C.c_int, [C.POINTER(OasisDitWeights), C.POINTER(OasisDitArgs), vp, C.c_size_t, vp]),
+    "oasis_dit_forward_current": (C.c_int, [C.POINTER(OasisDitWeights), C.POINTER(OasisDitArgs), vp, C.c_size_t,
+                                            C.c_int, vp]),
+    "oasis_frame_kv_workspace_size": (C.c_size_t, [C.c_int, C.c_int, C.c_int]),
+    "oasis_generate_frame_kv": (C.c_int, [C.POINTER(OasisDitWeights), C.POINTER(OasisVaeWeights),
+                                          C.POINTER(OasisFrameArgs), vp]),
     "oasis_gemm": (C.c_int, [C.POINTER(OasisGemmArgs), vp]),
     "oasis_gemm_workspace_size": (C.c_size_t, [C.c_int, C.c_int, C.c_int]),
     "oasis_gemm_static_scratch": (C.c_int, [C.POINTER(OasisGemmArgs), vp]),
@@ -129,6 +136,7 @@ SIGNATURES = {
     "oasis_silu_bf16": (C.c_int, [fp, vp, C.c_longlong, vp]),
     "oasis_attention_spatial": (C.c_int, [vp, vp, C.c_int, C.c_int, C.c_int, vp]),
     "oasis_attention_temporal": (C.c_int, [vp, vp, C.c_int, C.c_int, C.c_int, vp]),
+    "oasis_attention_temporal_cached": (C.c_int, [vp, vp, vp, C.c_int, C.c_int, C.c_int, vp]),
     "oasis_gated_residual": (C.c_int, [fp, fp, fp, fp, C.c_longlong, C.c_int, C.c_int, vp]),
     "oasis_post_quant": (C.c_int, [fp, fp, fp, fp, C.c_int, vp]),
 }

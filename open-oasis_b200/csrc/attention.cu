@@ -14,6 +14,8 @@
 // attention_temporal: causal softmax over the T frames of one session, per
 //   (patch, head). One warp per problem, lane = 2 of the 64 head dims, q/k/v for
 //   all frames held in registers, scores reduced with warp shuffles.
+// attention_temporal_cached: the same for only the generated frame's query, with
+//   the context frames' keys/values read from a cache written once per frame.
 #include "common.cuh"
 #include "pointwise.cuh"
 #include "status.h"
@@ -410,7 +412,94 @@ __global__ void __launch_bounds__(256) attention_temporal_kernel(const __nv_bflo
   }
 }
 
+// Context-cached temporal attention: the one query of the generated frame
+// (position Tp) of each (session, patch, head) against the cached keys/values
+// of the Tp context frames plus its own. past: packed QKV rows of the context
+// frames, [B, Tp, P, 3 H 64]; cur: packed QKV rows of the generated frame,
+// [B, P, 3 H 64]; out: [B, P, H 64]. The causal mask admits every key here.
+template <int TMAX>
+__global__ void __launch_bounds__(256) attention_temporal_cached_kernel(
+    const __nv_bfloat16* __restrict__ past, const __nv_bfloat16* __restrict__ cur, __nv_bfloat16* __restrict__ out,
+    int batch, int Tp, int P, int H) {
+  pdl_trigger();
+  pdl_wait();
+  const long long w = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int kQkvLd = 3 * H * kDh, kOutLd = H * kDh;
+  const long long total = (long long)batch * P * H;
+  if (w >= total) return;
+  const int head = w % H;
+  const long long bp = w / H;
+  const int p = bp % P;
+  const long long b = bp / P;
+  const int col = head * kDh + 2 * lane;
+  const __nv_bfloat16* cp = cur + bp * kQkvLd + col;
+  const float2 q = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(cp));
+  __nv_bfloat162 kr[TMAX], vr[TMAX];
+#pragma unroll
+  for (int s = 0; s < TMAX; ++s) {
+    if (s < Tp) {
+      const __nv_bfloat16* rp = past + ((b * Tp + s) * P + p) * kQkvLd + col + kOutLd;
+      kr[s] = *reinterpret_cast<const __nv_bfloat162*>(rp);
+      vr[s] = *reinterpret_cast<const __nv_bfloat162*>(rp + kOutLd);
+    } else if (s == Tp) {
+      kr[s] = *reinterpret_cast<const __nv_bfloat162*>(cp + kOutLd);
+      vr[s] = *reinterpret_cast<const __nv_bfloat162*>(cp + 2 * kOutLd);
+    }
+  }
+  const float sc = 0.125f * 1.4426950408889634f;
+  float sc_[TMAX];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int s = 0; s < TMAX; ++s) {
+    if (s <= Tp) {
+      const float2 k = __bfloat1622float2(kr[s]);
+      float d = q.x * k.x + q.y * k.y;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+      sc_[s] = d * sc;
+      mx = fmaxf(mx, sc_[s]);
+    }
+  }
+  float l = 0.f, o0 = 0.f, o1 = 0.f;
+#pragma unroll
+  for (int s = 0; s < TMAX; ++s) {
+    if (s <= Tp) {
+      const float e = exp2f(sc_[s] - mx);
+      const float2 v = __bfloat1622float2(vr[s]);
+      l += e;
+      o0 = fmaf(e, v.x, o0);
+      o1 = fmaf(e, v.y, o1);
+    }
+  }
+  const float inv = 1.f / l;
+  *reinterpret_cast<uint32_t*>(out + bp * kOutLd + col) = pack_bf16x2(o0 * inv, o1 * inv);
+}
+
 }  // namespace
+
+int attention_temporal_cached_launch(const __nv_bfloat16* past, const __nv_bfloat16* cur, __nv_bfloat16* out,
+                                     int batch, int past_frames, int P, int H, cudaStream_t s) {
+  OASIS_REQUIRE(cur && out && (past || past_frames == 0), "attention_temporal_cached: null pointer");
+  OASIS_REQUIRE(past_frames >= 0 && past_frames <= 31, "attention_temporal_cached: past_frames=%d outside [0, 31]",
+                past_frames);
+  OASIS_REQUIRE(H >= 1 && H <= 16, "attention_temporal_cached: heads=%d outside [1, 16]", H);
+  const long long warps = (long long)batch * P * H;
+  if (warps == 0) return OASIS_OK;
+  const int grid = (int)((warps * 32 + 255) / 256);
+  const int t = past_frames + 1;
+  if (t <= 2)
+    launch_pdl(attention_temporal_cached_kernel<2>, dim3(grid), dim3(256), 0, s, past, cur, out, batch, past_frames, P, H);
+  else if (t <= 4)
+    launch_pdl(attention_temporal_cached_kernel<4>, dim3(grid), dim3(256), 0, s, past, cur, out, batch, past_frames, P, H);
+  else if (t <= 8)
+    launch_pdl(attention_temporal_cached_kernel<8>, dim3(grid), dim3(256), 0, s, past, cur, out, batch, past_frames, P, H);
+  else if (t <= 16)
+    launch_pdl(attention_temporal_cached_kernel<16>, dim3(grid), dim3(256), 0, s, past, cur, out, batch, past_frames, P, H);
+  else
+    launch_pdl(attention_temporal_cached_kernel<32>, dim3(grid), dim3(256), 0, s, past, cur, out, batch, past_frames, P, H);
+  return check_launch("attention_temporal_cached_kernel");
+}
 
 int attention_full_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, int groups, int seq, int H, cudaStream_t s) {
   OASIS_REQUIRE(qkv && out, "attention_full: null pointer");

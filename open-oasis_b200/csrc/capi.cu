@@ -131,10 +131,28 @@ int compute_adaln(const OasisDitWeights* w, const float* cond, int rows, __nv_bf
   return gemm_launch(p, st);
 }
 
+// Context caching across DDIM steps (oasis_inference.py:1218-1403): the context
+// frames see only earlier frames (causal temporal attention) and keep the same
+// conditioning at every step, so their rows are computed once per frame.
+//   kSave: forward over the B x Tp context frames; each temporal sub-block's packed
+//          QKV is written to its cache slot [B, Tp, 144, 3072] (the final layer is
+//          skipped).
+//   kUse:  forward over the generated frame only (T = 1 rows per session); at
+//          temporal sub-blocks its query attends over the cached context keys
+//          and values plus its own, at temporal position Tp.
+enum KvMode { kKvNone = 0, kKvSave = 1, kKvUse = 2 };
+struct KvCtx {
+  int mode = kKvNone;
+  __nv_bfloat16* cache = nullptr;  // [temporal sub-blocks][B, Tp, 144, 3072] bf16
+  int past_frames = 0;             // Tp
+};
+
+size_t kv_slot_elems(int B, int Tp) { return (size_t)B * Tp * kP * 3 * kD; }
+
 // The 32 sub-blocks and the final layer for B sessions x T frames, given the
 // adaLN table [B T, ldm] of this step.
 int dit_blocks(const OasisDitWeights* w, int B, int T, float* z, const float* adaln, float* v_out,
-               int last_frame_only, const DitScratch& s, cudaStream_t st) {
+               int last_frame_only, const DitScratch& s, cudaStream_t st, const KvCtx& kv = KvCtx()) {
   const int F = B * T, M = F * kP;
   const int nsub = w->num_subblocks;
   const long long ldm = (long long)nsub * OASIS_ADALN_WIDTH + 2 * kD;
@@ -152,20 +170,30 @@ int dit_blocks(const OasisDitWeights* w, int B, int T, float* z, const float* ad
     ln.shift_off = off;
     ln.scale_off = off + kD;
     OASIS_TRY(layernorm_launch(z, s.xn, ln, st));
+    __nv_bfloat16* const slot =
+        (!spatial && kv.mode != kKvNone) ? kv.cache + (size_t)(i / 2) * kv_slot_elems(B, kv.past_frames) : nullptr;
+    __nv_bfloat16* const qkv = (!spatial && kv.mode == kKvSave) ? slot : s.qkv;
     {
       GemmProblem p = gemm(s.xn, sb.qkv_w, M, 3 * kD, kD, s.splitk, s.splitk_bytes);
       p.epi.mode = kEpiRopeBF16;
-      p.epi.out = s.qkv;
+      p.epi.out = qkv;
       p.epi.ldo = 3 * kD;
       p.epi.rope = spatial ? w->rope_spatial : w->rope_temporal;
       p.epi.rope_div = spatial ? 1 : kP;
       p.epi.rope_mod = spatial ? kP : T;
+      if (!spatial && kv.mode == kKvUse) {  // every row sits at temporal position Tp
+        p.epi.rope = w->rope_temporal + (size_t)kv.past_frames * 64;
+        p.epi.rope_div = 1;
+        p.epi.rope_mod = 1;
+      }
       OASIS_TRY(gemm_launch(p, st));
     }
     if (spatial)
-      OASIS_TRY(attention_full_launch(s.qkv, s.attn, F, kP, 16, st));
+      OASIS_TRY(attention_full_launch(qkv, s.attn, F, kP, 16, st));
+    else if (kv.mode == kKvUse)
+      OASIS_TRY(attention_temporal_cached_launch(slot, qkv, s.attn, B, kv.past_frames, kP, 16, st));
     else
-      OASIS_TRY(attention_temporal_launch(s.qkv, s.attn, B, T, kP, 16, st));
+      OASIS_TRY(attention_temporal_launch(qkv, s.attn, B, T, kP, 16, st));
     {
       GemmProblem p = gemm(s.attn, sb.out_w, M, kD, kD, s.splitk, s.splitk_bytes);
       p.epi.mode = kEpiGatedResid;
@@ -205,6 +233,7 @@ int dit_blocks(const OasisDitWeights* w, int B, int T, float* z, const float* ad
     }
   }
 
+  if (kv.mode == kKvSave) return OASIS_OK;  // only the cache is wanted
   // Final layer: LN + final adaLN modulate (only the rows that are returned) + linear.
   const long long foff = (long long)nsub * OASIS_ADALN_WIDTH;
   LayerNormParams ln;
@@ -444,6 +473,155 @@ int generate_frame_impl(const OasisDitWeights* w, const OasisVaeWeights* vw, con
   return vae_decode_impl(vw, &va, st);
 }
 
+// ---- context caching (precompute_past_state / dit_forward_currentonly) ----
+
+size_t kv_cache_bytes(int B, int Tp) { return (size_t)(OASIS_DIT_SUBBLOCKS / 2) * kv_slot_elems(B, Tp) * 2; }
+
+int precompute_past_impl(const OasisDitWeights* w, const OasisDitArgs* a, void* cache, size_t cache_bytes,
+                         cudaStream_t st) {
+  OASIS_REQUIRE(w && a, "precompute_past: null argument");
+  const int B = a->batch, Tp = a->frames;
+  OASIS_REQUIRE(B > 0 && Tp >= 1 && Tp <= 31, "precompute_past: batch=%d frames=%d (need frames in [1, 31])", B, Tp);
+  OASIS_REQUIRE(a->z && a->cond && cache, "precompute_past: null tensor");
+  OASIS_REQUIRE(w->num_subblocks >= 0 && w->num_subblocks <= OASIS_DIT_SUBBLOCKS, "precompute_past: num_subblocks");
+  if (cache_bytes < kv_cache_bytes(B, Tp))
+    return set_error(OASIS_ERR_WORKSPACE, "precompute_past: kv cache %zu bytes < %zu", cache_bytes,
+                     kv_cache_bytes(B, Tp));
+  Carve c(a->workspace, a->workspace_bytes);
+  DitScratch s;
+  carve_dit(c, B, Tp, &s);
+  if (!a->workspace || !c.ok())
+    return set_error(OASIS_ERR_WORKSPACE, "precompute_past: workspace %zu bytes < %zu", a->workspace_bytes, c.used);
+  OASIS_TRY(compute_adaln(w, a->cond, B * Tp, s.silu, s.adaln, s.splitk, s.splitk_bytes, st));
+  KvCtx kv;
+  kv.mode = kKvSave;
+  kv.cache = static_cast<__nv_bfloat16*>(cache);
+  kv.past_frames = Tp;
+  return dit_blocks(w, B, Tp, a->z, s.adaln, nullptr, 0, s, st, kv);
+}
+
+int forward_current_impl(const OasisDitWeights* w, const OasisDitArgs* a, const void* cache, size_t cache_bytes,
+                         int Tp, cudaStream_t st) {
+  OASIS_REQUIRE(w && a, "forward_current: null argument");
+  const int B = a->batch;
+  OASIS_REQUIRE(B > 0 && a->frames == 1, "forward_current: batch=%d frames=%d (frames must be 1)", B, a->frames);
+  OASIS_REQUIRE(Tp >= 0 && Tp <= 31, "forward_current: past_frames=%d outside [0, 31]", Tp);
+  OASIS_REQUIRE(a->z && a->cond && a->v_out && (cache || Tp == 0), "forward_current: null tensor");
+  OASIS_REQUIRE(w->num_subblocks >= 0 && w->num_subblocks <= OASIS_DIT_SUBBLOCKS, "forward_current: num_subblocks");
+  if (Tp > 0 && cache_bytes < kv_cache_bytes(B, Tp))
+    return set_error(OASIS_ERR_WORKSPACE, "forward_current: kv cache %zu bytes < %zu", cache_bytes,
+                     kv_cache_bytes(B, Tp));
+  Carve c(a->workspace, a->workspace_bytes);
+  DitScratch s;
+  carve_dit(c, B, 1, &s);
+  if (!a->workspace || !c.ok())
+    return set_error(OASIS_ERR_WORKSPACE, "forward_current: workspace %zu bytes < %zu", a->workspace_bytes, c.used);
+  OASIS_TRY(compute_adaln(w, a->cond, B, s.silu, s.adaln, s.splitk, s.splitk_bytes, st));
+  KvCtx kv;
+  kv.mode = kKvUse;
+  kv.cache = static_cast<__nv_bfloat16*>(const_cast<void*>(cache));
+  kv.past_frames = Tp;
+  return dit_blocks(w, B, 1, a->z, s.adaln, a->v_out, 1, s, st, kv);
+}
+
+struct FrameKvScratch {
+  float* cond_rows;     // [B Tp + S B, 1024]: context rows, then the generated frame's row per step
+  __nv_bfloat16* silu;  // same rows
+  float* adaln;         // same rows x (6144 S + 2048)
+  float* z_past;        // [B Tp 144, 1024]
+  float* z;             // [B 144, 1024]
+  float* v;             // [B 144, 64]
+  float* latent;        // [B, 576, 16]
+  __nv_bfloat16* cache;
+  void* shared;         // DiT scratch (context pass, then the per-step pass), later the VAE's
+  size_t shared_bytes;
+};
+
+size_t carve_frame_kv(Carve& c, int B, int T, int S, FrameKvScratch* f) {
+  const int Tp = T - 1;
+  const size_t R = (size_t)B * Tp + (size_t)S * B;
+  FrameKvScratch d;
+  d.cond_rows = c.take<float>(R * kD);
+  d.silu = c.take<__nv_bfloat16>(R * kD);
+  d.adaln = c.take<float>(R * OASIS_ADALN_ROWS);
+  d.z_past = c.take<float>((size_t)B * Tp * kP * kD);
+  d.z = c.take<float>((size_t)B * kP * kD);
+  d.v = c.take<float>((size_t)B * kP * kOut);
+  d.latent = c.take<float>((size_t)B * kVaeTok * 16);
+  d.cache = Tp ? c.take<__nv_bfloat16>(kv_cache_bytes(B, Tp) / 2) : nullptr;
+  Carve dit(nullptr, 0), vae(nullptr, 0);
+  carve_dit(dit, B, Tp > 1 ? Tp : 1, nullptr, false);
+  carve_vae(vae, B, nullptr);
+  d.shared_bytes = (dit.used > vae.used ? dit.used : vae.used) + 256;
+  d.shared = c.take<uint8_t>(d.shared_bytes);
+  if (f) *f = d;
+  return c.used;
+}
+
+// One frame with the context rows computed once (the reference's default path,
+// oasis_inference.py:1934-1960): cond is laid out as for generate_frame
+// ([steps][B][T][1024]); the context frames use step 0's rows.
+int generate_frame_kv_impl(const OasisDitWeights* w, const OasisVaeWeights* vw, const OasisFrameArgs* a,
+                           cudaStream_t st) {
+  OASIS_REQUIRE(w && a, "generate_frame_kv: null argument");
+  const int B = a->batch, T = a->frames, S = a->steps, Tp = T - 1;
+  OASIS_REQUIRE(B > 0 && T > 0 && T <= 32, "generate_frame_kv: batch=%d frames=%d", B, T);
+  OASIS_REQUIRE(S > 0 && S <= kMaxFrameSteps, "generate_frame_kv: steps=%d outside [1, %d]", S, kMaxFrameSteps);
+  OASIS_REQUIRE(a->chunk && a->cond && a->coeffs, "generate_frame_kv: null tensor");
+  OASIS_REQUIRE(T == 1 || a->context_z, "generate_frame_kv: frames > 1 needs context_z");
+  OASIS_REQUIRE(a->skip_decode || (vw && a->image), "generate_frame_kv: decoding needs VAE weights and an image");
+  OASIS_REQUIRE(w->num_subblocks >= 0 && w->num_subblocks <= OASIS_DIT_SUBBLOCKS, "generate_frame_kv: num_subblocks");
+  Carve c(a->workspace, a->workspace_bytes);
+  FrameKvScratch f;
+  carve_frame_kv(c, B, T, S, &f);
+  if (!a->workspace || !c.ok())
+    return set_error(OASIS_ERR_WORKSPACE, "generate_frame_kv: workspace %zu bytes < %zu", a->workspace_bytes, c.used);
+  Carve dc(f.shared, f.shared_bytes);
+  DitScratch s;
+  carve_dit(dc, B, Tp > 1 ? Tp : 1, &s, false);
+  const long long ldm = (long long)w->num_subblocks * OASIS_ADALN_WIDTH + 2 * kD;
+  const size_t row = kD * sizeof(float);
+  // gather the conditioning rows that are used: context frames (step 0), then the
+  // generated frame of every step (rows (i B + b) T + T - 1: one constant stride)
+  if (Tp > 0) {
+    cudaError_t e = cudaMemcpy2DAsync(f.cond_rows, Tp * row, a->cond, T * row, Tp * row, B, cudaMemcpyDeviceToDevice, st);
+    if (e != cudaSuccess) return set_error(OASIS_ERR_CUDA, "generate_frame_kv: cond copy: %s", cudaGetErrorString(e));
+  }
+  {
+    cudaError_t e = cudaMemcpy2DAsync(f.cond_rows + (size_t)B * Tp * kD, row, a->cond + (size_t)Tp * kD, T * row, row,
+                                      (size_t)S * B, cudaMemcpyDeviceToDevice, st);
+    if (e != cudaSuccess) return set_error(OASIS_ERR_CUDA, "generate_frame_kv: cond copy: %s", cudaGetErrorString(e));
+  }
+  const int R = B * Tp + S * B;
+  OASIS_TRY(compute_adaln(w, f.cond_rows, R, f.silu, f.adaln, s.splitk, s.splitk_bytes, st));
+  KvCtx kv;
+  kv.cache = f.cache;
+  kv.past_frames = Tp;
+  if (Tp > 0) {
+    cudaError_t e = cudaMemcpyAsync(f.z_past, a->context_z, (size_t)B * Tp * kP * row, cudaMemcpyDeviceToDevice, st);
+    if (e != cudaSuccess) return set_error(OASIS_ERR_CUDA, "generate_frame_kv: context copy: %s", cudaGetErrorString(e));
+    kv.mode = kKvSave;
+    OASIS_TRY(dit_blocks(w, B, Tp, f.z_past, f.adaln, nullptr, 0, s, st, kv));
+  }
+  kv.mode = kKvUse;
+  for (int i = 0; i < S; ++i) {
+    PatchEmbedParams pe;
+    pe.rows = B * kP;
+    pe.P = kP;
+    pe.out_group = kP;
+    pe.out_off = 0;
+    OASIS_TRY(patch_embed_launch(a->chunk, w->embed_w, w->embed_b, f.z, pe, st));
+    OASIS_TRY(dit_blocks(w, B, 1, f.z, f.adaln + ((size_t)B * Tp + (size_t)i * B) * ldm, f.v, 1, s, st, kv));
+    const OasisDdimCoeffs& k = a->coeffs[i];
+    DdimCoeffs dk{k.at_sqrt, k.one_minus_at_sqrt, k.inv_at_sqrt, k.inv_sigma, k.an_sqrt, k.one_minus_an_sqrt};
+    OASIS_TRY(ddim_launch(a->chunk, f.v, dk, (long long)B * kP * kOut, st));
+  }
+  if (a->skip_decode) return OASIS_OK;
+  OASIS_TRY(bridge_launch(a->chunk, f.latent, B, 1.0f / kScalingFactor, st));
+  OasisVaeArgs va{B, f.latent, a->image, f.shared, f.shared_bytes};
+  return vae_decode_impl(vw, &va, st);
+}
+
 }  // namespace
 }  // namespace oasis
 
@@ -547,6 +725,34 @@ int oasis_generate_frame(const OasisDitWeights* w, const OasisVaeWeights* vw, co
   return generate_frame_impl(w, vw, a, S(stream));
 }
 
+size_t oasis_kv_cache_size(int batch, int past_frames) {
+  if (batch <= 0 || past_frames <= 0) return 0;
+  return kv_cache_bytes(batch, past_frames);
+}
+
+int oasis_dit_precompute_past(const OasisDitWeights* w, const OasisDitArgs* a, void* kv_cache, size_t kv_cache_bytes,
+                              oasis_stream_t stream) {
+  g_msg[0] = 0;
+  return precompute_past_impl(w, a, kv_cache, kv_cache_bytes, S(stream));
+}
+
+int oasis_dit_forward_current(const OasisDitWeights* w, const OasisDitArgs* a, const void* kv_cache,
+                              size_t kv_cache_bytes, int past_frames, oasis_stream_t stream) {
+  g_msg[0] = 0;
+  return forward_current_impl(w, a, kv_cache, kv_cache_bytes, past_frames, S(stream));
+}
+
+size_t oasis_frame_kv_workspace_size(int batch, int frames, int steps) {
+  Carve c(nullptr, 0);
+  return carve_frame_kv(c, batch, frames, steps, nullptr) + 256;
+}
+
+int oasis_generate_frame_kv(const OasisDitWeights* w, const OasisVaeWeights* vw, const OasisFrameArgs* a,
+                            oasis_stream_t stream) {
+  g_msg[0] = 0;
+  return generate_frame_kv_impl(w, vw, a, S(stream));
+}
+
 int oasis_gemm(const OasisGemmArgs* a, oasis_stream_t stream) {
   OASIS_REQUIRE(a, "gemm: null args");
   GemmProblem p;
@@ -610,6 +816,13 @@ int oasis_attention_spatial(const void* qkv, void* out, int groups, int seq, int
 int oasis_attention_temporal(const void* qkv, void* out, int batch, int frames, int heads, oasis_stream_t stream) {
   return attention_temporal_launch(static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out), batch,
                                    frames, kP, heads, S(stream));
+}
+
+int oasis_attention_temporal_cached(const void* past_qkv, const void* cur_qkv, void* out, int batch, int past_frames,
+                                    int heads, oasis_stream_t stream) {
+  return attention_temporal_cached_launch(static_cast<const __nv_bfloat16*>(past_qkv),
+                                          static_cast<const __nv_bfloat16*>(cur_qkv), static_cast<__nv_bfloat16*>(out),
+                                          batch, past_frames, kP, heads, S(stream));
 }
 
 int oasis_gated_residual(float* z, const float* x, const float* bias, const float* gate, long long ldg,

@@ -58,5 +58,7 @@ int attention_full_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, int grou
 // row of (b, t, p) = (b * T + t) * P + p.
 int attention_temporal_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, int batch, int frames, int P, int H,
                               cudaStream_t s);
+int attention_temporal_cached_launch(const __nv_bfloat16* past, const __nv_bfloat16* cur, __nv_bfloat16* out,
+                                     int batch, int past_frames, int P, int H, cudaStream_t s);
 
 }  // namespace oasis

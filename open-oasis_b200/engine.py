@@ -66,6 +66,48 @@ def dit_forward(dw: DitDeviceWeights, z: torch.Tensor, cond: torch.Tensor, v_out
     return v_out
 
 
+def kv_cache_bytes(batch: int, past_frames: int) -> int:
+    return int(_lib.load().oasis_kv_cache_size(batch, past_frames))
+
+
+def kv_cache(batch: int, past_frames: int, device) -> torch.Tensor:
+    """Device buffer for the context frames' cached QKV of every temporal sub-block."""
+    return workspace(kv_cache_bytes(batch, past_frames), device)
+
+
+def dit_precompute_past(dw: DitDeviceWeights, z_past: torch.Tensor, cond_past: torch.Tensor, cache: torch.Tensor,
+                        ws: torch.Tensor, stream=None) -> torch.Tensor:
+    """Context frames z_past [B, Tp, 144, 1024] fp32 (overwritten), cond_past
+    [B, Tp, 1024] -> cache (precompute_past_state, oasis_inference.py:1354)."""
+    _check_cuda(z_past, "z_past")
+    _check_cuda(cond_past, "cond_past")
+    B, Tp = z_past.shape[0], z_past.shape[1]
+    if tuple(z_past.shape[2:]) != (H.N_PATCHES, H.D_MODEL) or tuple(cond_past.shape) != (B, Tp, H.D_MODEL):
+        raise ValueError(f"bad shapes z_past={tuple(z_past.shape)} cond_past={tuple(cond_past.shape)}")
+    a = _lib.OasisDitArgs(B, Tp, z_past.data_ptr(), cond_past.data_ptr(), 0, 0, ws.data_ptr(), ws.numel())
+    _lib.call("oasis_dit_precompute_past", dw.ref(), C.byref(a), cache.data_ptr(), cache.numel(), _stream(stream))
+    return cache
+
+
+def dit_forward_current(dw: DitDeviceWeights, z_cur: torch.Tensor, cond_cur: torch.Tensor, cache: torch.Tensor | None,
+                        past_frames: int, v_out: torch.Tensor, ws: torch.Tensor, stream=None) -> torch.Tensor:
+    """Generated frame z_cur [B, 144, 1024] fp32 (overwritten), cond_cur [B, 1024],
+    with `past_frames` cached context frames -> v_out [B, 144, 64]
+    (dit_forward_currentonly, oasis_inference.py:1372)."""
+    _check_cuda(z_cur, "z_cur")
+    _check_cuda(cond_cur, "cond_cur")
+    _check_cuda(v_out, "v_out")
+    B = z_cur.shape[0]
+    if tuple(z_cur.shape) != (B, H.N_PATCHES, H.D_MODEL) or tuple(cond_cur.shape) != (B, H.D_MODEL):
+        raise ValueError(f"bad shapes z_cur={tuple(z_cur.shape)} cond_cur={tuple(cond_cur.shape)}")
+    if tuple(v_out.shape) != (B, H.N_PATCHES, H.OUT_DIM):
+        raise ValueError("v_out must be [B, 144, 64]")
+    a = _lib.OasisDitArgs(B, 1, z_cur.data_ptr(), cond_cur.data_ptr(), v_out.data_ptr(), 1, ws.data_ptr(), ws.numel())
+    _lib.call("oasis_dit_forward_current", dw.ref(), C.byref(a), 0 if cache is None else cache.data_ptr(),
+              0 if cache is None else cache.numel(), past_frames, _stream(stream))
+    return v_out
+
+
 def ddim_update(chunk: torch.Tensor, v: torch.Tensor, step: H.DdimStep, stream=None) -> torch.Tensor:
     _check_cuda(chunk, "chunk")
     _check_cuda(v, "v")
@@ -131,11 +173,18 @@ def frame_workspace_bytes(batch: int, frames: int, steps: int) -> int:
     return int(_lib.load().oasis_frame_workspace_size(batch, frames, steps))
 
 
+def frame_kv_workspace_bytes(batch: int, frames: int, steps: int) -> int:
+    return int(_lib.load().oasis_frame_kv_workspace_size(batch, frames, steps))
+
+
 def generate_frame(dw: DitDeviceWeights, vw: VaeDeviceWeights | None, chunk: torch.Tensor,
                    context_z: torch.Tensor | None, cond: torch.Tensor, steps: list[H.DdimStep],
-                   image: torch.Tensor | None, ws: torch.Tensor, skip_decode: bool = False, stream=None):
+                   image: torch.Tensor | None, ws: torch.Tensor, skip_decode: bool = False, stream=None,
+                   kv: bool = False):
     """One frame for B sessions: len(steps) DDIM steps (chunk updated in place),
-    then bridge + VAE decode into image [B, 3, 360, 640] unless skip_decode."""
+    then bridge + VAE decode into image [B, 3, 360, 640] unless skip_decode.
+    kv=True runs the context frames once and only the generated frame per step
+    (oasis_generate_frame_kv; workspace from frame_kv_workspace_bytes)."""
     _check_cuda(chunk, "chunk")
     _check_cuda(cond, "cond")
     S, B, T = cond.shape[0], cond.shape[1], cond.shape[2]
@@ -151,20 +200,20 @@ def generate_frame(dw: DitDeviceWeights, vw: VaeDeviceWeights | None, chunk: tor
     a = _lib.OasisFrameArgs(B, T, S, chunk.data_ptr(), 0 if context_z is None else context_z.data_ptr(),
                             cond.data_ptr(), coeffs, 0 if image is None else image.data_ptr(), int(skip_decode),
                             ws.data_ptr(), ws.numel())
-    _lib.call("oasis_generate_frame", dw.ref(), None if vw is None else vw.ref(), C.byref(a), _stream(stream))
+    _lib.call("oasis_generate_frame_kv" if kv else "oasis_generate_frame", dw.ref(), None if vw is None else vw.ref(), C.byref(a), _stream(stream))
     return chunk
 
 
 class FrameEngine:
     """All device buffers of one generated frame for B sessions with T-frame
-    context windows. `run()` issues the whole frame through oasis_generate_frame
+    context windows (kv=True: context rows run once per frame). `run()` issues the whole frame through oasis_generate_frame
     (4 DDIM steps with all adaLN tables from one GEMM, bridge, VAE decode);
     `capture()` records it (and, for timing breakdowns, the steps alone and the
     decode alone) as CUDA graphs."""
 
     def __init__(self, dw: DitDeviceWeights, vw: VaeDeviceWeights, batch: int, frames: int,
-                 steps: list[H.DdimStep] | None = None):
-        self.dw, self.vw = dw, vw
+                 steps: list[H.DdimStep] | None = None, kv: bool = False):
+        self.dw, self.vw, self.kv = dw, vw, kv
         self.B, self.T = batch, frames
         self.steps = steps if steps is not None else H.ddim_schedule()
         dev = dw.device
@@ -174,7 +223,8 @@ class FrameEngine:
         self.cond = torch.zeros(len(self.steps), B, T, H.D_MODEL, device=dev)
         self.latent = torch.zeros(B, H.VAE_TOKENS, H.VAE_LATENT, device=dev)
         self.image = torch.zeros(B, 3, H.VAE_H * H.VAE_PATCH, H.VAE_W * H.VAE_PATCH, device=dev)
-        self.frame_ws = workspace(frame_workspace_bytes(B, T, len(self.steps)), dev)
+        nbytes = (frame_kv_workspace_bytes if kv else frame_workspace_bytes)(B, T, len(self.steps))
+        self.frame_ws = workspace(nbytes, dev)
         self.step_ws = None
         self.vae_ws = None
         self.graph = None
@@ -184,11 +234,11 @@ class FrameEngine:
 
     def run(self, stream=None):
         generate_frame(self.dw, self.vw, self.chunk, self._ctx(), self.cond, self.steps, self.image, self.frame_ws,
-                       stream=stream)
+                       stream=stream, kv=self.kv)
 
     def run_steps(self, stream=None):
         generate_frame(self.dw, None, self.chunk, self._ctx(), self.cond, self.steps, None, self.frame_ws,
-                       skip_decode=True, stream=stream)
+                       skip_decode=True, stream=stream, kv=self.kv)
 
     def run_decode(self, stream=None):
         if self.vae_ws is None:

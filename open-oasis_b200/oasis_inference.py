@@ -6,6 +6,8 @@ Mapping (reference file:line -> here):
   preload_dit_weights      :505   -> preload_dit_weights(state_dict, device, n_frames)
   prealloc_scratch         :790   -> prealloc_scratch(device, n_frames, batch=1)
   dit_forward_device       :1438  -> dit_forward_device(z_cur, cond_list, dev, scr, ...)
+  precompute_past_state    :1354  -> precompute_past_state(past_z, past_cond, dev, scr, ...)
+  dit_forward_currentonly  :1372  -> dit_forward_currentonly(curr_z, curr_cond, dev, scr, ...)
   ddim_step_fn (closure)   :1909  -> make_ddim_step_fn(dev, scr, context_z)(chunk, step_coeffs, cond_list)
   compute_cond_for_frame   :1406  -> compute_cond_for_frame(t_scalar, action_vec, dev, scr, tt_device)
   preload_vae_decoder_weights :679 -> preload_vae_decoder_weights(vae_state_dict, device)
@@ -18,6 +20,9 @@ Differences a caller sees (all deliberate, B200-first):
   * vae_input is (576, 16) fp32 (no padding to 32 columns);
   * vae_decode_forward fuses vae_unpatchify and the clamp into the predictor GEMM:
     vae_scr["pred_out"] is the (1, 3, 360, 640) frame in [-1, 1], not (576, 1216) patches;
+  * precompute_past_state / dit_forward_currentonly take the conditioning before
+    SiLU (the SiLU runs in the library) and any number n_frames - 1 of context
+    frames (the reference caches exactly one);
   * tt_device / scaler / mean_scale arguments are accepted and ignored;
   * errors raise OasisError (the C status and message) instead of ttnn exceptions.
 """
@@ -52,6 +57,14 @@ def prealloc_scratch(device="cuda", n_frames: int = 2, batch: int = 1) -> dict:
         "z_cur": torch.zeros(batch, n_frames, N_PATCHES, D_MODEL, device=dev),
         "final_out_f32": torch.zeros(batch, n_frames, N_PATCHES, OUT_DIM, device=dev),
         "cond": torch.zeros(batch, n_frames, D_MODEL, device=dev),
+        # context caching (precompute_past_state / dit_forward_currentonly)
+        "kv_cache": E.kv_cache(batch, n_frames - 1, dev) if n_frames > 1 else None,
+        "kv_ws": E.workspace(E.dit_workspace_bytes(batch, max(n_frames - 1, 1)), dev),
+        "z_past": torch.zeros(batch, max(n_frames - 1, 1), N_PATCHES, D_MODEL, device=dev),
+        "cond_past": torch.zeros(batch, max(n_frames - 1, 1), D_MODEL, device=dev),
+        "z_curr": torch.zeros(batch, N_PATCHES, D_MODEL, device=dev),
+        "cond_curr": torch.zeros(batch, D_MODEL, device=dev),
+        "t1_final_out_f32": torch.zeros(batch, N_PATCHES, OUT_DIM, device=dev),
     }
 
 
@@ -73,6 +86,37 @@ def dit_forward_device(z_cur, cond_list, dev: DitDeviceWeights, scr: dict, tt_de
     out = scr["final_out_f32"]
     E.dit_forward(dev, z, scr["cond"], out, scr["dit_ws"], last_frame_only=False)
     return out.view(T * N_PATCHES, OUT_DIM)
+
+
+def precompute_past_state(past_z, past_cond, dev: DitDeviceWeights, scr: dict, tt_device=None, scaler=None,
+                          mean_scale=None) -> None:
+    """Runs the n_frames - 1 context frames once and fills scr["kv_cache"] with
+    their RoPE'd QKV at every temporal sub-block.
+    past_z: ((n_frames - 1) 144, 1024) fp32 embedded context frames;
+    past_cond: one (1024,) pre-SiLU conditioning vector (shared by the context
+    frames, as in the reference) or a list of n_frames - 1 of them."""
+    Tp = scr["n_frames"] - 1
+    if Tp < 1 or scr["batch"] != 1:
+        raise ValueError("precompute_past_state needs a batch=1 scratch with n_frames >= 2")
+    conds = past_cond if isinstance(past_cond, (list, tuple)) else [past_cond] * Tp
+    scr["z_past"].view(-1, D_MODEL).copy_(past_z.reshape(-1, D_MODEL))
+    scr["cond_past"][0].copy_(_cond_rows(conds))
+    E.dit_precompute_past(dev, scr["z_past"], scr["cond_past"], scr["kv_cache"], scr["kv_ws"])
+
+
+def dit_forward_currentonly(curr_z, curr_cond, dev: DitDeviceWeights, scr: dict, tt_device=None, scaler=None,
+                            mean_scale=None) -> torch.Tensor:
+    """The generated frame alone (at temporal position n_frames - 1) against the
+    cache from precompute_past_state. curr_z (144, 1024) fp32; curr_cond (1024,)
+    pre-SiLU. Returns the (144, 64) v-prediction."""
+    if scr["batch"] != 1:
+        raise ValueError("dit_forward_currentonly needs a batch=1 scratch")
+    Tp = scr["n_frames"] - 1
+    scr["z_curr"].view(-1, D_MODEL).copy_(curr_z.reshape(-1, D_MODEL))
+    scr["cond_curr"].copy_(_cond_rows([curr_cond]))
+    out = scr["t1_final_out_f32"]
+    E.dit_forward_current(dev, scr["z_curr"], scr["cond_curr"], scr["kv_cache"], Tp, out, scr["kv_ws"])
+    return out.view(N_PATCHES, OUT_DIM)
 
 
 def make_ddim_step_fn(dev: DitDeviceWeights, scr: dict, context_z: torch.Tensor | None):

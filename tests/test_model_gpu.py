@@ -182,3 +182,67 @@ def test_generate_frame_matches_per_step_path(dit_full, vae_full):
     img_ref = O.vae_decode(O.bridge(c_ref), vsd)
     assert rel_l2(frame_chunk, c_ref) < REL_L2_TOL
     assert rel_l2(frame_img, img_ref) < REL_L2_TOL and cosine(frame_img, img_ref) > COS_TOL
+
+
+@pytest.mark.parametrize("B,T", [(2, 3), (1, 2), (1, 1)])
+def test_kv_cached_forward_matches_full_T(dit_small, B, T):
+    """precompute_past + forward_current (context rows once) equals the full-T
+    forward's last frame, and the oracle."""
+    sd, dw = dit_small
+    z, cond = _inputs(B, T, seed=7)
+    ref = O.dit_forward(z, cond, sd)[:, -1]
+    v_full = torch.empty(B, H.N_PATCHES, H.OUT_DIM, device=DEV)
+    E.dit_forward(dw, z.to(DEV), cond.to(DEV), v_full, E.workspace(E.dit_workspace_bytes(B, T), DEV))
+    Tp = T - 1
+    ws = E.workspace(E.dit_workspace_bytes(B, max(Tp, 1)), DEV)
+    cache = E.kv_cache(B, Tp, DEV) if Tp else None
+    if Tp:
+        E.dit_precompute_past(dw, z[:, :Tp].contiguous().to(DEV), cond[:, :Tp].contiguous().to(DEV), cache, ws)
+    v = torch.empty(B, H.N_PATCHES, H.OUT_DIM, device=DEV)
+    E.dit_forward_current(dw, z[:, Tp].contiguous().to(DEV), cond[:, Tp].contiguous().to(DEV), cache, Tp, v, ws)
+    torch.cuda.synchronize()
+    assert rel_l2(v, v_full) < 1e-4, rel_l2(v, v_full)
+    assert rel_l2(v, ref) < REL_L2_TOL and cosine(v, ref) > COS_TOL
+
+
+@pytest.mark.parametrize("B,T", [(2, 3), (1, 2)])
+def test_generate_frame_kv_matches_full_T(dit_full, vae_full, B, T):
+    """C3-style frame through oasis_generate_frame_kv equals oasis_generate_frame
+    and the oracle (every step's chunk and the decoded frame)."""
+    dsd, dw = dit_full
+    vsd, vw = vae_full
+    chunk, ctx_z, conds, steps = _frame_inputs(dsd, B, T, seed=8)
+    out = {}
+    for kv in (False, True):
+        fe = E.FrameEngine(dw, vw, B, T, steps, kv=kv)
+        fe.context_z.copy_(ctx_z)
+        for i, c in enumerate(conds):
+            fe.cond[i].copy_(c)
+        fe.chunk.copy_(chunk)
+        fe.run()
+        torch.cuda.synchronize()
+        out[kv] = (fe.chunk.clone(), fe.image.clone())
+    assert rel_l2(out[True][0], out[False][0]) < 1e-3
+    assert rel_l2(out[True][1], out[False][1]) < 1e-3
+    c_ref = chunk.clone()
+    for i, st in enumerate(steps):
+        c_ref, _ = O.ddim_step(c_ref, ctx_z, conds[i], st.at_sqrt ** 2, st.an_sqrt ** 2, dsd)
+    img_ref = O.vae_decode(O.bridge(c_ref), vsd)
+    assert rel_l2(out[True][0], c_ref) < REL_L2_TOL
+    assert rel_l2(out[True][1], img_ref) < REL_L2_TOL and cosine(out[True][1], img_ref) > COS_TOL
+
+
+def test_dropin_kv_functions(dit_small):
+    """oasis_inference.precompute_past_state / dit_forward_currentonly under the
+    reference's names give dit_forward_device's last-frame rows."""
+    from oasis_b200 import oasis_inference as OI
+
+    sd, dw = dit_small
+    T = 2
+    z, cond = _inputs(1, T, seed=9)
+    scr = OI.prealloc_scratch(DEV, n_frames=T)
+    full = OI.dit_forward_device(z.reshape(-1, H.D_MODEL).to(DEV), [c for c in cond[0].to(DEV)], dw, scr)
+    OI.precompute_past_state(z[0, 0].to(DEV), cond[0, 0].to(DEV), dw, scr)
+    v = OI.dit_forward_currentonly(z[0, 1].to(DEV), cond[0, 1].to(DEV), dw, scr)
+    torch.cuda.synchronize()
+    assert rel_l2(v, full[H.N_PATCHES:]) < 1e-4
