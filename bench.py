@@ -284,11 +284,46 @@ def latency_extras(dw, vw, peaks):
     dit_bytes = sum(t.numel() * t.element_size() for blk in dw.tensors.values() for t in blk.values())
     dit_bytes += dw.adaln_w.numel() * 2 + dw.final_w.numel() * 2
     ms_step = ms_steps / 4
+    del fe
+    fk = E.FrameEngine(dw, vw, 1, 2, kv=True)
+    make_inputs(fk, dw, 0, 1, 2)
+    fk.capture()
+    for _ in range(3):
+        fk.replay()
+    torch.cuda.synchronize()
+    ms_kv = time_graph(fk.replay, k) / k
+    del fk
     out = {"c3_ms_per_frame": round(ms_frame, 3), "c3_frames_per_sec": round(1000 / ms_frame, 1),
+           "c3_kv_ms_per_frame": round(ms_kv, 3),
            "c2_ms_per_dit_step": round(ms_step, 3),
            "c2_weight_stream_gbs": round(dit_bytes / (ms_step / 1000) / 1e9, 1),
            "c2_hbm_floor_ms": round(dit_bytes / (peaks["hbm_gbs"] * 1e9) * 1000, 3)}
+    return out
+
+
+def kv_frame(dw, vw, sess0, B, T, steps, PAR, sessions):
+    """The same frames with the context rows run once per frame
+    (oasis_generate_frame_kv, the reference's default KV-cache path): its own
+    FLOP count, reported beside the full-T number, never mixed into it."""
+    from oasis_b200 import engine as E
+
+    fe = E.FrameEngine(dw, vw, B, T, kv=True)
+    make_inputs(fe, dw, sess0, B, T)
+    fe.capture()
+    for _ in range(3):
+        fe.replay()
+    torch.cuda.synchronize()
+    PAR.barrier()
+    ms = PAR.max_over_ranks(time_graph(fe.replay, steps))
+    # context pass once (T-1 frames) + 4 steps over the generated frame (DiT), per frame
+    Tp = T - 1
+    ctx = B * Tp * 144 * 805.31e6 + B * Tp * 406.85e6 + B * Tp * 1.359e9 + B * 4.72e6 * Tp * T
+    cur = 4 * (B * 144 * 805.31e6 + B * 406.85e6 + B * 1.359e9 + B * 4.72e6 * 2 * T)
+    out = {"frames_per_sec": round(sessions * steps / (ms / 1000.0), 3), "ms_per_frame": round(ms / steps, 3),
+           "dit_tflop_per_frame_gpu": round((ctx + cur) / 1e12, 2),
+           "path": "oasis_generate_frame_kv: context rows once per frame, generated frame per DDIM step"}
     del fe
+    torch.cuda.empty_cache()
     return out
 
 
@@ -435,6 +470,7 @@ def main():
     e2e_value = args.sessions * args.steps / (PAR.max_over_ranks(ev[0].elapsed_time(ev[2])) / 1000.0)
 
     roof = gemm_roofline(B * T * 144, 10, peaks)
+    kv = kv_frame(dw, vw, sess0, B, T, args.steps, PAR, args.sessions)
     c5 = None if args.no_extras else c5_compare(rank, world, dev, PAR)
     extras, cpu = {}, None
     if rank == 0 and world == 1 and not args.no_extras:
@@ -459,7 +495,7 @@ def main():
             "clocks": clk,
             "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": int(launches_per_frame * args.steps),
-            "roofline": roof, "cpu_baseline": cpu, **extras, "c5_tp_vs_dp": c5,
+            "roofline": roof, "cpu_baseline": cpu, "kv_cache": kv, **extras, "c5_tp_vs_dp": c5,
         }
         emit(line)
     if dist.is_initialized():
