@@ -31,7 +31,11 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int kEpiWarps = 8;                 // two per TMEM lane quarter
+#ifndef OASIS_EPI_WARPS
+#define OASIS_EPI_WARPS 8
+#endif
+constexpr int kEpiWarps = OASIS_EPI_WARPS;     // kGroups per TMEM lane quarter
+constexpr int kGroups = kEpiWarps / 4;
 constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer + MMA + epilogue
 constexpr int kStgBytes = 32 * 128;          // per-warp store staging: 32 rows x 128 B
 
@@ -40,7 +44,7 @@ struct Cfg {
   // Two staging buffers per epilogue warp (the store of one chunk overlaps the
   // next; residual tiles are TMA-loaded into them ahead of time). Measured on
   // B200: worth a pipeline stage even at BN = 256.
-  static constexpr int NBUF = 2;
+  static constexpr int NBUF = kEpiWarps >= 16 ? 1 : 2;
   // Narrow tiles load two 64-wide K atoms per TMA instruction (a stage covers
   // K = 128): the per-instruction cost, not bytes, bounds small-M GEMMs.
   static constexpr int KA = BN <= 128 ? 2 : 1;
@@ -55,6 +59,19 @@ struct Cfg {
   static constexpr int BAR_BYTES = 512;
   static constexpr int SMEM = 1024 /*align slack*/ + STAGES * STAGE_BYTES + STG_BYTES + BAR_BYTES;
 };
+
+#ifdef OASIS_GEMM_PROF
+// Diagnostic build only: cycles each role spends waiting, summed over CTAs.
+// [0] MMA on acc_empty, [1] MMA on full, [2] producer on empty, [3] epilogue on
+// acc_full, [4] MMA loop total, [5] epilogue loop total.
+__device__ unsigned long long g_gemm_prof[8];
+#define PROF_T0() const long long _pt0 = clock64()
+#define PROF_ADD(i) \
+  if ((threadIdx.x & 31) == 0) atomicAdd(&g_gemm_prof[i], (unsigned long long)(clock64() - _pt0))
+#else
+#define PROF_T0()
+#define PROF_ADD(i)
+#endif
 
 struct SplitK {
   float* partials;  // [tiles][splits][BM][BN]
@@ -210,7 +227,13 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& e, const SplitK& 
   const bool resid = reads_resid(e.mode) && sk.splits == 1;  // fp32 modes: W == 32
   float4 rcur[8];
   if (resid && half < nchunks && n0 + half * W < N) load_resid(e, r, n0 + half * W, M, rcur);
-  if (!mbar_wait(acc_bar, acc_parity, kDevTimeoutAccFull)) {
+  bool acc_ready;
+  {
+    PROF_T0();
+    acc_ready = mbar_wait(acc_bar, acc_parity, kDevTimeoutAccFull);
+    PROF_ADD(3);
+  }
+  if (!acc_ready) {
     ok = false;
     return;
   }
@@ -218,11 +241,11 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& e, const SplitK& 
   float* part = nullptr;
   if (sk.splits > 1) part = sk.partials + ((long long)tile * sk.splits + split) * (BM * BN) + (quarter * 32 + lane) * BN;
 #pragma unroll 1
-  for (int c = half; c < nchunks; c += 2) {
+  for (int c = half; c < nchunks; c += kGroups) {
     const int nb = n0 + c * W;
     if (sk.splits == 1 && nb >= N) break;  // warp-uniform
     float4 rnext[8];
-    if (resid && c + 2 < nchunks && nb + 2 * W < N) load_resid(e, r, nb + 2 * W, M, rnext);
+    if (resid && c + kGroups < nchunks && nb + kGroups * W < N) load_resid(e, r, nb + kGroups * W, M, rnext);
     uint8_t* buf = stg + sbuf * kStgBytes;
     if (sk.splits == 1 && e.mode != kEpiImage) stage_begin(lane, nbuf);
 #pragma unroll 1
@@ -261,31 +284,37 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& e, const SplitK& 
 // the accumulator is ready, later ones as soon as a buffer's store has read it),
 // the result is computed in place and TMA-stored from the same buffer.
 __device__ __forceinline__ void epilogue_tile_resid(const EpiParams& e, const CUtensorMap* tm_out,
-                                                    const CUtensorMap* tm_res, uint8_t* stg, uint64_t* rbar,
+                                                    const CUtensorMap* tm_res, uint8_t* stg, int nbuf, uint64_t* rbar,
                                                     uint32_t& rphase, uint32_t t_acc, int M, int N, int BN, int m0q,
                                                     int n0, int half, int lane, uint64_t* acc_bar,
                                                     uint32_t acc_parity, bool& ok) {
   const int r = m0q + lane;
   const int nchunks = BN / 32;
-  int mine = 0;  // this warp's chunks: c = half + 2 i, i < mine
-  while (half + 2 * mine < nchunks && n0 + (half + 2 * mine) * 32 < N) ++mine;
+  int mine = 0;  // this warp's chunks: c = half + kGroups i, i < mine
+  while (half + kGroups * mine < nchunks && n0 + (half + kGroups * mine) * 32 < N) ++mine;
   if (lane == 0) {
     bulk_wait_read0();  // earlier stores no longer read the buffers
-    for (int i = 0; i < 2 && i < mine; ++i) {
+    for (int i = 0; i < nbuf && i < mine; ++i) {
       mbar_arrive_expect_tx(&rbar[i], kStgBytes);
-      tma_load_2d(stg + i * kStgBytes, tm_res, &rbar[i], n0 + (half + 2 * i) * 32, m0q);
+      tma_load_2d(stg + i * kStgBytes, tm_res, &rbar[i], n0 + (half + kGroups * i) * 32, m0q);
     }
   }
   __syncwarp();
-  if (!mbar_wait(acc_bar, acc_parity, kDevTimeoutAccFull)) {
+  bool acc_ready;
+  {
+    PROF_T0();
+    acc_ready = mbar_wait(acc_bar, acc_parity, kDevTimeoutAccFull);
+    PROF_ADD(3);
+  }
+  if (!acc_ready) {
     ok = false;
     return;
   }
   tc_fence_after();
 #pragma unroll 1
   for (int i = 0; i < mine; ++i) {
-    const int b = i & 1;
-    const int c = half + 2 * i;
+    const int b = i % nbuf;
+    const int c = half + kGroups * i;
     const int nb = n0 + c * 32;
     uint8_t* buf = stg + b * kStgBytes;
     float4 gate[8];  // issued before the waits so its latency overlaps them
@@ -309,11 +338,11 @@ __device__ __forceinline__ void epilogue_tile_resid(const EpiParams& e, const CU
     epilogue_math(e, r, nb, v, res, e.mode == kEpiGatedResid ? gate : nullptr);
     stage_write(buf, lane, false, 0, v);
     stage_commit(tm_out, buf, lane, m0q, nb);
-    if (i + 2 < mine) {  // refill this buffer with chunk i + 2 once the store has read it
+    if (i + nbuf < mine) {  // refill this buffer with chunk i + nbuf once the store has read it
       if (lane == 0) {
         bulk_wait_read0();
         mbar_arrive_expect_tx(&rbar[b], kStgBytes);
-        tma_load_2d(buf, tm_res, &rbar[b], n0 + (c + 4) * 32, m0q);
+        tma_load_2d(buf, tm_res, &rbar[b], n0 + (c + nbuf * kGroups) * 32, m0q);
       }
       __syncwarp();
     }
@@ -330,7 +359,7 @@ __device__ __forceinline__ void splitk_reduce(const EpiParams& e, const SplitK& 
   const float* base = sk.partials + (long long)tile * sk.splits * (BM * BN) + (quarter * 32 + lane) * BN;
   const int nchunks = BN / W;
 #pragma unroll 1
-  for (int c = half; c < nchunks; c += 2) {
+  for (int c = half; c < nchunks; c += kGroups) {
     const int nb = n0 + c * W;
     if (nb >= N) break;
     if (e.mode != kEpiImage) stage_begin(lane, 1);
@@ -359,6 +388,7 @@ __device__ __forceinline__ void splitk_reduce(const EpiParams& e, const SplitK& 
     if (e.mode != kEpiImage) stage_commit(tm_out, stg, lane, m0q, nb);
   }
 }
+
 
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -453,7 +483,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (u == (int)blockIdx.x && kb - kb0 < pre) {
             load_a(sa, &full[stage], kb, m0);  // W already in flight
           } else {
-            if (!mbar_wait(&empty[stage], phase ^ 1, kDevTimeoutSmemEmpty)) { ok = false; break; }
+            bool got;
+            {
+              PROF_T0();
+              got = mbar_wait(&empty[stage], phase ^ 1, kDevTimeoutSmemEmpty);
+              PROF_ADD(2);
+            }
+            if (!got) { ok = false; break; }
             mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
             load_a(sa, &full[stage], kb, m0);
             load_w(sa + C::A_BYTES, &full[stage], kb, n0);
@@ -471,12 +507,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
+#ifdef OASIS_GEMM_PROF
+      const long long loop_t0 = clock64();
+#endif
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, kDevTimeoutAccEmpty)) break;
+        bool got;
+        {
+          PROF_T0();
+          got = mbar_wait(&acc_empty[acc], acc_phase ^ 1, kDevTimeoutAccEmpty);
+          PROF_ADD(0);
+        }
+        if (!got) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = 0; kb < kb_per_split; ++kb) {
-          if (!mbar_wait(&full[stage], phase, kDevTimeoutTmaFull)) { ok = false; break; }
+          {
+            PROF_T0();
+            got = mbar_wait(&full[stage], phase, kDevTimeoutTmaFull);
+            PROF_ADD(1);
+          }
+          if (!got) { ok = false; break; }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smem + stage * C::STAGE_BYTES);
 #pragma unroll
@@ -497,6 +547,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1;
       }
+#ifdef OASIS_GEMM_PROF
+      atomicAdd(&g_gemm_prof[4], (unsigned long long)(clock64() - loop_t0));
+#endif
     }
   } else {
     // ---------------- Epilogue (warps 2..9) ----------------
@@ -509,7 +562,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     uint8_t* stg = staging + (warp - 2) * kStgBytes * C::NBUF;
     uint64_t* my_rbar = rbar + 2 * (warp - 2);
-    const bool resid_tma = C::NBUF == 2 && reads_resid(epi.mode) && splits == 1;
+    const bool resid_tma = reads_resid(epi.mode) && splits == 1;
     int sbuf = 0;
     uint32_t rphase = 0;
     const int ep_tid = threadIdx.x - 64;
@@ -521,7 +574,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m0q = (tile / n_tiles) * BM + quarter * 32, n0 = (tile % n_tiles) * BN;
       const uint32_t t_acc = tmem_base + lane_off + acc * BN;
       if (resid_tma)
-        epilogue_tile_resid(epi, &tmO, &tmR, stg, my_rbar, rphase, t_acc, M, N, BN, m0q, n0, half, lane,
+        epilogue_tile_resid(epi, &tmO, &tmR, stg, C::NBUF, my_rbar, rphase, t_acc, M, N, BN, m0q, n0, half, lane,
                             &acc_full[acc], acc_phase, ok);
       else
         epilogue_tile(epi, sk, &tmO, stg, C::NBUF, sbuf, t_acc, M, N, BN, m0q, n0, tile, split, quarter, half,
@@ -697,6 +750,17 @@ int num_sms() {
   }
   return g_num_sms[dev & 63];
 }
+
+#ifdef OASIS_GEMM_PROF
+extern "C" int oasis_debug_gemm_prof(unsigned long long* out8, int reset) {
+  cudaMemcpyFromSymbol(out8, g_gemm_prof, sizeof(g_gemm_prof));
+  if (reset) {
+    unsigned long long z[8] = {0};
+    cudaMemcpyToSymbol(g_gemm_prof, z, sizeof(z));
+  }
+  return 0;
+}
+#endif
 
 size_t gemm_workspace_bytes(int M, int N, int K) {
   Plan pl = choose_plan(M, N, K);
