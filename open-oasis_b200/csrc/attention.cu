@@ -12,10 +12,12 @@
 //   Flash-style: K/V tiles of 64 keys staged in swizzled shared memory with
 //   cp.async double buffering, online softmax in fp32, bf16 mma.sync m16n8k16.
 // attention_temporal: causal softmax over the T frames of one session, per
-//   (patch, head). One warp per problem, lane = 2 of the 64 head dims, q/k/v for
-//   all frames held in registers, scores reduced with warp shuffles.
-// attention_temporal_cached: the same for only the generated frame's query, with
-//   the context frames' keys/values read from a cache written once per frame.
+//   (patch, head). A warp covers 256 columns (four heads) of one (session,
+//   patch), 16 bytes per lane per row, so every q/k/v access is a coalesced
+//   512-byte run; T <= 8 holds all frames in registers, longer T shares key
+//   loads across blocks of four queries with an online softmax.
+// attention_temporal_cached: the generated frame's query only, with the context
+//   frames' keys/values read from a cache written once per frame.
 #include "common.cuh"
 #include "pointwise.cuh"
 #include "status.h"
@@ -352,128 +354,253 @@ __global__ void __launch_bounds__(kSpatialWarps * 32, 1)
 }
 
 // One warp per (session, patch, head); lane owns head dims 2*lane, 2*lane+1.
+
+// Causal temporal attention for T <= TMAX <= 8 in the lane-per-columns layout
+// of the cached kernel below (a warp covers 256 columns = four heads of one
+// (session, patch), lane l the 8 columns [8 l, 8 l + 8)): every frame's q, k and
+// v segments are loaded up front as 16-byte packets (3 T loads per lane, whole
+// 512-byte runs per warp), then each query's scores over the earlier frames are
+// reduced across the 8 lanes of its head with three shuffles.
 template <int TMAX>
-__global__ void __launch_bounds__(256) attention_temporal_kernel(const __nv_bfloat16* __restrict__ qkv,
-                                                                 __nv_bfloat16* __restrict__ out, int batch,
-                                                                 int T, int P, int H) {
+__global__ void __launch_bounds__(256) attention_temporal_rows_kernel(const __nv_bfloat16* __restrict__ qkv,
+                                                                      __nv_bfloat16* __restrict__ out, int batch,
+                                                                      int T, int P, int H);
+
+// Context-cached temporal attention: the one query of the generated frame
+// (position Tp) of each (session, patch) against the cached keys/values of the
+// Tp context frames plus its own. past: packed QKV rows of the context frames,
+// [B, Tp, P, 3 H 64]; cur: packed QKV rows of the generated frame,
+// [B, P, 3 H 64]; out: [B, P, H 64]. The causal mask admits every key.
+//
+// Lane-per-columns layout: a warp covers 256 consecutive columns of the q, k and
+// v sections (four heads), lane l the 8 columns [8 l, 8 l + 8) (one 16-byte load
+// per row and section), so a key row's K and V segments are read as whole
+// coalesced 512-byte runs; the 8 lanes of a head combine their partial dot
+// products with three shuffles. Online softmax over the keys; the next key row
+// is loaded while the current one is used.
+constexpr int kCachedCols = 8;                 // columns per lane
+constexpr int kCachedWarpCols = 32 * kCachedCols;
+
+__device__ __forceinline__ void bf16x8_to_f32(const uint4& r, float (&f)[8]) {
+  const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[j]));
+    f[2 * j] = t.x;
+    f[2 * j + 1] = t.y;
+  }
+}
+
+__global__ void __launch_bounds__(256) attention_temporal_cached_kernel(const __nv_bfloat16* __restrict__ past,
+                                                                        const __nv_bfloat16* __restrict__ cur,
+                                                                        __nv_bfloat16* __restrict__ out, int batch,
+                                                                        int Tp, int P, int H) {
   pdl_trigger();
   pdl_wait();
+  const int HD = H * kDh, ld = 3 * HD;
+  const int wpr = (HD + kCachedWarpCols - 1) / kCachedWarpCols;  // warps per (session, patch)
   const long long w = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  const int kQkvLd = 3 * H * kDh, kOutLd = H * kDh;
-  const long long total = (long long)batch * P * H;
-  if (w >= total) return;
-  const int head = w % H;
-  const long long bp = w / H;
+  if (w >= (long long)batch * P * wpr) return;  // warp-uniform
+  const long long bp = w / wpr;
+  const int part = (int)(w - bp * wpr);
   const int p = bp % P;
   const long long b = bp / P;
-  const long long row0 = b * T * P + p;  // row of frame t = row0 + t * P
-  const int col = head * kDh + 2 * lane;
-
-  // all loads first: q, k, v of every frame (independent 128-byte row segments)
-  __nv_bfloat162 qr[TMAX], kr[TMAX], vr[TMAX];
+  int col = part * kCachedWarpCols + kCachedCols * lane;
+  const bool active = col < HD;  // whole heads are active or idle together
+  if (!active) col = 0;
+  const __nv_bfloat16* crow = cur + bp * ld;
+  float q[8];
+  bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(crow + col)), q);
 #pragma unroll
-  for (int s = 0; s < TMAX; ++s) {
-    if (s < T) {
-      const __nv_bfloat16* rp = qkv + (row0 + (long long)s * P) * kQkvLd + col;
-      qr[s] = *reinterpret_cast<const __nv_bfloat162*>(rp);
-      kr[s] = *reinterpret_cast<const __nv_bfloat162*>(rp + kOutLd);
-      vr[s] = *reinterpret_cast<const __nv_bfloat162*>(rp + 2 * kOutLd);
+  for (int i = 0; i < 8; ++i) q[i] *= 0.125f * 1.4426950408889634f;  // 1/sqrt(64), log2 units
+  auto key_row = [&](int t) -> const __nv_bfloat16* {
+    return t < Tp ? past + ((b * Tp + t) * P + p) * ld : crow;
+  };
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  float mx = -INFINITY, l = 0.f;
+  uint4 kc = __ldg(reinterpret_cast<const uint4*>(key_row(0) + HD + col));
+  uint4 vc = __ldg(reinterpret_cast<const uint4*>(key_row(0) + 2 * HD + col));
+  for (int t = 0; t <= Tp; ++t) {
+    uint4 kn = kc, vn = vc;
+    if (t < Tp) {
+      const __nv_bfloat16* nr = key_row(t + 1);
+      kn = __ldg(reinterpret_cast<const uint4*>(nr + HD + col));
+      vn = __ldg(reinterpret_cast<const uint4*>(nr + 2 * HD + col));
+    }
+    float k[8], v[8];
+    bf16x8_to_f32(kc, k);
+    float sc = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) sc = fmaf(q[i], k[i], sc);
+    sc += __shfl_xor_sync(0xffffffffu, sc, 1);
+    sc += __shfl_xor_sync(0xffffffffu, sc, 2);
+    sc += __shfl_xor_sync(0xffffffffu, sc, 4);
+    const float mnew = fmaxf(mx, sc);
+    const float corr = exp2f(mx - mnew);  // 0 on the first key
+    const float e = exp2f(sc - mnew);
+    l = l * corr + e;
+    mx = mnew;
+    bf16x8_to_f32(vc, v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = fmaf(e, v[i], acc[i] * corr);
+    kc = kn;
+    vc = vn;
+  }
+  if (active) {
+    const float inv = 1.f / l;
+    *reinterpret_cast<uint4*>(out + bp * HD + col) =
+        make_uint4(pack_bf16x2(acc[0] * inv, acc[1] * inv), pack_bf16x2(acc[2] * inv, acc[3] * inv),
+                   pack_bf16x2(acc[4] * inv, acc[5] * inv), pack_bf16x2(acc[6] * inv, acc[7] * inv));
+  }
+}
+
+template <int TMAX>
+__global__ void __launch_bounds__(256) attention_temporal_rows_kernel(const __nv_bfloat16* __restrict__ qkv,
+                                                                      __nv_bfloat16* __restrict__ out, int batch,
+                                                                      int T, int P, int H) {
+  pdl_trigger();
+  pdl_wait();
+  const int HD = H * kDh, ld = 3 * HD;
+  const int wpr = (HD + kCachedWarpCols - 1) / kCachedWarpCols;
+  const long long w = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= (long long)batch * P * wpr) return;  // warp-uniform
+  const long long bp = w / wpr;
+  const int part = (int)(w - bp * wpr);
+  const int p = bp % P;
+  const long long b = bp / P;
+  int col = part * kCachedWarpCols + kCachedCols * lane;
+  const bool active = col < HD;
+  if (!active) col = 0;
+  const __nv_bfloat16* base = qkv + (b * T * P + p) * ld + col;  // frame t: + t P ld
+  uint4 qr[TMAX], kr[TMAX], vr[TMAX];
+#pragma unroll
+  for (int t = 0; t < TMAX; ++t) {
+    if (t < T) {
+      const __nv_bfloat16* rp = base + (long long)t * P * ld;
+      qr[t] = __ldg(reinterpret_cast<const uint4*>(rp));
+      kr[t] = __ldg(reinterpret_cast<const uint4*>(rp + HD));
+      vr[t] = __ldg(reinterpret_cast<const uint4*>(rp + 2 * HD));
     }
   }
-  const float sc = 0.125f * 1.4426950408889634f;
+  __nv_bfloat16* obase = out + (b * T * P + p) * (long long)HD + col;
 #pragma unroll
   for (int tq = 0; tq < TMAX; ++tq) {
     if (tq < T) {
-      const float2 q = __bfloat1622float2(qr[tq]);
-      float sc_[TMAX];
+      float q[8];
+      bf16x8_to_f32(qr[tq], q);
+      float sc[TMAX];
       float mx = -INFINITY;
 #pragma unroll
-      for (int s = 0; s <= tq; ++s) {
-        const float2 k = __bfloat1622float2(kr[s]);
-        float d = q.x * k.x + q.y * k.y;
+      for (int s2 = 0; s2 <= tq; ++s2) {
+        float k[8];
+        bf16x8_to_f32(kr[s2], k);
+        float d = 0.f;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-        sc_[s] = d * sc;
-        mx = fmaxf(mx, sc_[s]);
+        for (int i = 0; i < 8; ++i) d = fmaf(q[i], k[i], d);
+        d += __shfl_xor_sync(0xffffffffu, d, 1);
+        d += __shfl_xor_sync(0xffffffffu, d, 2);
+        d += __shfl_xor_sync(0xffffffffu, d, 4);
+        sc[s2] = d * (0.125f * 1.4426950408889634f);
+        mx = fmaxf(mx, sc[s2]);
       }
-      float l = 0.f, o0 = 0.f, o1 = 0.f;
+      float acc[8], l = 0.f;
 #pragma unroll
-      for (int s = 0; s <= tq; ++s) {
-        const float e = exp2f(sc_[s] - mx);
-        const float2 v = __bfloat1622float2(vr[s]);
+      for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+#pragma unroll
+      for (int s2 = 0; s2 <= tq; ++s2) {
+        const float e = exp2f(sc[s2] - mx);
+        float v[8];
+        bf16x8_to_f32(vr[s2], v);
         l += e;
-        o0 = fmaf(e, v.x, o0);
-        o1 = fmaf(e, v.y, o1);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = fmaf(e, v[i], acc[i]);
       }
-      const float inv = 1.f / l;
-      *reinterpret_cast<uint32_t*>(out + (row0 + (long long)tq * P) * kOutLd + col) = pack_bf16x2(o0 * inv, o1 * inv);
+      if (active) {
+        const float inv = 1.f / l;
+        *reinterpret_cast<uint4*>(obase + (long long)tq * P * HD) =
+            make_uint4(pack_bf16x2(acc[0] * inv, acc[1] * inv), pack_bf16x2(acc[2] * inv, acc[3] * inv),
+                       pack_bf16x2(acc[4] * inv, acc[5] * inv), pack_bf16x2(acc[6] * inv, acc[7] * inv));
+      }
     }
   }
 }
 
-// Context-cached temporal attention: the one query of the generated frame
-// (position Tp) of each (session, patch, head) against the cached keys/values
-// of the Tp context frames plus its own. past: packed QKV rows of the context
-// frames, [B, Tp, P, 3 H 64]; cur: packed QKV rows of the generated frame,
-// [B, P, 3 H 64]; out: [B, P, H 64]. The causal mask admits every key here.
-template <int TMAX>
-__global__ void __launch_bounds__(256) attention_temporal_cached_kernel(
-    const __nv_bfloat16* __restrict__ past, const __nv_bfloat16* __restrict__ cur, __nv_bfloat16* __restrict__ out,
-    int batch, int Tp, int P, int H) {
+// The same layout for any T <= 32: queries in blocks of four share each key
+// row's loads (online softmax per query, keys past a query masked), so a
+// (session, patch) reads its key rows about T / 8 times instead of T / 2.
+__global__ void __launch_bounds__(128) attention_temporal_rows_long_kernel(const __nv_bfloat16* __restrict__ qkv,
+                                                                           __nv_bfloat16* __restrict__ out,
+                                                                           int batch, int T, int P, int H) {
   pdl_trigger();
   pdl_wait();
+  constexpr int QB = 4;
+  const int HD = H * kDh, ld = 3 * HD;
+  const int wpr = (HD + kCachedWarpCols - 1) / kCachedWarpCols;
   const long long w = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  const int kQkvLd = 3 * H * kDh, kOutLd = H * kDh;
-  const long long total = (long long)batch * P * H;
-  if (w >= total) return;
-  const int head = w % H;
-  const long long bp = w / H;
+  if (w >= (long long)batch * P * wpr) return;  // warp-uniform
+  const long long bp = w / wpr;
+  const int part = (int)(w - bp * wpr);
   const int p = bp % P;
   const long long b = bp / P;
-  const int col = head * kDh + 2 * lane;
-  const __nv_bfloat16* cp = cur + bp * kQkvLd + col;
-  const float2 q = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(cp));
-  __nv_bfloat162 kr[TMAX], vr[TMAX];
+  int col = part * kCachedWarpCols + kCachedCols * lane;
+  const bool active = col < HD;
+  if (!active) col = 0;
+  const __nv_bfloat16* base = qkv + (b * T * P + p) * ld + col;
+  __nv_bfloat16* obase = out + (b * T * P + p) * (long long)HD + col;
+  const long long fstride = (long long)P * ld;
+  for (int t0 = 0; t0 < T; t0 += QB) {
+    float q[QB][8], acc[QB][8], mx[QB], l[QB];
 #pragma unroll
-  for (int s = 0; s < TMAX; ++s) {
-    if (s < Tp) {
-      const __nv_bfloat16* rp = past + ((b * Tp + s) * P + p) * kQkvLd + col + kOutLd;
-      kr[s] = *reinterpret_cast<const __nv_bfloat162*>(rp);
-      vr[s] = *reinterpret_cast<const __nv_bfloat162*>(rp + kOutLd);
-    } else if (s == Tp) {
-      kr[s] = *reinterpret_cast<const __nv_bfloat162*>(cp + kOutLd);
-      vr[s] = *reinterpret_cast<const __nv_bfloat162*>(cp + 2 * kOutLd);
+    for (int j = 0; j < QB; ++j) {
+      const int tq = t0 + j < T ? t0 + j : T - 1;
+      bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(base + tq * fstride)), q[j]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        q[j][i] *= 0.125f * 1.4426950408889634f;
+        acc[j][i] = 0.f;
+      }
+      mx[j] = -INFINITY;
+      l[j] = 0.f;
+    }
+    const int last = t0 + QB - 1 < T - 1 ? t0 + QB - 1 : T - 1;
+    for (int s2 = 0; s2 <= last; ++s2) {
+      float k[8], v[8];
+      bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(base + s2 * fstride + HD)), k);
+      bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(base + s2 * fstride + 2 * HD)), v);
+#pragma unroll
+      for (int j = 0; j < QB; ++j) {
+        float d = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) d = fmaf(q[j][i], k[i], d);
+        d += __shfl_xor_sync(0xffffffffu, d, 1);
+        d += __shfl_xor_sync(0xffffffffu, d, 2);
+        d += __shfl_xor_sync(0xffffffffu, d, 4);
+        if (s2 <= t0 + j) {  // causal
+          const float mnew = fmaxf(mx[j], d);
+          const float corr = exp2f(mx[j] - mnew);
+          const float e = exp2f(d - mnew);
+          l[j] = l[j] * corr + e;
+          mx[j] = mnew;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[j][i] = fmaf(e, v[i], acc[j][i] * corr);
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < QB; ++j) {
+      if (active && t0 + j < T) {
+        const float inv = 1.f / l[j];
+        *reinterpret_cast<uint4*>(obase + (long long)(t0 + j) * P * HD) = make_uint4(
+            pack_bf16x2(acc[j][0] * inv, acc[j][1] * inv), pack_bf16x2(acc[j][2] * inv, acc[j][3] * inv),
+            pack_bf16x2(acc[j][4] * inv, acc[j][5] * inv), pack_bf16x2(acc[j][6] * inv, acc[j][7] * inv));
+      }
     }
   }
-  const float sc = 0.125f * 1.4426950408889634f;
-  float sc_[TMAX];
-  float mx = -INFINITY;
-#pragma unroll
-  for (int s = 0; s < TMAX; ++s) {
-    if (s <= Tp) {
-      const float2 k = __bfloat1622float2(kr[s]);
-      float d = q.x * k.x + q.y * k.y;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-      sc_[s] = d * sc;
-      mx = fmaxf(mx, sc_[s]);
-    }
-  }
-  float l = 0.f, o0 = 0.f, o1 = 0.f;
-#pragma unroll
-  for (int s = 0; s < TMAX; ++s) {
-    if (s <= Tp) {
-      const float e = exp2f(sc_[s] - mx);
-      const float2 v = __bfloat1622float2(vr[s]);
-      l += e;
-      o0 = fmaf(e, v.x, o0);
-      o1 = fmaf(e, v.y, o1);
-    }
-  }
-  const float inv = 1.f / l;
-  *reinterpret_cast<uint32_t*>(out + bp * kOutLd + col) = pack_bf16x2(o0 * inv, o1 * inv);
 }
 
 }  // namespace
@@ -484,20 +611,10 @@ int attention_temporal_cached_launch(const __nv_bfloat16* past, const __nv_bfloa
   OASIS_REQUIRE(past_frames >= 0 && past_frames <= 31, "attention_temporal_cached: past_frames=%d outside [0, 31]",
                 past_frames);
   OASIS_REQUIRE(H >= 1 && H <= 16, "attention_temporal_cached: heads=%d outside [1, 16]", H);
-  const long long warps = (long long)batch * P * H;
+  const long long warps = (long long)batch * P * ((H * kDh + kCachedWarpCols - 1) / kCachedWarpCols);
   if (warps == 0) return OASIS_OK;
   const int grid = (int)((warps * 32 + 255) / 256);
-  const int t = past_frames + 1;
-  if (t <= 2)
-    launch_pdl(attention_temporal_cached_kernel<2>, dim3(grid), dim3(256), 0, s, past, cur, out, batch, past_frames, P, H);
-  else if (t <= 4)
-    launch_pdl(attention_temporal_cached_kernel<4>, dim3(grid), dim3(256), 0, s, past, cur, out, batch, past_frames, P, H);
-  else if (t <= 8)
-    launch_pdl(attention_temporal_cached_kernel<8>, dim3(grid), dim3(256), 0, s, past, cur, out, batch, past_frames, P, H);
-  else if (t <= 16)
-    launch_pdl(attention_temporal_cached_kernel<16>, dim3(grid), dim3(256), 0, s, past, cur, out, batch, past_frames, P, H);
-  else
-    launch_pdl(attention_temporal_cached_kernel<32>, dim3(grid), dim3(256), 0, s, past, cur, out, batch, past_frames, P, H);
+  launch_pdl(attention_temporal_cached_kernel, dim3(grid), dim3(256), 0, s, past, cur, out, batch, past_frames, P, H);
   return check_launch("attention_temporal_cached_kernel");
 }
 
@@ -540,20 +657,18 @@ int attention_temporal_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, int 
   OASIS_REQUIRE(qkv && out, "attention_temporal: null pointer");
   OASIS_REQUIRE(frames >= 1 && frames <= 32, "attention_temporal: frames=%d outside [1, 32]", frames);
   OASIS_REQUIRE(H >= 1 && H <= 16, "attention_temporal: heads=%d outside [1, 16]", H);
-  const long long warps = (long long)batch * P * H;
+  const long long warps = (long long)batch * P * ((H * kDh + kCachedWarpCols - 1) / kCachedWarpCols);
   if (warps == 0) return OASIS_OK;
-  const int grid = (int)((warps * 32 + 255) / 256);
+  const int grid = (int)((warps * 32 + 127) / 128);  // 4-warp blocks
   if (frames <= 2)
-    launch_pdl(attention_temporal_kernel<2>, dim3(grid), dim3(256), 0, s, qkv, out, batch, frames, P, H);
+    launch_pdl(attention_temporal_rows_kernel<2>, dim3(grid), dim3(128), 0, s, qkv, out, batch, frames, P, H);
   else if (frames <= 4)
-    launch_pdl(attention_temporal_kernel<4>, dim3(grid), dim3(256), 0, s, qkv, out, batch, frames, P, H);
+    launch_pdl(attention_temporal_rows_kernel<4>, dim3(grid), dim3(128), 0, s, qkv, out, batch, frames, P, H);
   else if (frames <= 8)
-    launch_pdl(attention_temporal_kernel<8>, dim3(grid), dim3(256), 0, s, qkv, out, batch, frames, P, H);
-  else if (frames <= 16)
-    launch_pdl(attention_temporal_kernel<16>, dim3(grid), dim3(256), 0, s, qkv, out, batch, frames, P, H);
+    launch_pdl(attention_temporal_rows_kernel<8>, dim3(grid), dim3(128), 0, s, qkv, out, batch, frames, P, H);
   else
-    launch_pdl(attention_temporal_kernel<32>, dim3(grid), dim3(256), 0, s, qkv, out, batch, frames, P, H);
-  return check_launch("attention_temporal_kernel");
+    launch_pdl(attention_temporal_rows_long_kernel, dim3(grid), dim3(128), 0, s, qkv, out, batch, frames, P, H);
+  return check_launch("attention_temporal_rows_kernel");
 }
 
 }  // namespace oasis

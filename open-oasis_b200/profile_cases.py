@@ -4,6 +4,8 @@
     python open-oasis_b200/profile_cases.py attn_spatial --groups 512
     python open-oasis_b200/profile_cases.py attn_temporal --batch 64 --frames 8
     python open-oasis_b200/profile_cases.py layernorm --rows 73728
+    python open-oasis_b200/profile_cases.py attn_temporal_cached --batch 64 --frames 8
+    python open-oasis_b200/profile_cases.py frame --batch 64 --frames 8 [--kv] --reps 1
 
 Each case allocates only what the one kernel needs (a few GB at most), runs it
 `reps` times and exits, so an ncu capture with -k/-c ends by itself quickly.
@@ -65,6 +67,33 @@ def attn_temporal(a):
     return lambda: _lib.call("oasis_attention_temporal", qkv.data_ptr(), out.data_ptr(), a.batch, a.frames, 16, _st())
 
 
+def attn_temporal_cached(a):
+    P = 144
+    past = torch.randn(a.batch * (a.frames - 1) * P, 3072, device="cuda").to(torch.bfloat16)
+    cur = torch.randn(a.batch * P, 3072, device="cuda").to(torch.bfloat16)
+    out = torch.empty(a.batch * P, 1024, device="cuda", dtype=torch.bfloat16)
+    a._keep = (past, cur, out)
+    return lambda: _lib.call("oasis_attention_temporal_cached", past.data_ptr(), cur.data_ptr(), out.data_ptr(),
+                             a.batch, a.frames - 1, 16, _st())
+
+
+def frame(a):
+    """One whole frame (4 DDIM steps + VAE) for --batch sessions x --frames T,
+    full-T (default) or with the context rows cached (--kv)."""
+    from oasis_b200 import engine as E
+    from oasis_b200.weights import DitDeviceWeights, VaeDeviceWeights, init_dit_weights, init_vae_weights
+
+    dev = torch.device("cuda")
+    dw = DitDeviceWeights(init_dit_weights(seed=0), dev)
+    vw = VaeDeviceWeights(init_vae_weights(seed=0), dev)
+    fe = E.FrameEngine(dw, vw, a.batch, a.frames, kv=a.kv)
+    fe.chunk.normal_()
+    fe.context_z.normal_()
+    fe.cond.normal_()
+    a._keep = (dw, vw, fe)
+    return fe.run
+
+
 def layernorm(a):
     x = torch.randn(a.rows, 1024, device="cuda")
     y = torch.empty(a.rows, 1024, device="cuda", dtype=torch.bfloat16)
@@ -79,7 +108,8 @@ def layernorm(a):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["gemm", "attn_spatial", "attn_temporal", "layernorm"])
+    ap.add_argument("case", choices=["gemm", "attn_spatial", "attn_temporal", "attn_temporal_cached", "layernorm",
+                                     "frame"])
     ap.add_argument("--m", type=int, default=16384)
     ap.add_argument("--n", type=int, default=4096)
     ap.add_argument("--k", type=int, default=1024)
@@ -92,6 +122,7 @@ def main():
     ap.add_argument("--frames", type=int, default=8)
     ap.add_argument("--rows", type=int, default=73728)
     ap.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--kv", action="store_true", help="frame case: context rows cached")
     ap.add_argument("--time", action="store_true", help="print the mean time per launch (CUDA events)")
     a = ap.parse_args()
     launch = globals()[a.case](a)

@@ -247,23 +247,25 @@ def test_attention_temporal(B, T):
     assert rel_l2(out.float(), ref) < 1e-2
 
 
-@pytest.mark.parametrize("B,T", [(1, 1), (1, 2), (2, 8), (1, 32), (3, 5)])
-def test_attention_temporal_cached(B, T):
+@pytest.mark.parametrize("B,T,H", [(1, 1, 16), (1, 2, 16), (2, 8, 16), (1, 32, 16), (3, 5, 16), (2, 8, 8), (2, 3, 2),
+                                   (1, 4, 1)])
+def test_attention_temporal_cached(B, T, H):
     """The generated frame's query against cached context K/V equals the last
-    frame's rows of full causal temporal attention."""
-    P, Tp = 144, T - 1
-    qkv = rand_bf16(B * T * P, 3072, seed=B * 10 + T).reshape(B, T, P, 3072)
+    frame's rows of full causal temporal attention (H heads: 16, or 16 / n under
+    n-way tensor parallelism)."""
+    P, Tp, HD = 144, T - 1, H * 64
+    qkv = rand_bf16(B * T * P, 3 * HD, seed=B * 10 + T).reshape(B, T, P, 3 * HD)
     past = qkv[:, :Tp].contiguous()
     cur = qkv[:, Tp].contiguous()
-    out = torch.empty(B * P, 1024, device=DEV, dtype=torch.bfloat16)
+    out = torch.empty(B * P, HD, device=DEV, dtype=torch.bfloat16)
     _lib.call("oasis_attention_temporal_cached", past.data_ptr() if Tp else 0, cur.data_ptr(), out.data_ptr(), B, Tp,
-              16, _s())
-    full = torch.empty(B * T * P, 1024, device=DEV, dtype=torch.bfloat16)
-    _lib.call("oasis_attention_temporal", qkv.data_ptr(), full.data_ptr(), B, T, 16, _s())
+              H, _s())
+    full = torch.empty(B * T * P, HD, device=DEV, dtype=torch.bfloat16)
+    _lib.call("oasis_attention_temporal", qkv.data_ptr(), full.data_ptr(), B, T, H, _s())
     torch.cuda.synchronize()
-    assert rel_l2(out.reshape(B, P, 1024).float(), full.reshape(B, T, P, 1024)[:, Tp].float()) < 1e-3
-    x = qkv.float().reshape(B, T, P, 3, 16, 64).permute(3, 0, 2, 4, 1, 5)
-    ref = _attn_ref(x[0][..., Tp:, :], x[1], x[2], None).permute(0, 3, 1, 2, 4).reshape(B * P, 1024)
+    assert rel_l2(out.reshape(B, P, HD).float(), full.reshape(B, T, P, HD)[:, Tp].float()) < 1e-2
+    x = qkv.float().reshape(B, T, P, 3, H, 64).permute(3, 0, 2, 4, 1, 5)
+    ref = _attn_ref(x[0][..., Tp:, :], x[1], x[2], None).permute(0, 3, 1, 2, 4).reshape(B * P, HD)
     assert rel_l2(out.float(), ref) < 1e-2
 
 
