@@ -224,10 +224,11 @@ __global__ void __launch_bounds__(NW * 32) attention_full_kernel(const __nv_bflo
 
 // Spatial attention over exactly 144 tokens: one (frame, head) problem per CTA
 // iteration, persistent over problems. 9 warps x 16 query rows cover all 144
-// queries, so K and V are staged once per problem; the whole 16 x 144 score
-// strip of a warp stays in registers (single-pass softmax, no key tail: 144 =
-// 9 x 16). The next problem's q/k/v slices are prefetched into the other half of
-// a double buffer with cp.async while the current one is computed.
+// queries, so K and V are staged once per problem; a warp's 16 x 144 score strip
+// is computed in two key chunks (80 + 64, no key tail: 144 = 9 x 16) with an
+// online softmax, which keeps it under 112 registers so two CTAs share an SM.
+// The next problem's q/k/v slices are prefetched into the other half of a double
+// buffer with cp.async while the current one is computed.
 constexpr int kSpatialSeq = 144;
 constexpr int kSpatialWarps = 9;
 constexpr int kSpatialTile = kSpatialSeq * kDh;  // bf16 elements per q, k or v slice
@@ -243,7 +244,7 @@ __device__ __forceinline__ void spatial_prefetch(__nv_bfloat16* buf, const __nv_
   }
 }
 
-__global__ void __launch_bounds__(kSpatialWarps * 32, 1)
+__global__ void __launch_bounds__(kSpatialWarps * 32, 2)
     attention_spatial_kernel(const __nv_bfloat16* __restrict__ qkv, __nv_bfloat16* __restrict__ out, int items, int H) {
   pdl_trigger();
   pdl_wait();
@@ -272,58 +273,82 @@ __global__ void __launch_bounds__(kSpatialWarps * 32, 1)
       const int r = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
       ldsm_x4(qa[kk], sQ + swz(r, kk * 16 + (lane >> 4) * 8));
     }
-    float s[18][4];
-#pragma unroll
-    for (int i = 0; i < 18; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
-#pragma unroll
-    for (int np = 0; np < 9; ++np) {
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        uint32_t b[4];
-        const int m = lane >> 3;
-        ldsm_x4(b, sK + swz(np * 16 + (lane & 7) + (m >> 1) * 8, kk * 16 + (m & 1) * 8));
-        mma_bf16(s[2 * np], qa[kk], b[0], b[1]);
-        mma_bf16(s[2 * np + 1], qa[kk], b[2], b[3]);
-      }
-    }
-    float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-    for (int i = 0; i < 18; ++i) {
-      mx0 = fmaxf(mx0, fmaxf(s[i][0], s[i][1]));
-      mx1 = fmaxf(mx1, fmaxf(s[i][2], s[i][3]));
-    }
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-    const float o0 = mx0 * sc, o1 = mx1 * sc;
-    float l0 = 0.f, l1 = 0.f;
-#pragma unroll
-    for (int i = 0; i < 18; ++i) {
-      s[i][0] = exp2f(s[i][0] * sc - o0);
-      s[i][1] = exp2f(s[i][1] * sc - o0);
-      s[i][2] = exp2f(s[i][2] * sc - o1);
-      s[i][3] = exp2f(s[i][3] * sc - o1);
-      l0 += s[i][0] + s[i][1];
-      l1 += s[i][2] + s[i][3];
-    }
+    // keys in two chunks (80 + 64) with an online softmax: half the score
+    // registers of a single pass, so two CTAs fit on an SM
     float o[8][4];
 #pragma unroll
     for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
 #pragma unroll
-    for (int kk = 0; kk < 9; ++kk) {
-      uint32_t pa[4];
-      pa[0] = pack_bf16x2(s[2 * kk][0], s[2 * kk][1]);
-      pa[1] = pack_bf16x2(s[2 * kk][2], s[2 * kk][3]);
-      pa[2] = pack_bf16x2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-      pa[3] = pack_bf16x2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+    for (int ch = 0; ch < 2; ++ch) {
+      const int nb0 = ch == 0 ? 0 : 5, nbn = ch == 0 ? 5 : 4;  // 16-key blocks of this chunk
+      float s[10][4];
 #pragma unroll
-      for (int dp = 0; dp < 4; ++dp) {
-        uint32_t b[4];
-        const int m = lane >> 3;
-        ldsm_x4_t(b, sV + swz(kk * 16 + (lane & 7) + (m & 1) * 8, dp * 16 + (m >> 1) * 8));
-        mma_bf16(o[2 * dp], pa, b[0], b[1]);
-        mma_bf16(o[2 * dp + 1], pa, b[2], b[3]);
+      for (int i = 0; i < 10; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
+#pragma unroll
+      for (int nq = 0; nq < 5; ++nq) {
+        if (nq < nbn) {
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            uint32_t b[4];
+            const int m = lane >> 3;
+            ldsm_x4(b, sK + swz((nb0 + nq) * 16 + (lane & 7) + (m >> 1) * 8, kk * 16 + (m & 1) * 8));
+            mma_bf16(s[2 * nq], qa[kk], b[0], b[1]);
+            mma_bf16(s[2 * nq + 1], qa[kk], b[2], b[3]);
+          }
+        }
+      }
+      float mx0 = m0, mx1 = m1;
+#pragma unroll
+      for (int i = 0; i < 10; ++i) {
+        if (i < 2 * nbn) {
+          s[i][0] *= sc; s[i][1] *= sc; s[i][2] *= sc; s[i][3] *= sc;
+          mx0 = fmaxf(mx0, fmaxf(s[i][0], s[i][1]));
+          mx1 = fmaxf(mx1, fmaxf(s[i][2], s[i][3]));
+        }
+      }
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+      const float a0 = exp2f(m0 - mx0), a1 = exp2f(m1 - mx1);  // 0 on the first chunk
+      m0 = mx0;
+      m1 = mx1;
+      l0 *= a0;
+      l1 *= a1;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        o[i][0] *= a0; o[i][1] *= a0;
+        o[i][2] *= a1; o[i][3] *= a1;
+      }
+#pragma unroll
+      for (int i = 0; i < 10; ++i) {
+        if (i < 2 * nbn) {
+          s[i][0] = exp2f(s[i][0] - mx0);
+          s[i][1] = exp2f(s[i][1] - mx0);
+          s[i][2] = exp2f(s[i][2] - mx1);
+          s[i][3] = exp2f(s[i][3] - mx1);
+          l0 += s[i][0] + s[i][1];
+          l1 += s[i][2] + s[i][3];
+        }
+      }
+#pragma unroll
+      for (int kk = 0; kk < 5; ++kk) {
+        if (kk < nbn) {
+          uint32_t pa[4];
+          pa[0] = pack_bf16x2(s[2 * kk][0], s[2 * kk][1]);
+          pa[1] = pack_bf16x2(s[2 * kk][2], s[2 * kk][3]);
+          pa[2] = pack_bf16x2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+          pa[3] = pack_bf16x2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+          for (int dp = 0; dp < 4; ++dp) {
+            uint32_t b[4];
+            const int m = lane >> 3;
+            ldsm_x4_t(b, sV + swz((nb0 + kk) * 16 + (lane & 7) + (m & 1) * 8, dp * 16 + (m >> 1) * 8));
+            mma_bf16(o[2 * dp], pa, b[0], b[1]);
+            mma_bf16(o[2 * dp + 1], pa, b[2], b[3]);
+          }
+        }
       }
     }
     l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
@@ -352,8 +377,6 @@ __global__ void __launch_bounds__(kSpatialWarps * 32, 1)
     __syncthreads();  // this buffer is refilled two iterations from now
   }
 }
-
-// One warp per (session, patch, head); lane owns head dims 2*lane, 2*lane+1.
 
 // Causal temporal attention for T <= TMAX <= 8 in the lane-per-columns layout
 // of the cached kernel below (a warp covers 256 columns = four heads of one
@@ -634,8 +657,8 @@ int attention_full_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, int grou
       attr[dev & 63] = true;
     }
     const int items = groups * H;
-    const int grid = items < num_sms() ? items : num_sms();
-    launch_pdl(attention_spatial_kernel, dim3(grid), dim3(kSpatialWarps * 32), smem, s, qkv, out, items, H);
+    const int g2 = items < 2 * num_sms() ? items : 2 * num_sms();  // two CTAs per SM
+    launch_pdl(attention_spatial_kernel, dim3(g2), dim3(kSpatialWarps * 32), smem, s, qkv, out, items, H);
   } else if (seq <= 160) {
     constexpr int NW = 3;  // 48 query rows per CTA
     dim3 grid((seq + NW * 16 - 1) / (NW * 16), H, groups);
