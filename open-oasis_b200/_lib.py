@@ -135,6 +135,7 @@ SIGNATURES = {
     "oasis_layernorm": (C.c_int, [C.POINTER(OasisLayerNormArgs), vp]),
     "oasis_silu_bf16": (C.c_int, [fp, vp, C.c_longlong, vp]),
     "oasis_attention_spatial": (C.c_int, [vp, vp, C.c_int, C.c_int, C.c_int, vp]),
+    "oasis_attention_tc": (C.c_int, [vp, vp, C.c_int, C.c_int, C.c_int, vp]),
     "oasis_attention_temporal": (C.c_int, [vp, vp, C.c_int, C.c_int, C.c_int, vp]),
     "oasis_attention_temporal_cached": (C.c_int, [vp, vp, vp, C.c_int, C.c_int, C.c_int, vp]),
     "oasis_gated_residual": (C.c_int, [fp, fp, fp, fp, C.c_longlong, C.c_int, C.c_int, vp]),

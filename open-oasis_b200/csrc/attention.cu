@@ -646,6 +646,13 @@ int attention_full_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, int grou
   OASIS_REQUIRE(groups >= 0 && seq > 0, "attention_full: bad shape");
   OASIS_REQUIRE(H >= 1 && H <= 16, "attention_full: heads=%d outside [1, 16]", H);
   if (groups == 0) return OASIS_OK;
+  // The tcgen05 kernel (attention_tc.cu) is selected with OASIS_ATTN_TC=1 while
+  // it is slower than this file's mma.sync kernels.
+  static const bool use_tc = [] {
+    const char* e = getenv("OASIS_ATTN_TC");
+    return e && e[0] == '1';
+  }();
+  if (use_tc && attention_tc_supported(seq)) return attention_tc_launch(qkv, out, groups, seq, H, s);
   if (seq == kSpatialSeq) {
     constexpr int smem = 2 * 3 * kSpatialTile * 2;
     static bool attr[64] = {false};

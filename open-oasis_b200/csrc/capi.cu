@@ -631,7 +631,11 @@ extern "C" {
 
 const char* oasis_last_error(void) { return g_msg; }
 
-int oasis_device_error(int reset) { return read_device_error(reset); }
+int oasis_device_error(int reset) {
+  const int a = read_device_error(reset);
+  const int b = read_device_error_tc(reset);
+  return a ? a : b;
+}
 
 unsigned long long oasis_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
@@ -823,6 +827,11 @@ int oasis_attention_temporal_cached(const void* past_qkv, const void* cur_qkv, v
   return attention_temporal_cached_launch(static_cast<const __nv_bfloat16*>(past_qkv),
                                           static_cast<const __nv_bfloat16*>(cur_qkv), static_cast<__nv_bfloat16*>(out),
                                           batch, past_frames, kP, heads, S(stream));
+}
+
+int oasis_attention_tc(const void* qkv, void* out, int groups, int seq, int heads, oasis_stream_t stream) {
+  return attention_tc_launch(static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out), groups, seq,
+                             heads, S(stream));
 }
 
 int oasis_gated_residual(float* z, const float* x, const float* bias, const float* gate, long long ldg,

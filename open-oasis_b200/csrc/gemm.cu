@@ -75,8 +75,8 @@ __device__ unsigned long long g_gemm_prof[8];
 
 struct SplitK {
   float* partials;  // [tiles][splits][BM][BN]
-  int* counters;    // [tiles]
-  int splits;
+  int* unused;
+  int splits;       // CTAs per tile (one cluster), each summing K / splits
 };
 
 __host__ __device__ constexpr bool bf16_out(int mode) {
@@ -349,46 +349,63 @@ __device__ __forceinline__ void epilogue_tile_resid(const EpiParams& e, const CU
   }
 }
 
-// Split-K fix-up run by the last split of a tile: sums the partials in split order.
-__device__ __forceinline__ void splitk_reduce(const EpiParams& e, const SplitK& sk, const CUtensorMap* tm_out,
-                                              uint8_t* stg, int M, int N, int BN, int m0q, int n0, int tile,
-                                              int quarter, int half, int lane) {
-  const int r = m0q + lane;
+// Split-K fix-up. The `splits` CTAs of a tile form one thread-block cluster;
+// after every CTA has written its fp32 partial tile and the cluster barrier has
+// passed, CTA `split` sums rows [split BM / splits, (split + 1) BM / splits) of
+// the tile over the partials in split order (deterministic) and applies the
+// epilogue. `tid` / `nthr` enumerate the threads taking part.
+__device__ __forceinline__ void splitk_cluster_reduce(const EpiParams& e, const SplitK& sk, int M, int N, int BN,
+                                                      int m0, int n0, int tile, int split, int tid, int nthr) {
+  const int rows = BM / sk.splits;
+  const int groups = BN / 32;
   const bool bf16 = bf16_out(e.mode);
-  const int W = bf16 ? 64 : 32;
-  const float* base = sk.partials + (long long)tile * sk.splits * (BM * BN) + (quarter * 32 + lane) * BN;
-  const int nchunks = BN / W;
-#pragma unroll 1
-  for (int c = half; c < nchunks; c += kGroups) {
-    const int nb = n0 + c * W;
-    if (nb >= N) break;
-    if (e.mode != kEpiImage) stage_begin(lane, 1);
-#pragma unroll 1
-    for (int g = 0; g < W / 32; ++g) {
-      float v[32];
+  const float* base = sk.partials + (long long)tile * sk.splits * (BM * BN);
+  for (int it = tid; it < rows * groups; it += nthr) {
+    const int lr = split * rows + it / groups;  // row within the tile
+    const int g = it - (it / groups) * groups;
+    const int r = m0 + lr, nb = n0 + g * 32;
+    if (r >= M || nb >= N) continue;
+    float v[32];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = 0.f;
-      for (int s2 = 0; s2 < sk.splits; ++s2) {
-        const float4* src = reinterpret_cast<const float4*>(base + (long long)s2 * (BM * BN) + c * W + g * 32);
+    for (int i = 0; i < 32; ++i) v[i] = 0.f;
+    for (int s2 = 0; s2 < sk.splits; ++s2) {
+      const float4* src = reinterpret_cast<const float4*>(base + (long long)s2 * (BM * BN) + lr * BN + g * 32);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float4 y = __ldcg(src + i);
-          v[4 * i] += y.x; v[4 * i + 1] += y.y; v[4 * i + 2] += y.z; v[4 * i + 3] += y.w;
-        }
-      }
-      float4 res[8];
-      if (reads_resid(e.mode)) load_resid(e, r, nb + g * 32, M, res);
-      epilogue_math(e, r, nb + g * 32, v, res);
-      if (e.mode == kEpiImage) {
-        if (r < M) store_image(e, r, nb, N, v);
-      } else {
-        stage_write(stg, lane, bf16, g * 4, v);
+      for (int i = 0; i < 8; ++i) {
+        const float4 y = __ldcg(src + i);
+        v[4 * i] += y.x; v[4 * i + 1] += y.y; v[4 * i + 2] += y.z; v[4 * i + 3] += y.w;
       }
     }
-    if (e.mode != kEpiImage) stage_commit(tm_out, stg, lane, m0q, nb);
+    float4 res[8];
+    if (reads_resid(e.mode)) load_resid(e, r, nb, M, res);
+    epilogue_math(e, r, nb, v, res);
+    if (e.mode == kEpiImage) {
+      store_image(e, r, nb, N, v);
+    } else if (nb + 32 <= N) {
+      if (bf16) {
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(e.out) + (long long)r * e.ldo + nb);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          dst[j] = make_uint4(pack_bf16x2(v[8 * j], v[8 * j + 1]), pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
+                              pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
+      } else {
+        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(e.out) + (long long)r * e.ldo + nb);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      }
+    } else {  // ragged last column group (N is a multiple of 16)
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        if (nb + i < N) {
+          if (bf16)
+            static_cast<__nv_bfloat16*>(e.out)[(long long)r * e.ldo + nb + i] = __float2bfloat16(v[i]);
+          else
+            static_cast<float*>(e.out)[(long long)r * e.ldo + nb + i] = v[i];
+        }
+      }
+    }
   }
 }
-
 
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -405,7 +422,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_full = empty + C::STAGES;
   uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
-  int* sk_flag = reinterpret_cast<int*>(tmem_base_slot + 1);
   uint64_t* rbar = reinterpret_cast<uint64_t*>(tmem_base_slot + 4);  // [kEpiWarps][2], 8-byte aligned
 
   const int warp = threadIdx.x >> 5;
@@ -565,7 +581,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool resid_tma = reads_resid(epi.mode) && splits == 1;
     int sbuf = 0;
     uint32_t rphase = 0;
-    const int ep_tid = threadIdx.x - 64;
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
@@ -583,28 +598,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
-      if (splits > 1) {
-        __threadfence();
-        named_barrier_sync(1, 32 * kEpiWarps);
-        if (ep_tid == 0) {
-          const int prev = atomicAdd(&sk.counters[tile], 1);
-          const int last = (prev == splits - 1);
-          if (last) sk.counters[tile] = 0;  // every split has arrived: ready for the next launch
-          *sk_flag = last;
-        }
-        named_barrier_sync(1, 32 * kEpiWarps);
-        if (*sk_flag) {
-          __threadfence();
-          splitk_reduce(epi, sk, &tmO, stg, M, N, BN, m0q, n0, tile, quarter, half, lane);
-        }
-        named_barrier_sync(1, 32 * kEpiWarps);  // sk_flag is reused by the next tile
-      }
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
     if (lane == 0) bulk_wait0();  // stores complete before the staging memory goes away
   }
 
+  if (splits > 1) {
+    // one unit per CTA here (grid = tiles x splits, clusters of `splits`): once
+    // every CTA of the cluster has written its partial, reduce this CTA's rows
+    __threadfence();
+    cluster_sync_all();
+    const int tile = blockIdx.x / splits, split = blockIdx.x - tile * splits;
+    splitk_cluster_reduce(epi, sk, M, N, BN, (tile / n_tiles) * BM, (tile % n_tiles) * BN, tile, split,
+                          threadIdx.x, blockDim.x);
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -703,18 +711,17 @@ int launch_bn(const GemmProblem& p, int splits, cudaStream_t stream) {
   const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
   SplitK sk{nullptr, nullptr, splits};
   if (splits > 1) {
-    const size_t part_bytes = (size_t)tiles * splits * BM * BN * sizeof(float);
-    const size_t need = part_bytes + (size_t)tiles * sizeof(int);
+    const size_t need = (size_t)tiles * splits * BM * BN * sizeof(float);
     if (!p.workspace || p.workspace_bytes < need)
       return set_error(OASIS_ERR_WORKSPACE, "split-K GEMM needs %zu workspace bytes, got %zu", need,
                        p.workspace_bytes);
     sk.partials = static_cast<float*>(p.workspace);
-    sk.counters = reinterpret_cast<int*>(static_cast<uint8_t*>(p.workspace) + part_bytes);
-    cudaError_t e = cudaMemsetAsync(sk.counters, 0, (size_t)tiles * sizeof(int), stream);
-    if (e != cudaSuccess) return set_error(OASIS_ERR_CUDA, "memset counters: %s", cudaGetErrorString(e));
+    // one CTA per (tile, split); the splits of a tile are one cluster
+    launch_pdl_cluster(gemm_kernel<BN>, dim3(tiles * splits), dim3(kThreads), C::SMEM, stream, splits, ta, tw, to,
+                       tr, p.M, p.N, p.K, p.epi, sk);
+    return check_launch("gemm_kernel");
   }
-  const int units = tiles * splits;
-  const int grid = units < num_sms() ? units : num_sms();
+  const int grid = tiles < num_sms() ? tiles : num_sms();
   launch_pdl(gemm_kernel<BN>, dim3(grid), dim3(kThreads), C::SMEM, stream, ta, tw, to, tr, p.M, p.N, p.K, p.epi, sk);
   return check_launch("gemm_kernel");
 }
@@ -766,7 +773,7 @@ size_t gemm_workspace_bytes(int M, int N, int K) {
   Plan pl = choose_plan(M, N, K);
   if (pl.splits <= 1) return 0;
   const size_t tiles = (size_t)((M + BM - 1) / BM) * ((N + pl.bn - 1) / pl.bn);
-  return tiles * pl.splits * BM * pl.bn * sizeof(float) + tiles * sizeof(int);
+  return tiles * pl.splits * BM * pl.bn * sizeof(float);
 }
 
 size_t gemm_splitk_bytes(int M, int N, int K, int block_n, int splits) {
@@ -777,7 +784,7 @@ size_t gemm_splitk_bytes(int M, int N, int K, int block_n, int splits) {
   if (pl.bn <= 128 && K % (2 * BK)) pl.bn = 256;  // as gemm_launch
   if (pl.splits <= 1) return 0;
   const size_t tiles = (size_t)((M + BM - 1) / BM) * ((N + pl.bn - 1) / pl.bn);
-  return tiles * pl.splits * BM * pl.bn * sizeof(float) + tiles * sizeof(int);
+  return tiles * pl.splits * BM * pl.bn * sizeof(float);
 }
 
 int gemm_launch(const GemmProblem& p, cudaStream_t stream) {
@@ -803,6 +810,7 @@ int gemm_launch(const GemmProblem& p, cudaStream_t stream) {
   OASIS_REQUIRE(pl.bn != 32 || !bf16_out(p.epi.mode), "GEMM: block_n=32 needs an fp32 epilogue");
   if (pl.bn <= 128 && p.K % (2 * BK)) pl.bn = 256;  // narrower tiles stage K in 128-wide steps
   const int k_stages = p.K / (pl.bn <= 128 ? 2 * BK : BK);
+  OASIS_REQUIRE(pl.splits >= 1 && pl.splits <= 8, "GEMM: splits=%d outside [1, 8] (one cluster per tile)", pl.splits);
   OASIS_REQUIRE(k_stages % pl.splits == 0, "GEMM: splits=%d must divide the %d K stages", pl.splits, k_stages);
   switch (pl.bn) {
     case 32: return launch_bn<32>(p, pl.splits, stream);
@@ -816,6 +824,22 @@ int gemm_launch(const GemmProblem& p, cudaStream_t stream) {
 }  // namespace oasis
 
 namespace oasis {
+
+int make_tma_bf16_2d(CUtensorMap* map, const void* ptr, long long inner, long long outer, long long ld,
+                     int box_inner, int box_outer) {
+  OASIS_TRY(get_encoder());
+  OASIS_REQUIRE((reinterpret_cast<uintptr_t>(ptr) & 15) == 0, "TMA source not 16-byte aligned");
+  OASIS_REQUIRE((ld * 2) % 16 == 0, "TMA row stride not a multiple of 16 bytes");
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(OASIS_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return OASIS_OK;
+}
 
 int read_device_error(int reset) {
   cudaError_t e = cudaDeviceSynchronize();

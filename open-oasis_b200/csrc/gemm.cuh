@@ -1,5 +1,6 @@
 // Host-visible declarations for the tcgen05 GEMM family.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -45,7 +46,7 @@ struct GemmProblem {
   EpiParams epi;
   int block_n = 0;          // 0 = heuristic, else 64/128/256
   int splits = 0;           // 0 = heuristic, 1 = no split-K
-  void* workspace = nullptr;  // split-K partials + tile counters (may be null -> no split)
+  void* workspace = nullptr;  // split-K partial tiles (may be null -> no split)
   size_t workspace_bytes = 0;
 };
 
@@ -59,5 +60,10 @@ size_t gemm_workspace_bytes(int M, int N, int K);
 size_t gemm_splitk_bytes(int M, int N, int K, int block_n, int splits);
 
 int num_sms();
+
+// 2-D bf16 TMA map with the 128-byte swizzle over a row-major matrix of `outer`
+// rows x `inner` columns (row stride `ld` elements), box {box_inner, box_outer}.
+int make_tma_bf16_2d(CUtensorMap* map, const void* ptr, long long inner, long long outer, long long ld,
+                     int box_inner, int box_outer);
 
 }  // namespace oasis

@@ -5,7 +5,7 @@
 // only its own tensors), code running where cudaMalloc is forbidden or would
 // synchronize the device at a bad moment, or a plugin ABI that passes only
 // inputs and outputs. For them this entry point takes its split-K scratch
-// (partial tiles + per-tile arrival counters) from a fixed array in device
+// (the partial tiles of the split-K clusters) from a fixed array in device
 // memory that the library owns. It allocates nothing itself.
 //
 // Costs and limits, stated once here:
@@ -15,8 +15,8 @@
 //    OASIS_ERR_WORKSPACE (use oasis_gemm with a workspace instead);
 //  * all calls share the one array: two calls that overlap on the GPU (different
 //    streams, or different host threads on the same device) race on it. Issue them
-//    on one stream, one after another. The tile counters are cleared by every
-//    launch; the partials need no clearing (every split overwrites its own).
+//    on one stream, one after another. The partials need no clearing (every
+//    split overwrites its own before the cluster barrier).
 //  * the first call on each device looks the array's device address up (with
 //    that device current) and caches it; make that first call before any stream
 //    capture.

@@ -223,15 +223,42 @@ def _attn_ref(q, k, v, mask=None):
     return torch.softmax(s, -1) @ v
 
 
-@pytest.mark.parametrize("groups,seq", [(1, 144), (5, 144), (2, 576), (1, 50), (3, 200)])
-def test_attention_full(groups, seq):
-    qkv = rand_bf16(groups * seq, 3072, seed=groups * 1000 + seq)
-    out = torch.empty(groups * seq, 1024, device=DEV, dtype=torch.bfloat16)
-    _lib.call("oasis_attention_spatial", qkv.data_ptr(), out.data_ptr(), groups, seq, 16, _s())
+ATTN_CASES = [(1, 144, 16), (5, 144, 16), (37, 144, 16), (9, 144, 8), (3, 144, 2), (2, 576, 16), (3, 576, 16),
+              (1, 576, 4), (1, 50, 16), (3, 200, 16)]
+
+
+@pytest.mark.parametrize("groups,seq,H", ATTN_CASES)
+def test_attention_full(groups, seq, H):
+    """Full attention within groups: seq 144 (DiT spatial) and 576 (VAE) run the
+    tcgen05 kernel (128-row query tiles that straddle groups), other lengths the
+    mma.sync kernel; H = 16 / n under n-way tensor parallelism."""
+    HD = H * 64
+    qkv = rand_bf16(groups * seq, 3 * HD, seed=groups * 1000 + seq + H)
+    out = torch.full((groups * seq, HD), float("nan"), device=DEV, dtype=torch.bfloat16)
+    _lib.call("oasis_attention_spatial", qkv.data_ptr(), out.data_ptr(), groups, seq, H, _s())
     torch.cuda.synchronize()
-    x = qkv.float().reshape(groups, seq, 3, 16, 64).permute(2, 0, 3, 1, 4)  # 3 G H S D
-    ref = _attn_ref(x[0], x[1], x[2]).permute(0, 2, 1, 3).reshape(groups * seq, 1024)
-    assert rel_l2(out.float(), ref) < 1e-2
+    assert _lib.load().oasis_device_error(1) == 0
+    x = qkv.float().reshape(groups, seq, 3, H, 64).permute(2, 0, 3, 1, 4)  # 3 G H S D
+    ref = _attn_ref(x[0], x[1], x[2]).permute(0, 2, 1, 3).reshape(groups * seq, HD)
+    assert not torch.isnan(out.float()).any()
+    assert rel_l2(out.float(), ref) < 1e-2, rel_l2(out.float(), ref)
+
+
+@pytest.mark.parametrize("groups,seq,H", [c for c in ATTN_CASES if c[1] in (144, 576)])
+def test_attention_tc(groups, seq, H):
+    """The tcgen05 attention kernel (OASIS_ATTN_TC=1 selects it on the model path)
+    against the PyTorch fp32 reference."""
+    from oasis_b200 import _lib as L
+
+    HD = H * 64
+    qkv = rand_bf16(groups * seq, 3 * HD, seed=groups * 7 + seq + H)
+    out = torch.full((groups * seq, HD), float("nan"), device=DEV, dtype=torch.bfloat16)
+    L.call("oasis_attention_tc", qkv.data_ptr(), out.data_ptr(), groups, seq, H, _s())
+    torch.cuda.synchronize()
+    assert L.load().oasis_device_error(1) == 0
+    x = qkv.float().reshape(groups, seq, 3, H, 64).permute(2, 0, 3, 1, 4)
+    ref = _attn_ref(x[0], x[1], x[2]).permute(0, 2, 1, 3).reshape(groups * seq, HD)
+    assert rel_l2(out.float(), ref) < 1e-2, rel_l2(out.float(), ref)
 
 
 @pytest.mark.parametrize("B,T", [(1, 1), (1, 2), (2, 8), (1, 32), (3, 5)])
