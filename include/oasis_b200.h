@@ -325,7 +325,7 @@ int oasis_attention_spatial(const void* qkv, void* out, int groups, int seq, int
  * of (b, t, p) = (b T + t) 144 + p. Replaces sdpa_temporal_causal
  * (src/sdpa_causal.py:17-100) and its block-diagonal packing. */
 /* The same full attention on the 5th-generation tensor cores (tcgen05.mma with
- * TMEM accumulators, TMA-fed): seq = 144 or a multiple of 192. */
+ * TMEM accumulators, TMA-fed): seq a multiple of 144. */
 int oasis_attention_tc(const void* qkv, void* out, int groups, int seq, int heads, oasis_stream_t stream);
 int oasis_attention_temporal(const void* qkv, void* out, int batch, int frames, int heads, oasis_stream_t stream);
 /* The generated frame's query per (session, patch, head) against the cached

@@ -163,16 +163,16 @@ __global__ void __launch_bounds__(NW * 32) attention_full_kernel(const __nv_bflo
     mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-    const float alpha0 = exp2f(m0 - mx0), alpha1 = exp2f(m1 - mx1);
+    const float alpha0 = ex2_approx(m0 - mx0), alpha1 = ex2_approx(m1 - mx1);
     m0 = mx0;
     m1 = mx1;
     float rs0 = 0.f, rs1 = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      s[i][0] = exp2f(s[i][0] - mx0);
-      s[i][1] = exp2f(s[i][1] - mx0);
-      s[i][2] = exp2f(s[i][2] - mx1);
-      s[i][3] = exp2f(s[i][3] - mx1);
+      s[i][0] = ex2_approx(s[i][0] - mx0);
+      s[i][1] = ex2_approx(s[i][1] - mx0);
+      s[i][2] = ex2_approx(s[i][2] - mx1);
+      s[i][3] = ex2_approx(s[i][3] - mx1);
       rs0 += s[i][0] + s[i][1];
       rs1 += s[i][2] + s[i][3];
     }
@@ -311,7 +311,7 @@ __global__ void __launch_bounds__(kSpatialWarps * 32, 2)
       mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
       mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
       mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-      const float a0 = exp2f(m0 - mx0), a1 = exp2f(m1 - mx1);  // 0 on the first chunk
+      const float a0 = ex2_approx(m0 - mx0), a1 = ex2_approx(m1 - mx1);  // 0 on the first chunk
       m0 = mx0;
       m1 = mx1;
       l0 *= a0;
@@ -324,10 +324,10 @@ __global__ void __launch_bounds__(kSpatialWarps * 32, 2)
 #pragma unroll
       for (int i = 0; i < 10; ++i) {
         if (i < 2 * nbn) {
-          s[i][0] = exp2f(s[i][0] - mx0);
-          s[i][1] = exp2f(s[i][1] - mx0);
-          s[i][2] = exp2f(s[i][2] - mx1);
-          s[i][3] = exp2f(s[i][3] - mx1);
+          s[i][0] = ex2_approx(s[i][0] - mx0);
+          s[i][1] = ex2_approx(s[i][1] - mx0);
+          s[i][2] = ex2_approx(s[i][2] - mx1);
+          s[i][3] = ex2_approx(s[i][3] - mx1);
           l0 += s[i][0] + s[i][1];
           l1 += s[i][2] + s[i][3];
         }
@@ -462,8 +462,8 @@ __global__ void __launch_bounds__(256) attention_temporal_cached_kernel(const __
     sc += __shfl_xor_sync(0xffffffffu, sc, 2);
     sc += __shfl_xor_sync(0xffffffffu, sc, 4);
     const float mnew = fmaxf(mx, sc);
-    const float corr = exp2f(mx - mnew);  // 0 on the first key
-    const float e = exp2f(sc - mnew);
+    const float corr = ex2_approx(mx - mnew);  // 0 on the first key
+    const float e = ex2_approx(sc - mnew);
     l = l * corr + e;
     mx = mnew;
     bf16x8_to_f32(vc, v);
@@ -535,7 +535,7 @@ __global__ void __launch_bounds__(256) attention_temporal_rows_kernel(const __nv
       for (int i = 0; i < 8; ++i) acc[i] = 0.f;
 #pragma unroll
       for (int s2 = 0; s2 <= tq; ++s2) {
-        const float e = exp2f(sc[s2] - mx);
+        const float e = ex2_approx(sc[s2] - mx);
         float v[8];
         bf16x8_to_f32(vr[s2], v);
         l += e;
@@ -605,8 +605,8 @@ __global__ void __launch_bounds__(128) attention_temporal_rows_long_kernel(const
         d += __shfl_xor_sync(0xffffffffu, d, 4);
         if (s2 <= t0 + j) {  // causal
           const float mnew = fmaxf(mx[j], d);
-          const float corr = exp2f(mx[j] - mnew);
-          const float e = exp2f(d - mnew);
+          const float corr = ex2_approx(mx[j] - mnew);
+          const float e = ex2_approx(d - mnew);
           l[j] = l[j] * corr + e;
           mx[j] = mnew;
 #pragma unroll
@@ -646,12 +646,15 @@ int attention_full_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, int grou
   OASIS_REQUIRE(groups >= 0 && seq > 0, "attention_full: bad shape");
   OASIS_REQUIRE(H >= 1 && H <= 16, "attention_full: heads=%d outside [1, 16]", H);
   if (groups == 0) return OASIS_OK;
-  // The tcgen05 kernel (attention_tc.cu) is selected with OASIS_ATTN_TC=1 while
-  // it is slower than this file's mma.sync kernels.
-  static const bool use_tc = [] {
+  // The tcgen05 kernel (attention_tc.cu) runs the VAE's 576-token attention
+  // (measured 400 -> 260 us at 64 frames); at 144 tokens it ties with the
+  // mma.sync kernel below (225 us at 512 frames), which stays the default there.
+  // OASIS_ATTN_TC=1 / 0 forces one or the other for every supported length.
+  static const int tc_mode = [] {
     const char* e = getenv("OASIS_ATTN_TC");
-    return e && e[0] == '1';
+    return e ? (e[0] == '1' ? 1 : 0) : -1;
   }();
+  const bool use_tc = tc_mode == 1 || (tc_mode == -1 && seq > kSpatialSeq);
   if (use_tc && attention_tc_supported(seq)) return attention_tc_launch(qkv, out, groups, seq, H, s);
   if (seq == kSpatialSeq) {
     constexpr int smem = 2 * 3 * kSpatialTile * 2;

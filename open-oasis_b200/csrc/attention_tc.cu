@@ -20,8 +20,8 @@
 //                        operand (V rows are key-major as they sit in memory)
 //   O    = O alpha_j + PV_j  in registers (alpha_j rescales to the new max)
 // Warp 0 streams Q (double-buffered per unit) and K/V blocks (2-stage ring) with
-// TMA, warp 1 owns TMEM and issues the MMAs from one thread, warps 4..7 do the
-// softmax and the output. Persistent over units. Every wait is bounded and
+// TMA, warp 1 owns TMEM and issues the MMAs from one thread, two warps per TMEM
+// lane quarter do the softmax and the output. Persistent over units. Every wait is bounded and
 // records a code in this file's device error word.
 #include <cuda.h>
 
@@ -34,9 +34,15 @@ namespace oasis {
 namespace {
 
 constexpr int kTcRows = 128;    // query rows per unit = TMEM lanes
-constexpr int kTcThreads = 256;  // warp 0 TMA, warp 1 MMA, warps 4..7 softmax
+// Warp 0 TMA, warp 1 MMA, warps 4 .. 4 + 4 SWQ softmax: SWQ warps share each TMEM
+// lane quarter (32 query rows), splitting the key columns of a block and the 64
+// output dims between them.
 constexpr int kTcSoftWarp0 = 4;
+constexpr int kTcSWQ = 2;
+constexpr int kTcThreads = 32 * (kTcSoftWarp0 + 4 * kTcSWQ);
 constexpr int kTcSCols = 192;    // TMEM columns reserved per S buffer (KB <= 192)
+// (all callers use KB = 144: shared memory then holds two Q tiles, two K/V stages
+// and two P tiles within the 227 KB limit)
 constexpr int kTcPVCol = 384;    // PV buffers at columns 384 and 448
 
 template <int KB>
@@ -48,7 +54,7 @@ struct TcCfg {
   static constexpr int STAGES = 2;
   static constexpr int P_ATOMS = (KB + 63) / 64;  // 64-key atoms of the P operand
   static constexpr int P_BYTES = P_ATOMS * kTcRows * 128;
-  static constexpr int BAR_BYTES = 256;
+  static constexpr int BAR_BYTES = 256 + 2 * 2 * kTcRows * 4;  // barriers + row max/sum exchange
   static constexpr int SMEM = 1024 + 2 * Q_BYTES + STAGES * STAGE_BYTES + 2 * P_BYTES + BAR_BYTES;
 };
 
@@ -118,6 +124,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* pv_full = bars + 12;  // [2]
   uint64_t* pv_free = bars + 14;  // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  float* xch = reinterpret_cast<float*>(bars + 32);  // [2 rounds][2 halves][128 rows]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int HD = H * 64;
@@ -134,9 +141,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 4);
+      mbar_init(&p_full[i], 4 * kTcSWQ);
       mbar_init(&pv_full[i], 1);
-      mbar_init(&pv_free[i], 4);
+      mbar_init(&pv_free[i], 4 * kTcSWQ);
     }
     fence_barrier_init();
   }
@@ -212,7 +219,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const int b = jb & 1;
           if (!tc_wait(&kv_full[st], ph, kDevTimeoutTmaFull, 6)) { ok = false; break; }
           // S[b] is free once the softmax of block jb - 2 has read it (it then wrote P)
-          if (jb >= 2 && !tc_wait(&p_full[b], ((jb >> 1) - 1) & 1, kDevTimeoutAccEmpty, 7)) { ok = false; break; }
+          if (jb >= 2 && !tc_wait(&p_full[b], ((jb >> 1) - 1) & 1, kDevTimeoutAccEmpty, 0)) { ok = false; break; }
           tc_fence_after();
           const uint32_t k_addr = smem_u32(sKV + st * C::STAGE_BYTES);
           const uint32_t d = tmem + b * kTcSCols;
@@ -236,44 +243,62 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // Blocks are handled in one stream across units, P V of block j being
     // accumulated after the softmax of block j + 1 (so its MMA latency is hidden);
     // a unit's output is written when its last block has been accumulated.
-    const int row_t = threadIdx.x - kTcSoftWarp0 * 32;  // TMEM lane = query row in the unit
-    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    // Half `hf` of a lane quarter takes the 32-column chunks c with c % SWQ == hf
+    // (the 16-column tail of KB = 144 goes to the last half) and output dims
+    // [hf 64 / SWQ, (hf + 1) 64 / SWQ); row max and sum are exchanged through
+    // shared memory with a named barrier per quarter.
+    constexpr int ODIM = 64 / kTcSWQ;
+    constexpr int NCH = KB / 32;
+    const int quarter = warp & 3;
+    const int hf = (warp - kTcSoftWarp0) >> 2;
+    const int row_t = quarter * 32 + lane;  // TMEM lane = query row in the unit
+    const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
     const float sc = 0.125f * 1.4426950408889634f;  // 1/sqrt(64) in log2 units
+    auto pair_sync = [&]() {
+      if constexpr (kTcSWQ > 1) named_barrier_sync(1 + quarter, 32 * kTcSWQ);
+    };
     int jb = 0;
     bool ok = true;
-    float o[64];
+    float o[ODIM];
 #pragma unroll
-    for (int i = 0; i < 64; ++i) o[i] = 0.f;
+    for (int i = 0; i < ODIM; ++i) o[i] = 0.f;
     bool pending = false, pending_last = false;
     float alpha_prev = 0.f, l_done = 0.f;
     int r_done = 0, head_done = 0;
-    // O = O alpha + PV_j for global block j
+    // O = O alpha + PV_j (this half's dims) for global block j
     auto accumulate = [&](int j, float alpha) -> bool {
       const int b = j & 1;
       if (!tc_wait(&pv_full[b], (j >> 1) & 1, kDevTimeoutAccFull, 8)) return false;
       tc_fence_after();
-      float pv[64];
-      tmem_ld64(lane_base + kTcPVCol + b * 64, pv);
 #pragma unroll
-      for (int i = 0; i < 64; ++i) o[i] = fmaf(o[i], alpha, pv[i]);
+      for (int h = 0; h < ODIM / 32; ++h) {
+        float pv[32];
+        tmem_ld32(lane_base + kTcPVCol + b * 64 + hf * ODIM + h * 32, pv);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[h * 32 + i] = fmaf(o[h * 32 + i], alpha, pv[i]);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&pv_free[b]);
       return true;
     };
-    auto finish = [&]() {  // write the finished unit's row, clear O
+    auto finish = [&]() {  // write the finished unit's row (this half's dims), clear O
       if (r_done < rows && l_done > 0.f) {
         const float inv = 1.f / l_done;
-        uint4* dst = reinterpret_cast<uint4*>(out + (long long)r_done * HD + head_done * 64);
+        uint4* dst = reinterpret_cast<uint4*>(out + (long long)r_done * HD + head_done * 64 + hf * ODIM);
 #pragma unroll
-        for (int q = 0; q < 8; ++q)
+        for (int q = 0; q < ODIM / 8; ++q)
           dst[q] = make_uint4(pack_bf16x2(o[8 * q] * inv, o[8 * q + 1] * inv),
                               pack_bf16x2(o[8 * q + 2] * inv, o[8 * q + 3] * inv),
                               pack_bf16x2(o[8 * q + 4] * inv, o[8 * q + 5] * inv),
                               pack_bf16x2(o[8 * q + 6] * inv, o[8 * q + 7] * inv));
       }
 #pragma unroll
-      for (int i = 0; i < 64; ++i) o[i] = 0.f;
+      for (int i = 0; i < ODIM; ++i) o[i] = 0.f;
+    };
+    auto store_p = [&](uint8_t* prow, int chunk, const uint32_t (&pk)[4]) {  // 16-byte chunk = 8 keys
+      uint8_t* dst = prow + (chunk >> 3) * (kTcRows * 128) + (((chunk & 7) ^ (row_t & 7)) << 4);
+      *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
     };
 #ifdef OASIS_TC_PROF
     const long long prof_t0 = clock64();
@@ -290,83 +315,111 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tc_fence_after();
         uint8_t* prow = sP + b * C::P_BYTES + row_t * 128;
         float alpha = 1.f;
-        if (__any_sync(0xffffffffu, mine)) {
-          // pass 1: row max of this block (TMEM loads are warp-collective)
+#ifdef OASIS_TC_PROF
+        long long pt = clock64();
+#define TC_SECTION(i) if (lane == 0) { const long long n_ = clock64(); atomicAdd(&g_tc_prof[i], (unsigned long long)(n_ - pt)); pt = n_; }
+#else
+#define TC_SECTION(i)
+#endif
+        if (__any_sync(0xffffffffu, mine)) {  // same rows, same decision in both halves
           const uint32_t sbase = lane_base + b * kTcSCols;
+          // pass 1: row max of this block (TMEM loads are warp-collective)
           float bm = -1e30f;
 #pragma unroll
-          for (int c = 0; c < KB / 64; ++c) {
-            float s[64];
-            tmem_ld64(sbase + c * 64, s);
+          for (int c = hf; c < NCH; c += kTcSWQ) {
+            float s[32];
+            tmem_ld32(sbase + c * 32, s);
 #pragma unroll
-            for (int k = 0; k < 64; ++k) bm = fmaxf(bm, s[k]);
+            for (int k = 0; k < 32; ++k) bm = fmaxf(bm, s[k]);
           }
-          if constexpr (KB % 64) {
-            float s[16];
-            static_assert(KB % 64 == 16, "tail of 16 columns");
-            tmem_ld16(sbase + (KB / 64) * 64, s);
+          if constexpr (KB % 32 != 0) {
+            if (hf == kTcSWQ - 1) {
+              float s[16];
+              tmem_ld16(sbase + NCH * 32, s);
 #pragma unroll
-            for (int k = 0; k < 16; ++k) bm = fmaxf(bm, s[k]);
+              for (int k = 0; k < 16; ++k) bm = fmaxf(bm, s[k]);
+            }
           }
+          if constexpr (kTcSWQ > 1) {
+            xch[hf * kTcRows + row_t] = bm;
+            pair_sync();
+            bm = fmaxf(xch[row_t], xch[kTcRows + row_t]);
+          }
+          TC_SECTION(11)
           const float mnew = mine ? fmaxf(m, bm * sc) : m;
-          alpha = mine ? exp2f(m - mnew) : 1.f;
+          alpha = mine ? ex2_approx(m - mnew) : 1.f;
           // pass 2: p = exp2(s c - m), row sum, bf16 P in the swizzled operand layout
           float rs = 0.f;
 #pragma unroll
-          for (int c = 0; c < KB / 64; ++c) {
-            float s[64];
-            tmem_ld64(sbase + c * 64, s);
+          for (int c = hf; c < NCH; c += kTcSWQ) {
+            float s[32];
+            tmem_ld32(sbase + c * 32, s);
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
+            for (int q = 0; q < 4; ++q) {
               uint32_t pk[4];
 #pragma unroll
               for (int k = 0; k < 4; ++k) {
-                const float p0 = mine ? exp2f(fmaf(s[8 * q + 2 * k], sc, -mnew)) : 0.f;
-                const float p1 = mine ? exp2f(fmaf(s[8 * q + 2 * k + 1], sc, -mnew)) : 0.f;
+                const float p0 = mine ? ex2_approx(fmaf(s[8 * q + 2 * k], sc, -mnew)) : 0.f;
+                const float p1 = mine ? ex2_approx(fmaf(s[8 * q + 2 * k + 1], sc, -mnew)) : 0.f;
                 rs += p0 + p1;
                 pk[k] = pack_bf16x2(p0, p1);
               }
-              // 16-byte chunk q of 64-key atom c (8 keys per chunk)
-              uint8_t* dst = prow + c * (kTcRows * 128) + ((q ^ (row_t & 7)) << 4);
-              *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+              store_p(prow, c * 4 + q, pk);
             }
           }
-          if constexpr (KB % 64) {
-            float s[16];
-            tmem_ld16(sbase + (KB / 64) * 64, s);
+          if constexpr (KB % 32 != 0) {
+            if (hf == kTcSWQ - 1) {
+              float s[16];
+              tmem_ld16(sbase + NCH * 32, s);
 #pragma unroll
-            for (int q = 0; q < 2; ++q) {
-              uint32_t pk[4];
+              for (int q = 0; q < 2; ++q) {
+                uint32_t pk[4];
 #pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                const float p0 = mine ? exp2f(fmaf(s[8 * q + 2 * k], sc, -mnew)) : 0.f;
-                const float p1 = mine ? exp2f(fmaf(s[8 * q + 2 * k + 1], sc, -mnew)) : 0.f;
-                rs += p0 + p1;
-                pk[k] = pack_bf16x2(p0, p1);
+                for (int k = 0; k < 4; ++k) {
+                  const float p0 = mine ? ex2_approx(fmaf(s[8 * q + 2 * k], sc, -mnew)) : 0.f;
+                  const float p1 = mine ? ex2_approx(fmaf(s[8 * q + 2 * k + 1], sc, -mnew)) : 0.f;
+                  rs += p0 + p1;
+                  pk[k] = pack_bf16x2(p0, p1);
+                }
+                store_p(prow, NCH * 4 + q, pk);
               }
-              uint8_t* dst = prow + (KB / 64) * (kTcRows * 128) + ((q ^ (row_t & 7)) << 4);
-              *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
             }
+          }
+          TC_SECTION(12)
+          if constexpr (kTcSWQ > 1) {
+            xch[2 * kTcRows + hf * kTcRows + row_t] = rs;
+            pair_sync();
+            rs = xch[2 * kTcRows + row_t] + xch[3 * kTcRows + row_t];
           }
           if (mine) {
             l = l * alpha + rs;
             m = mnew;
           }
+          TC_SECTION(13)
         } else {
-          // no row of this warp belongs to the block's group: zero P rows
+          // no row of this warp belongs to the block's group: zero this half's P chunks
+          const uint32_t zero[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-          for (int chunk = 0; chunk < KB / 8; ++chunk) {
-            uint8_t* dst = prow + (chunk >> 3) * (kTcRows * 128) + (((chunk & 7) ^ (row_t & 7)) << 4);
-            *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+          for (int c = hf; c < NCH; c += kTcSWQ)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) store_p(prow, c * 4 + q, zero);
+          if constexpr (KB % 32 != 0) {
+            if (hf == kTcSWQ - 1) {
+              store_p(prow, NCH * 4, zero);
+              store_p(prow, NCH * 4 + 1, zero);
+            }
           }
         }
         tc_fence_before();    // S[b] reads done before the MMA may overwrite it
         fence_proxy_async();  // P writes visible to the tensor core
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[b]);
+        TC_SECTION(14)
         if (pending) {
           if (!accumulate(jb - 1, alpha_prev)) { ok = false; break; }
+          TC_SECTION(15)
           if (pending_last) finish();
+          TC_SECTION(7)
         }
         pending = true;
         alpha_prev = alpha;
@@ -414,7 +467,7 @@ int launch_tc(const __nv_bfloat16* qkv, __nv_bfloat16* out, int groups, int seq,
 
 }  // namespace
 
-bool attention_tc_supported(int seq) { return seq == 144 || (seq >= 192 && seq % 192 == 0); }
+bool attention_tc_supported(int seq) { return seq >= 144 && seq % 144 == 0; }
 
 int attention_tc_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, int groups, int seq, int H, cudaStream_t s) {
   OASIS_REQUIRE(qkv && out, "attention_tc: null pointer");
@@ -422,8 +475,7 @@ int attention_tc_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, int groups
   OASIS_REQUIRE(attention_tc_supported(seq), "attention_tc: seq=%d unsupported", seq);
   OASIS_REQUIRE((long long)groups * seq < (1LL << 31), "attention_tc: too many rows");
   if (groups == 0) return OASIS_OK;
-  if (seq == 144) return launch_tc<144>(qkv, out, groups, seq, H, s);
-  return launch_tc<192>(qkv, out, groups, seq, H, s);
+  return launch_tc<144>(qkv, out, groups, seq, H, s);  // key blocks of 144 (VAE: 4 per 576-token frame)
 }
 
 #ifdef OASIS_TC_PROF

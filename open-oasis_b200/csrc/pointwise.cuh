@@ -54,7 +54,7 @@ int post_quant_launch(const float* lat, const float* w, const float* b, float* z
 // Attention over a packed qkv buffer [rows, 3 * 1024] bf16 (q | k | v, 16 heads x 64).
 // Full (non-causal) attention within groups of `seq` consecutive rows.
 int attention_full_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, int groups, int seq, int H, cudaStream_t s);
-// tcgen05 version for seq = 144 or a multiple of 192 (attention_tc.cu).
+// tcgen05 version for seq a multiple of 144 (attention_tc.cu).
 bool attention_tc_supported(int seq);
 int attention_tc_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, int groups, int seq, int H, cudaStream_t s);
 int read_device_error_tc(int reset);
