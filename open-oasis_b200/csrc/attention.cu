@@ -646,15 +646,15 @@ int attention_full_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, int grou
   OASIS_REQUIRE(groups >= 0 && seq > 0, "attention_full: bad shape");
   OASIS_REQUIRE(H >= 1 && H <= 16, "attention_full: heads=%d outside [1, 16]", H);
   if (groups == 0) return OASIS_OK;
-  // The tcgen05 kernel (attention_tc.cu) runs the VAE's 576-token attention
-  // (measured 400 -> 260 us at 64 frames); at 144 tokens it ties with the
-  // mma.sync kernel below (225 us at 512 frames), which stays the default there.
-  // OASIS_ATTN_TC=1 / 0 forces one or the other for every supported length.
+  // The tcgen05 kernel (attention_tc.cu) runs every length it supports
+  // (multiples of 144): measured 225 -> 214 us for 512 DiT frames and
+  // 400 -> 250 us for 64 VAE frames against the mma.sync kernels below, which
+  // serve other lengths. OASIS_ATTN_TC=0 selects the mma.sync kernels.
   static const int tc_mode = [] {
     const char* e = getenv("OASIS_ATTN_TC");
     return e ? (e[0] == '1' ? 1 : 0) : -1;
   }();
-  const bool use_tc = tc_mode == 1 || (tc_mode == -1 && seq > kSpatialSeq);
+  const bool use_tc = tc_mode != 0;
   if (use_tc && attention_tc_supported(seq)) return attention_tc_launch(qkv, out, groups, seq, H, s);
   if (seq == kSpatialSeq) {
     constexpr int smem = 2 * 3 * kSpatialTile * 2;

@@ -19,7 +19,8 @@
 //   PV_j = P_j V_j       tcgen05.mma M=128 N=64 K=KB with V as an MN-major
 //                        operand (V rows are key-major as they sit in memory)
 //   O    = O alpha_j + PV_j  in registers (alpha_j rescales to the new max)
-// Warp 0 streams Q (double-buffered per unit) and K/V blocks (2-stage ring) with
+// Warp 0 streams Q (one buffer: the next unit's Q loads while the last block of
+// the current unit is in softmax) and K/V blocks (3-stage ring) with
 // TMA, warp 1 owns TMEM and issues the MMAs from one thread, two warps per TMEM
 // lane quarter do the softmax and the output. Persistent over units. Every wait is bounded and
 // records a code in this file's device error word.
@@ -37,8 +38,11 @@ constexpr int kTcRows = 128;    // query rows per unit = TMEM lanes
 // Warp 0 TMA, warp 1 MMA, warps 4 .. 4 + 4 SWQ softmax: SWQ warps share each TMEM
 // lane quarter (32 query rows), splitting the key columns of a block and the 64
 // output dims between them.
-constexpr int kTcSoftWarp0 = 4;
-constexpr int kTcSWQ = 2;
+#ifndef OASIS_TC_SWQ
+#define OASIS_TC_SWQ 2
+#endif
+constexpr int kTcSWQ = OASIS_TC_SWQ;
+constexpr int kTcSoftWarp0 = kTcSWQ >= 4 ? 2 : 4;
 constexpr int kTcThreads = 32 * (kTcSoftWarp0 + 4 * kTcSWQ);
 constexpr int kTcSCols = 192;    // TMEM columns reserved per S buffer (KB <= 192)
 // (all callers use KB = 144: shared memory then holds two Q tiles, two K/V stages
@@ -51,11 +55,13 @@ struct TcCfg {
   static constexpr int Q_BYTES = kTcRows * 128;
   static constexpr int KV_BYTES = KB * 128;  // one K or V block: KB rows of 64 bf16
   static constexpr int STAGE_BYTES = 2 * KV_BYTES;
-  static constexpr int STAGES = 2;
+  static constexpr int STAGES = 3;   // K/V ring depth
+  static constexpr int Q_BUFS = 1;   // the next unit's Q loads during the last block's softmax
   static constexpr int P_ATOMS = (KB + 63) / 64;  // 64-key atoms of the P operand
   static constexpr int P_BYTES = P_ATOMS * kTcRows * 128;
-  static constexpr int BAR_BYTES = 256 + 2 * 2 * kTcRows * 4;  // barriers + row max/sum exchange
-  static constexpr int SMEM = 1024 + 2 * Q_BYTES + STAGES * STAGE_BYTES + 2 * P_BYTES + BAR_BYTES;
+  static constexpr int BAR_BYTES = 256 + 2 * kTcSWQ * kTcRows * 4;  // barriers + row max/sum exchange
+  static constexpr int SMEM = 1024 + Q_BUFS * Q_BYTES + STAGES * STAGE_BYTES + 2 * P_BYTES + BAR_BYTES;
+  static_assert(SMEM <= 232448, "shared memory");
 };
 
 // K-major operands (Q, K, P): S = Q K^T reads K like a weight matrix. MN-major B
@@ -111,20 +117,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   using C = TcCfg<KB>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;                                   // [2][128 rows x 128 B]
-  uint8_t* sKV = sQ + 2 * C::Q_BYTES;                   // [STAGES][K block | V block]
+  uint8_t* sQ = smem;                                   // [Q_BUFS][128 rows x 128 B]
+  uint8_t* sKV = sQ + C::Q_BUFS * C::Q_BYTES;           // [STAGES][K block | V block]
   uint8_t* sP = sKV + C::STAGES * C::STAGE_BYTES;       // [2][P_ATOMS][128 rows x 128 B]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * C::P_BYTES);
-  uint64_t* q_full = bars;        // [2]
-  uint64_t* q_empty = bars + 2;   // [2]
-  uint64_t* kv_full = bars + 4;   // [2]
-  uint64_t* kv_empty = bars + 6;  // [2]
-  uint64_t* s_full = bars + 8;    // [2]
-  uint64_t* p_full = bars + 10;   // [2]
-  uint64_t* pv_full = bars + 12;  // [2]
-  uint64_t* pv_free = bars + 14;  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
-  float* xch = reinterpret_cast<float*>(bars + 32);  // [2 rounds][2 halves][128 rows]
+  uint64_t* q_full = bars;        // [Q_BUFS <= 2]
+  uint64_t* q_empty = bars + 2;   // [Q_BUFS <= 2]
+  uint64_t* kv_full = bars + 4;   // [STAGES <= 3]
+  uint64_t* kv_empty = bars + 7;  // [STAGES <= 3]
+  uint64_t* s_full = bars + 10;   // [2]
+  uint64_t* p_full = bars + 12;   // [2]
+  uint64_t* pv_full = bars + 14;  // [2]
+  uint64_t* pv_free = bars + 16;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+  float* xch = reinterpret_cast<float*>(bars + 32);  // [2 rounds][SWQ parts][128 rows]
+  static_assert(C::Q_BUFS <= 2 && C::STAGES <= 3, "barrier slots");
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int HD = H * 64;
@@ -135,11 +142,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (threadIdx.x == 0) {
     prefetch_tmap(&tmQ);
     prefetch_tmap(&tmKV);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < C::Q_BUFS; ++i) {
       mbar_init(&q_full[i], 1);
       mbar_init(&q_empty[i], 1);
+    }
+    for (int i = 0; i < C::STAGES; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 4 * kTcSWQ);
       mbar_init(&pv_full[i], 1);
@@ -165,8 +176,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       bool ok = true;
       for (int u = blockIdx.x, qi = 0; u < units && ok; u += gridDim.x, ++qi) {
         const TcUnit t = tc_unit(u, H, seq, rows, nsub);
-        const int qb = qi & 1;
-        if (!tc_wait(&q_empty[qb], ((qi >> 1) & 1) ^ 1, kDevTimeoutSmemEmpty, 1)) break;
+        const int qb = qi % C::Q_BUFS;
+        if (!tc_wait(&q_empty[qb], ((qi / C::Q_BUFS) & 1) ^ 1, kDevTimeoutSmemEmpty, 1)) break;
         mbar_arrive_expect_tx(&q_full[qb], C::Q_BYTES);
         tma_load_2d(sQ + qb * C::Q_BYTES, &tmQ, &q_full[qb], t.head * 64, t.q0);
         for (int i = 0; i < t.nblk; ++i) {
@@ -212,8 +223,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       bool pending = false;  // PV of block jb - 1 not yet issued
       for (int u = blockIdx.x, qi = 0; u < units && ok; u += gridDim.x, ++qi) {
         const TcUnit t = tc_unit(u, H, seq, rows, nsub);
-        const int qb = qi & 1;
-        if (!tc_wait(&q_full[qb], (qi >> 1) & 1, kDevTimeoutTmaFull, 5)) break;
+        const int qb = qi % C::Q_BUFS;
+        if (!tc_wait(&q_full[qb], (qi / C::Q_BUFS) & 1, kDevTimeoutTmaFull, 5)) break;
         const uint32_t q_addr = smem_u32(sQ + qb * C::Q_BYTES);
         for (int i = 0; i < t.nblk; ++i, ++jb) {
           const int b = jb & 1;
@@ -250,7 +261,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     constexpr int ODIM = 64 / kTcSWQ;
     constexpr int NCH = KB / 32;
     const int quarter = warp & 3;
-    const int hf = (warp - kTcSoftWarp0) >> 2;
+    const int hf = (warp - kTcSoftWarp0) >> 2;  // which part of the quarter's columns
     const int row_t = quarter * 32 + lane;  // TMEM lane = query row in the unit
     const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
     const float sc = 0.125f * 1.4426950408889634f;  // 1/sqrt(64) in log2 units
@@ -270,12 +281,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int b = j & 1;
       if (!tc_wait(&pv_full[b], (j >> 1) & 1, kDevTimeoutAccFull, 8)) return false;
       tc_fence_after();
+      if constexpr (ODIM >= 32) {
 #pragma unroll
-      for (int h = 0; h < ODIM / 32; ++h) {
-        float pv[32];
-        tmem_ld32(lane_base + kTcPVCol + b * 64 + hf * ODIM + h * 32, pv);
+        for (int h = 0; h < ODIM / 32; ++h) {
+          float pv[32];
+          tmem_ld32(lane_base + kTcPVCol + b * 64 + hf * ODIM + h * 32, pv);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) o[h * 32 + i] = fmaf(o[h * 32 + i], alpha, pv[i]);
+          for (int i = 0; i < 32; ++i) o[h * 32 + i] = fmaf(o[h * 32 + i], alpha, pv[i]);
+        }
+      } else {
+        float pv[16];
+        tmem_ld16(lane_base + kTcPVCol + b * 64 + hf * ODIM, pv);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) o[i] = fmaf(o[i], alpha, pv[i]);
       }
       tc_fence_before();
       __syncwarp();
@@ -343,7 +361,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           if constexpr (kTcSWQ > 1) {
             xch[hf * kTcRows + row_t] = bm;
             pair_sync();
-            bm = fmaxf(xch[row_t], xch[kTcRows + row_t]);
+#pragma unroll
+            for (int w2 = 0; w2 < kTcSWQ; ++w2) bm = fmaxf(bm, xch[w2 * kTcRows + row_t]);
           }
           TC_SECTION(11)
           const float mnew = mine ? fmaxf(m, bm * sc) : m;
@@ -387,9 +406,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
           TC_SECTION(12)
           if constexpr (kTcSWQ > 1) {
-            xch[2 * kTcRows + hf * kTcRows + row_t] = rs;
+            xch[(kTcSWQ + hf) * kTcRows + row_t] = rs;
             pair_sync();
-            rs = xch[2 * kTcRows + row_t] + xch[3 * kTcRows + row_t];
+            rs = 0.f;
+#pragma unroll
+            for (int w2 = 0; w2 < kTcSWQ; ++w2) rs += xch[(kTcSWQ + w2) * kTcRows + row_t];
           }
           if (mine) {
             l = l * alpha + rs;
