@@ -277,3 +277,84 @@ class FrameEngine:
         if self.graph is None:
             raise RuntimeError("capture() first")
         self.graph.replay()
+
+
+class VideoEngine:
+    """The autoregressive video loop on the GPU (oasis_inference.py:2262-2310).
+
+    Each `step()` generates one frame for B sessions (S DDIM steps + bridge + VAE
+    through a FrameEngine, full-T or context-cached) and then rolls the context
+    window on the device: the generated latent patches are patch-embedded straight
+    into the newest context slot and the conditioning window rolls with them, so
+    no frame data goes back to the host between frames (the reference reads the
+    chunk back, unpatchifies and patch-embeds it on the host, :2296-2306).
+
+    Per-frame inputs: the noise chunk [B, 144, 64], the generated frame's
+    conditioning per step [S, B, 1024] and its context conditioning [B, 1024]
+    (stabilisation level, same action) for when it joins the window."""
+
+    def __init__(self, dw: DitDeviceWeights, vw: VaeDeviceWeights, batch: int, frames: int,
+                 steps: list[H.DdimStep] | None = None, kv: bool = False):
+        if frames < 2:
+            raise ValueError("the video loop needs a context window (frames >= 2)")
+        self.fe = FrameEngine(dw, vw, batch, frames, steps, kv=kv)
+        self.dw, self.B, self.T = dw, batch, frames
+        dev = dw.device
+        S = len(self.fe.steps)
+        self.ctx_cond = torch.zeros(batch, frames - 1, H.D_MODEL, device=dev)
+        self.gen_cond = torch.zeros(S, batch, H.D_MODEL, device=dev)      # staging, per frame
+        self.new_ctx_cond = torch.zeros(batch, H.D_MODEL, device=dev)    # staging, per frame
+        self._tmp_z = torch.empty(batch, max(frames - 2, 1), H.N_PATCHES, H.D_MODEL, device=dev)
+        self._tmp_c = torch.empty(batch, max(frames - 2, 1), H.D_MODEL, device=dev)
+        self.graph = None
+
+    @property
+    def context_z(self) -> torch.Tensor:
+        return self.fe.context_z
+
+    @property
+    def image(self) -> torch.Tensor:
+        return self.fe.image
+
+    def set_context(self, context_z: torch.Tensor, ctx_cond: torch.Tensor):
+        self.fe.context_z.copy_(context_z)
+        self.ctx_cond.copy_(ctx_cond)
+
+    def _frame_and_roll(self, stream=None):
+        fe, T = self.fe, self.T
+        fe.cond[:, :, :T - 1].copy_(self.ctx_cond.unsqueeze(0).expand(fe.cond.shape[0], -1, -1, -1))
+        fe.cond[:, :, T - 1].copy_(self.gen_cond)
+        fe.run(stream)
+        if T > 2:  # drop the oldest context frame (through a scratch copy: the ranges overlap)
+            self._tmp_z.copy_(fe.context_z[:, 1:])
+            fe.context_z[:, :-1].copy_(self._tmp_z)
+            self._tmp_c.copy_(self.ctx_cond[:, 1:])
+            self.ctx_cond[:, :-1].copy_(self._tmp_c)
+        # the generated latent patches -> newest context slot (rows (T-2) 144 .. of each session)
+        patch_embed(self.dw, fe.chunk.view(-1, H.OUT_DIM), fe.context_z, (T - 1) * H.N_PATCHES,
+                    (T - 2) * H.N_PATCHES, stream)
+        self.ctx_cond[:, -1].copy_(self.new_ctx_cond)
+
+    def step(self, noise: torch.Tensor, gen_cond: torch.Tensor, new_ctx_cond: torch.Tensor) -> torch.Tensor:
+        """One frame; returns the decoded image buffer [B, 3, 360, 640] (overwritten
+        by the next step)."""
+        self.fe.chunk.copy_(noise, non_blocking=True)
+        self.gen_cond.copy_(gen_cond, non_blocking=True)
+        self.new_ctx_cond.copy_(new_ctx_cond, non_blocking=True)
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self._frame_and_roll()
+        return self.fe.image
+
+    def capture(self):
+        """Records frame + context roll as one CUDA graph (its inputs are the
+        staging buffers `step()` fills). Runs one eager frame first: call it
+        before `set_context`, or set the context again afterwards."""
+        self._frame_and_roll()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._frame_and_roll()
+        self.graph = g
+        return g

@@ -255,3 +255,32 @@ def generate_frame(chunk: torch.Tensor, context_z: torch.Tensor | None, conds: l
     for c, co in zip(conds, coeffs):
         chunk, _ = ddim_step(chunk, context_z, c, co["at"], co["an"], dit_sd)
     return chunk, vae_decode(bridge(chunk), vae_sd)
+
+
+# ---- autoregressive video loop: oasis_inference.py:2262-2310 ---------------
+def context_roll(context_z: torch.Tensor, ctx_cond: torch.Tensor, chunk: torch.Tensor, new_cond: torch.Tensor,
+                 sd: dict) -> tuple[torch.Tensor, torch.Tensor]:
+    """Context update after a generated frame (oasis_inference.py:2296-2306): the
+    final chunk is unpatchified and patch-embedded (patch_embed_host), the window
+    drops its oldest frame and appends it; the conditioning window does the same
+    with the new frame's context conditioning. context_z [B, T-1, 144, 1024],
+    ctx_cond [B, T-1, 1024], chunk [B, 144, 64], new_cond [B, 1024]."""
+    new_z = patch_embed(unpatchify(chunk), sd)[:, None]
+    return (torch.cat([context_z[:, 1:], new_z], dim=1), torch.cat([ctx_cond[:, 1:], new_cond[:, None]], dim=1))
+
+
+def generate_video(noise: torch.Tensor, context_z: torch.Tensor, ctx_cond: torch.Tensor, gen_conds: torch.Tensor,
+                   new_ctx_conds: torch.Tensor, coeffs: list[dict], dit_sd: dict,
+                   vae_sd: dict) -> tuple[list[torch.Tensor], torch.Tensor, torch.Tensor]:
+    """F frames of the video loop (oasis_inference.py:2262-2310). noise [F, B, 144, 64]
+    (clamped, patchified), gen_conds [F, S, B, 1024] (the generated frame's
+    conditioning per DDIM step), new_ctx_conds [F, B, 1024] (its conditioning once
+    it joins the context). Returns the F decoded frames [B, 3, 360, 640] and the
+    final context and conditioning windows."""
+    images = []
+    for f in range(noise.shape[0]):
+        conds = [torch.cat([ctx_cond, gen_conds[f, i][:, None]], dim=1) for i in range(len(coeffs))]
+        chunk, img = generate_frame(noise[f].clone(), context_z, conds, coeffs, dit_sd, vae_sd)
+        images.append(img)
+        context_z, ctx_cond = context_roll(context_z, ctx_cond, chunk, new_ctx_conds[f], dit_sd)
+    return images, context_z, ctx_cond

@@ -247,3 +247,48 @@ def test_dropin_kv_functions(dit_small):
     v = OI.dit_forward_currentonly(z[0, 1].to(DEV), cond[0, 1].to(DEV), dw, scr)
     torch.cuda.synchronize()
     assert rel_l2(v, full[H.N_PATCHES:]) < 5e-3
+
+
+@pytest.fixture(scope="module")
+def video_case(dit_full, vae_full):
+    """Inputs of a 3-frame loop (B=1, T=3) and the oracle's frames and final windows."""
+    dsd, _ = dit_full
+    vsd, _ = vae_full
+    B, T, F_ = 1, 3, 3
+    g = torch.Generator().manual_seed(11)
+    steps = H.ddim_schedule()
+    ctx_lat = torch.randn(B * (T - 1), 16, 18, 32, generator=g)
+    ctx_z = O.patch_embed(ctx_lat, dsd).reshape(B, T - 1, H.N_PATCHES, H.D_MODEL).contiguous()
+    noise = H.patchify(torch.randn(F_ * B, 16, 18, 32, generator=g).clamp(-H.NOISE_ABS_MAX, H.NOISE_ABS_MAX))
+    noise = noise.reshape(F_, B, H.N_PATCHES, H.OUT_DIM)
+    acts = torch.zeros(F_, B, 25)
+    acts[..., 3] = 1
+    ctx_cond = O.cond_vector(torch.full((B * (T - 1),), H.STABILIZATION_LEVEL - 1), None, dsd).reshape(B, T - 1, -1)
+    gen_conds = torch.stack([torch.stack([O.cond_vector(torch.full((B,), st.noise_level), acts[f], dsd)
+                                          for st in steps]) for f in range(F_)])  # [F, S, B, D]
+    new_ctx = torch.stack([O.cond_vector(torch.full((B,), H.STABILIZATION_LEVEL - 1), acts[f], dsd)
+                           for f in range(F_)])  # [F, B, D]
+    coeffs = [{"at": st.at_sqrt ** 2, "an": st.an_sqrt ** 2} for st in steps]
+    ref = O.generate_video(noise, ctx_z, ctx_cond, gen_conds, new_ctx, coeffs, dsd, vsd)
+    return dict(B=B, T=T, F=F_, steps=steps, ctx_z=ctx_z, ctx_cond=ctx_cond, noise=noise, gen_conds=gen_conds,
+                new_ctx=new_ctx, ref=ref)
+
+
+@pytest.mark.parametrize("kv", [False, True])
+def test_video_loop_matches_oracle(dit_full, vae_full, video_case, kv):
+    """Three frames of the autoregressive loop (context window rolled on the
+    device, graph-replayed; full-T and context-cached frames) against the
+    oracle's loop: every decoded frame and the final windows."""
+    _, dw = dit_full
+    _, vw = vae_full
+    c = video_case
+    ref_imgs, cz, cc = c["ref"]
+    ve = E.VideoEngine(dw, vw, c["B"], c["T"], c["steps"], kv=kv)
+    ve.capture()
+    ve.set_context(c["ctx_z"].to(DEV), c["ctx_cond"].to(DEV))
+    for f in range(c["F"]):
+        img = ve.step(c["noise"][f].to(DEV), c["gen_conds"][f].to(DEV), c["new_ctx"][f].to(DEV))
+        torch.cuda.synchronize()
+        assert rel_l2(img, ref_imgs[f]) < REL_L2_TOL and cosine(img, ref_imgs[f]) > COS_TOL, (f, rel_l2(img, ref_imgs[f]))
+    assert rel_l2(ve.context_z, cz) < REL_L2_TOL
+    assert torch.allclose(ve.ctx_cond.cpu(), cc, atol=1e-5)
