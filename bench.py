@@ -322,7 +322,20 @@ def kv_frame(dw, vw, sess0, B, T, steps, PAR, sessions):
     out = {"frames_per_sec": round(sessions * steps / (ms / 1000.0), 3), "ms_per_frame": round(ms / steps, 3),
            "dit_tflop_per_frame_gpu": round((ctx + cur) / 1e12, 2),
            "path": "oasis_generate_frame_kv: context rows once per frame, generated frame per DDIM step"}
+    # the autoregressive loop: the same frames plus the on-device context roll
+    # (patch embed of the generated latent into the window), one graph per frame
+    ve = E.VideoEngine(dw, vw, B, T, kv=True)
+    ve.capture()
+    ve.set_context(fe.context_z, fe.cond[0, :, :T - 1])
+    noise, gen, new_ctx = fe.chunk.clone(), fe.cond[:, :, T - 1].clone(), fe.cond[0, :, 0].clone()
     del fe
+    for _ in range(2):
+        ve.step(noise, gen, new_ctx)
+    torch.cuda.synchronize()
+    PAR.barrier()
+    ms_v = PAR.max_over_ranks(time_graph(lambda: ve.step(noise, gen, new_ctx), steps))
+    out["video_loop_frames_per_sec"] = round(sessions * steps / (ms_v / 1000.0), 3)
+    del ve
     torch.cuda.empty_cache()
     return out
 
