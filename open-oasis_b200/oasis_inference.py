@@ -30,6 +30,7 @@ from __future__ import annotations
 
 import torch
 
+from . import checkpoint as CK
 from . import engine as E
 from . import host as H
 from .host import sigmoid_beta_schedule, timestep_embedding  # noqa: F401  (reference names)
@@ -41,8 +42,11 @@ N_PATCHES = H.N_PATCHES
 OUT_DIM = H.OUT_DIM
 
 
-def preload_dit_weights(state_dict: dict, device="cuda", n_frames: int = 2) -> DitDeviceWeights:
-    """Packs a reference-keyed DiT state dict onto the GPU (bf16 GEMM weights)."""
+def preload_dit_weights(state_dict, device="cuda", n_frames: int = 2) -> DitDeviceWeights:
+    """Packs a reference-keyed DiT state dict (or the path of the released
+    safetensors file) onto the GPU (bf16 GEMM weights)."""
+    if isinstance(state_dict, str):
+        state_dict = CK.load_dit_checkpoint(state_dict)
     return DitDeviceWeights(state_dict, device)
 
 
@@ -151,7 +155,11 @@ def compute_cond_for_frame(t_scalar, action_vec, dev: DitDeviceWeights, scr=None
     return c.to(dev.device)
 
 
-def preload_vae_decoder_weights(vae_state_dict: dict, device="cuda") -> VaeDeviceWeights:
+def preload_vae_decoder_weights(vae_state_dict, device="cuda", rotary_table=None) -> VaeDeviceWeights:
+    """Packs the VAE decoder (state dict, or the path of the released safetensors
+    file plus optionally the (18, 32, 32) pixel RoPE table of the VAE module)."""
+    if isinstance(vae_state_dict, str):
+        vae_state_dict = CK.load_vae_checkpoint(vae_state_dict, rotary_table)
     return VaeDeviceWeights(vae_state_dict, device)
 
 

@@ -205,7 +205,9 @@ class VaeDeviceWeights:
         self.norm_b = f32(sd["dec_norm.bias"])
         self.pred_w = bf(sd["predictor.weight"])
         self.pred_b = f32(sd["predictor.bias"])
-        self.rope = f32(H.rope_pair_table(H.vae_rope_angles(sd["rotary_freqs"].float())))
+        # per-token angles from a checkpoint's RoPE table, else the axial frequencies
+        ang = sd["rotary_angles"].float() if "rotary_angles" in sd else H.vae_rope_angles(sd["rotary_freqs"].float())
+        self.rope = f32(H.rope_pair_table(ang))
 
         st = _lib.OasisVaeWeights()
         st.num_blocks = nb

@@ -230,7 +230,8 @@ def n_vae_blocks(sd: dict) -> int:
 def vae_decode(latent: torch.Tensor, sd: dict) -> torch.Tensor:
     """latent (B, 576, 16) -> image (B, 3, 360, 640) clamped to [-1, 1]."""
     b = latent.shape[0]
-    fr = vae_rope_freqs(sd["rotary_freqs"].float())  # (576, 32)
+    # (576, 32): a checkpoint's per-token RoPE table, else the axial frequencies
+    fr = sd["rotary_angles"].float() if "rotary_angles" in sd else vae_rope_freqs(sd["rotary_freqs"].float())
     x = F.linear(latent, sd["post_quant_conv.weight"], sd["post_quant_conv.bias"])
     for i in range(n_vae_blocks(sd)):
         p = f"decoder.{i}"
