@@ -75,7 +75,6 @@ __device__ unsigned long long g_gemm_prof[8];
 
 struct SplitK {
   float* partials;  // [tiles][splits][BM][BN]
-  int* unused;
   int splits;       // CTAs per tile (one cluster), each summing K / splits
 };
 
@@ -709,7 +708,7 @@ int launch_bn(const GemmProblem& p, int splits, cudaStream_t stream) {
   else
     tr = to;
   const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
-  SplitK sk{nullptr, nullptr, splits};
+  SplitK sk{nullptr, splits};
   if (splits > 1) {
     const size_t need = (size_t)tiles * splits * BM * BN * sizeof(float);
     if (!p.workspace || p.workspace_bytes < need)
