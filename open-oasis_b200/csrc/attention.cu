@@ -647,8 +647,8 @@ int attention_full_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, int grou
   OASIS_REQUIRE(H >= 1 && H <= 16, "attention_full: heads=%d outside [1, 16]", H);
   if (groups == 0) return OASIS_OK;
   // The tcgen05 kernel (attention_tc.cu) runs every length it supports
-  // (multiples of 144): measured 225 -> 214 us for 512 DiT frames and
-  // 400 -> 250 us for 64 VAE frames against the mma.sync kernels below, which
+  // (multiples of 144): measured 225 -> 207 us for 512 DiT frames and
+  // 400 -> 243 us for 64 VAE frames against the mma.sync kernels below, which
   // serve other lengths. OASIS_ATTN_TC=0 selects the mma.sync kernels.
   static const int tc_mode = [] {
     const char* e = getenv("OASIS_ATTN_TC");

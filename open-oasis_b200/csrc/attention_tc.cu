@@ -333,7 +333,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tc_fence_after();
         uint8_t* prow = sP + b * C::P_BYTES + row_t * 128;
         float alpha = 1.f;
-#ifdef OASIS_TC_PROF
+#ifdef OASIS_TC_PROF_SECTIONS
         long long pt = clock64();
 #define TC_SECTION(i) if (lane == 0) { const long long n_ = clock64(); atomicAdd(&g_tc_prof[i], (unsigned long long)(n_ - pt)); pt = n_; }
 #else
@@ -341,23 +341,29 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #endif
         if (__any_sync(0xffffffffu, mine)) {  // same rows, same decision in both halves
           const uint32_t sbase = lane_base + b * kTcSCols;
-          // pass 1: row max of this block (TMEM loads are warp-collective)
+          // this part's S columns into registers with one TMEM round trip
+          // (loads are warp-collective), then the row max and p = exp2(s c - m)
+          constexpr int CPT = (NCH + kTcSWQ - 1) / kTcSWQ;  // 32-column chunks per part
+          constexpr bool TAIL = KB % 32 != 0;
+          const bool has_tail = TAIL && hf == kTcSWQ - 1;
+          uint32_t sr[CPT][32];
+          uint32_t st16[16];
+#pragma unroll
+          for (int i2 = 0; i2 < CPT; ++i2)
+            if (hf + i2 * kTcSWQ < NCH) tmem_ld32_issue(sbase + (hf + i2 * kTcSWQ) * 32, sr[i2]);
+          if (has_tail) tmem_ld16_issue(sbase + NCH * 32, st16);
+#pragma unroll
+          for (int i2 = 0; i2 < CPT; ++i2) tmem_wait_ld(sr[i2]);
+          tmem_wait_ld(st16);
           float bm = -1e30f;
 #pragma unroll
-          for (int c = hf; c < NCH; c += kTcSWQ) {
-            float s[32];
-            tmem_ld32(sbase + c * 32, s);
+          for (int i2 = 0; i2 < CPT; ++i2)
+            if (hf + i2 * kTcSWQ < NCH)
 #pragma unroll
-            for (int k = 0; k < 32; ++k) bm = fmaxf(bm, s[k]);
-          }
-          if constexpr (KB % 32 != 0) {
-            if (hf == kTcSWQ - 1) {
-              float s[16];
-              tmem_ld16(sbase + NCH * 32, s);
+              for (int k = 0; k < 32; ++k) bm = fmaxf(bm, __uint_as_float(sr[i2][k]));
+          if (has_tail)
 #pragma unroll
-              for (int k = 0; k < 16; ++k) bm = fmaxf(bm, s[k]);
-            }
-          }
+            for (int k = 0; k < 16; ++k) bm = fmaxf(bm, __uint_as_float(st16[k]));
           if constexpr (kTcSWQ > 1) {
             xch[hf * kTcRows + row_t] = bm;
             pair_sync();
@@ -367,42 +373,28 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           TC_SECTION(11)
           const float mnew = mine ? fmaxf(m, bm * sc) : m;
           alpha = mine ? ex2_approx(m - mnew) : 1.f;
-          // pass 2: p = exp2(s c - m), row sum, bf16 P in the swizzled operand layout
           float rs = 0.f;
+          auto emit = [&](const uint32_t* sv, int chunk) {  // 8 keys -> one 16-byte P chunk
+            uint32_t pk[4];
 #pragma unroll
-          for (int c = hf; c < NCH; c += kTcSWQ) {
-            float s[32];
-            tmem_ld32(sbase + c * 32, s);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint32_t pk[4];
-#pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                const float p0 = mine ? ex2_approx(fmaf(s[8 * q + 2 * k], sc, -mnew)) : 0.f;
-                const float p1 = mine ? ex2_approx(fmaf(s[8 * q + 2 * k + 1], sc, -mnew)) : 0.f;
-                rs += p0 + p1;
-                pk[k] = pack_bf16x2(p0, p1);
-              }
-              store_p(prow, c * 4 + q, pk);
+            for (int k = 0; k < 4; ++k) {
+              const float p0 = mine ? ex2_approx(fmaf(__uint_as_float(sv[2 * k]), sc, -mnew)) : 0.f;
+              const float p1 = mine ? ex2_approx(fmaf(__uint_as_float(sv[2 * k + 1]), sc, -mnew)) : 0.f;
+              rs += p0 + p1;
+              pk[k] = pack_bf16x2(p0, p1);
             }
+            store_p(prow, chunk, pk);
+          };
+#pragma unroll
+          for (int i2 = 0; i2 < CPT; ++i2) {
+            const int c = hf + i2 * kTcSWQ;
+            if (c < NCH)
+#pragma unroll
+              for (int q = 0; q < 4; ++q) emit(&sr[i2][8 * q], c * 4 + q);
           }
-          if constexpr (KB % 32 != 0) {
-            if (hf == kTcSWQ - 1) {
-              float s[16];
-              tmem_ld16(sbase + NCH * 32, s);
-#pragma unroll
-              for (int q = 0; q < 2; ++q) {
-                uint32_t pk[4];
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                  const float p0 = mine ? ex2_approx(fmaf(s[8 * q + 2 * k], sc, -mnew)) : 0.f;
-                  const float p1 = mine ? ex2_approx(fmaf(s[8 * q + 2 * k + 1], sc, -mnew)) : 0.f;
-                  rs += p0 + p1;
-                  pk[k] = pack_bf16x2(p0, p1);
-                }
-                store_p(prow, NCH * 4 + q, pk);
-              }
-            }
+          if (has_tail) {
+            emit(&st16[0], NCH * 4);
+            emit(&st16[8], NCH * 4 + 1);
           }
           TC_SECTION(12)
           if constexpr (kTcSWQ > 1) {
