@@ -22,7 +22,7 @@ def _s():
 
 
 def gemm(a, w, mode, out, *, bias=None, resid=None, gate=None, ldg=0, rows_per_frame=1, rope=None,
-         rope_div=1, rope_mod=1, block_n=0, splits=0, ws=None):
+         rope_div=1, rope_mod=1, rope_dim=0, block_n=0, splits=0, ws=None):
     M, K = a.shape
     N = w.shape[0]
     args = _lib.OasisGemmArgs()
@@ -32,7 +32,7 @@ def gemm(a, w, mode, out, *, bias=None, resid=None, gate=None, ldg=0, rows_per_f
     args.bias = _lib.ptr(bias)
     args.resid, args.ldr = _lib.ptr(resid), N
     args.gate, args.ldg, args.rows_per_frame = _lib.ptr(gate), ldg, rows_per_frame
-    args.rope, args.rope_div, args.rope_mod = _lib.ptr(rope), rope_div, rope_mod
+    args.rope, args.rope_div, args.rope_mod, args.rope_dim = _lib.ptr(rope), rope_div, rope_mod, rope_dim
     args.block_n, args.splits = block_n, splits
     if ws is not None:
         args.workspace, args.workspace_bytes = ws.data_ptr(), ws.numel()
@@ -117,16 +117,16 @@ def test_gemm_residual():
     assert rel_l2(z, ref) < 1e-5
 
 
-def _rope_ref(x, tab, pos):
-    """x [M, 3072] fp32; rotate q/k column pairs with tab[pos[r], pair]."""
+def _rope_ref(x, tab, pos, hd=1024):
+    """x [M, 3 hd] fp32; rotate q/k column pairs with tab[pos[r], pair]."""
     out = x.clone()
-    c = tab[pos][:, :, 0].repeat(1, 16)  # (M, 512) one entry per pair across 16 heads
-    s = tab[pos][:, :, 1].repeat(1, 16)
+    c = tab[pos][:, :, 0].repeat(1, hd // 64)  # one entry per pair across the heads
+    s = tab[pos][:, :, 1].repeat(1, hd // 64)
     for sec in range(2):
-        seg = x[:, sec * 1024:(sec + 1) * 1024]
+        seg = x[:, sec * hd:(sec + 1) * hd]
         x0, x1 = seg[:, 0::2], seg[:, 1::2]
-        out[:, sec * 1024:(sec + 1) * 1024][:, 0::2] = x0 * c - x1 * s
-        out[:, sec * 1024:(sec + 1) * 1024][:, 1::2] = x1 * c + x0 * s
+        out[:, sec * hd:(sec + 1) * hd][:, 0::2] = x0 * c - x1 * s
+        out[:, sec * hd:(sec + 1) * hd][:, 1::2] = x1 * c + x0 * s
     return out
 
 
@@ -149,6 +149,31 @@ def test_gemm_rope(kind):
     pos = (torch.arange(M, device=DEV) // div) % mod
     ref = _rope_ref(x, tab_d, pos)
     assert rel_l2(out.float(), ref) < 5e-3
+
+
+@pytest.mark.parametrize("n", [2, 4, 8])
+def test_tensor_parallel_shard_shapes(n):
+    """The GEMM shapes one rank runs under n-way tensor parallelism (QKV + RoPE on
+    its 16 / n heads, O and FC2 row shards with K = 1024 / n and 4096 / n, FC1
+    column shard) against PyTorch, at the C5 row count of one DiT step slice."""
+    M, D, HD = 2 * 144 * 3, 1024, 1024 // n
+    a = rand_bf16(M, D, seed=21)
+    tab = H.rope_pair_table(H.temporal_rope_angles(H.default_temporal_freqs())).to(DEV)
+    w = rand_bf16(3 * HD, D, scale=0.05, seed=22)
+    qkv = torch.empty(M, 3 * HD, device=DEV, dtype=torch.bfloat16)
+    gemm(a, w, 6, qkv, rope=tab, rope_div=144, rope_mod=3, rope_dim=HD)
+    pos = (torch.arange(M, device=DEV) // 144) % 3
+    ref = _rope_ref(a.float() @ w.float().T, tab, pos, hd=HD)
+    assert rel_l2(qkv.float(), ref) < 5e-3
+    for K in (HD, 4 * HD):  # O and FC2 row shards: fp32 partials
+        x, wo = rand_bf16(M, K, seed=23 + K), rand_bf16(D, K, scale=0.05, seed=24 + K)
+        part = torch.empty(M, D, device=DEV)
+        gemm(x, wo, 0, part)
+        assert rel_l2(part, x.float() @ wo.float().T) < 1e-5
+    w1, b1 = rand_bf16(4 * HD, D, scale=0.05, seed=25), torch.randn(4 * HD, device=DEV) * 0.1
+    h = torch.empty(M, 4 * HD, device=DEV, dtype=torch.bfloat16)
+    gemm(a, w1, 2, h, bias=b1)
+    assert rel_l2(h.float(), F.gelu(a.float() @ w1.float().T + b1, approximate="tanh")) < 5e-3
 
 
 def test_gemm_image():
@@ -261,16 +286,20 @@ def test_attention_tc(groups, seq, H):
     assert rel_l2(out.float(), ref) < 1e-2, rel_l2(out.float(), ref)
 
 
-@pytest.mark.parametrize("B,T", [(1, 1), (1, 2), (2, 8), (1, 32), (3, 5)])
-def test_attention_temporal(B, T):
-    P = 144
-    qkv = rand_bf16(B * T * P, 3072, seed=B * 100 + T)
-    out = torch.empty(B * T * P, 1024, device=DEV, dtype=torch.bfloat16)
-    _lib.call("oasis_attention_temporal", qkv.data_ptr(), out.data_ptr(), B, T, 16, _s())
+@pytest.mark.parametrize("B,T,H", [(1, 1, 16), (1, 2, 16), (2, 8, 16), (1, 32, 16), (3, 5, 16), (2, 8, 8), (1, 16, 4),
+                                   (2, 8, 2), (1, 32, 2)])
+def test_attention_temporal(B, T, H):
+    """Causal temporal attention (H = 16, or 16 / n heads per rank under n-way
+    tensor parallelism: a warp's 256 columns then cover fewer than four heads)."""
+    P, HD = 144, H * 64
+    qkv = rand_bf16(B * T * P, 3 * HD, seed=B * 100 + T + H)
+    out = torch.full((B * T * P, HD), float("nan"), device=DEV, dtype=torch.bfloat16)
+    _lib.call("oasis_attention_temporal", qkv.data_ptr(), out.data_ptr(), B, T, H, _s())
     torch.cuda.synchronize()
-    x = qkv.float().reshape(B, T, P, 3, 16, 64).permute(3, 0, 2, 4, 1, 5)  # 3 B P H T D
+    x = qkv.float().reshape(B, T, P, 3, H, 64).permute(3, 0, 2, 4, 1, 5)  # 3 B P H T D
     mask = torch.tril(torch.ones(T, T, dtype=torch.bool, device=DEV))
-    ref = _attn_ref(x[0], x[1], x[2], mask).permute(0, 3, 1, 2, 4).reshape(B * T * P, 1024)
+    ref = _attn_ref(x[0], x[1], x[2], mask).permute(0, 3, 1, 2, 4).reshape(B * T * P, HD)
+    assert not torch.isnan(out.float()).any()
     assert rel_l2(out.float(), ref) < 1e-2
 
 
