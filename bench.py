@@ -234,8 +234,9 @@ def gemm_roofline(M, reps, peaks):
     resid = torch.zeros(M, 1024, device=dev)
     frames = (M + 143) // 144
     gate = torch.randn(frames, 6144, device=dev)
-    rope = torch.zeros(144, 32, 2, device=dev)
+    rope = torch.zeros(16, 144, 4, device=dev)  # identity rotation, the kernel's table layout
     rope[..., 0] = 1
+    rope[..., 2] = 1
     bias = torch.zeros(4096, device=dev)
     total_f, total_ms, per = 0.0, 0.0, {}
     for name, N, K, mode in shapes:

@@ -43,6 +43,7 @@ typedef void* oasis_stream_t; /* cudaStream_t */
 #define OASIS_DIT_SUBBLOCKS 32       /* blocks.{0..15}.{s,t} interleaved: 2i = spatial, 2i+1 = temporal */
 #define OASIS_ADALN_WIDTH 6144       /* per sub-block adaLN output (shift, 1+scale, gate) x (msa, mlp) */
 #define OASIS_ADALN_ROWS (OASIS_DIT_SUBBLOCKS * OASIS_ADALN_WIDTH + 2048) /* + final (shift, 1+scale) */
+#define OASIS_MAX_FRAMES 32          /* temporal positions of rope_temporal (T <= 32) */
 #define OASIS_VAE_BLOCKS 12
 
 /* ---------------------------------------------------------------- errors -- */
@@ -89,8 +90,8 @@ typedef struct OasisDitWeights {
   const float* embed_w; /* [64, 1024] */
   const float* embed_b; /* [1024] */
   /* RoPE tables as (cos, sin) pairs per position and head-dim pair. */
-  const float* rope_spatial;  /* [144, 32, 2] axial (h, w) */
-  const float* rope_temporal; /* [32, 32, 2]  frame index t < 32 */
+  const float* rope_spatial;  /* [16, 144, 4] axial (h, w): (cos, sin) of pairs 2q, 2q+1 at [q, pos] */
+  const float* rope_temporal; /* [16, 32, 4]  frame index t < 32, same layout */
 } OasisDitWeights;
 
 typedef struct OasisVaeBlock {
@@ -110,7 +111,7 @@ typedef struct OasisVaeWeights {
   const float* norm_w; const float* norm_b; /* dec_norm [1024] */
   const void* pred_w;                       /* bf16 [1200, 1024] predictor */
   const float* pred_b;                      /* [1200] */
-  const float* rope;                        /* [576, 32, 2]; pairs >= 16 are (1, 0) */
+  const float* rope;                        /* [16, 576, 4] as rope_spatial; pairs >= 16 are (1, 0) */
 } OasisVaeWeights;
 
 /* ---------------------------------------------------------- composite ---- */
@@ -259,7 +260,9 @@ int oasis_generate_frame_kv(const OasisDitWeights* w, const OasisVaeWeights* vw,
  *   4 GATED_RESID  out_f32 = resid + gate[r / rows_per_frame, n] * acc   (O / FC2)
  *   5 RESID        out_f32 = resid + acc              (VAE proj / FC2)
  *   6 ROPE         out_bf16 = acc with interleaved RoPE on columns [0, 2 rope_dim)
- *                  at position (r / rope_div) % rope_mod    (QKV + rope_layout)
+ *                  at position (r / rope_div) % rope_mod    (QKV + rope_layout);
+ *                  rope[(q * rope_stride + pos) * 4 + {0..3}] = (cos, sin) of the
+ *                  head-dim pairs 2q and 2q + 1
  *   7 IMAGE        VAE predictor: scatter 20x20x3 patches into [frames, 3, 360, 640],
  *                  clamped to [-1, 1]
  * K must be a multiple of 64 and N of 16. Split-K needs `workspace`. */
@@ -277,6 +280,7 @@ typedef struct OasisGemmArgs {
   int splits;  /* 0 = heuristic, 1 = none */
   void* workspace; size_t workspace_bytes;
   int rope_dim; /* ROPE: width of the q (and k) section; 0 = 1024 (16 heads) */
+  int rope_stride; /* ROPE: positions per row of the [16, positions, 4] table; 0 = rope_mod */
 } OasisGemmArgs;
 
 int oasis_gemm(const OasisGemmArgs* a, oasis_stream_t stream);

@@ -93,7 +93,8 @@ class OasisGemmArgs(C.Structure):
                 ("mode", C.c_int), ("out", vp), ("ldo", C.c_longlong), ("bias", fp), ("resid", fp),
                 ("ldr", C.c_longlong), ("gate", fp), ("ldg", C.c_longlong), ("rows_per_frame", C.c_int),
                 ("rope", fp), ("rope_div", C.c_int), ("rope_mod", C.c_int), ("block_n", C.c_int),
-                ("splits", C.c_int), ("workspace", vp), ("workspace_bytes", C.c_size_t), ("rope_dim", C.c_int)]
+                ("splits", C.c_int), ("workspace", vp), ("workspace_bytes", C.c_size_t), ("rope_dim", C.c_int),
+                ("rope_stride", C.c_int)]
 
 
 class OasisLayerNormArgs(C.Structure):

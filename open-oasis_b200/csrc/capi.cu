@@ -181,8 +181,9 @@ int dit_blocks(const OasisDitWeights* w, int B, int T, float* z, const float* ad
       p.epi.rope = spatial ? w->rope_spatial : w->rope_temporal;
       p.epi.rope_div = spatial ? 1 : kP;
       p.epi.rope_mod = spatial ? kP : T;
+      p.epi.rope_stride = spatial ? kP : OASIS_MAX_FRAMES;
       if (!spatial && kv.mode == kKvUse) {  // every row sits at temporal position Tp
-        p.epi.rope = w->rope_temporal + (size_t)kv.past_frames * 64;
+        p.epi.rope = w->rope_temporal + (size_t)kv.past_frames * 4;
         p.epi.rope_div = 1;
         p.epi.rope_mod = 1;
       }
@@ -349,6 +350,7 @@ int vae_decode_impl(const OasisVaeWeights* w, const OasisVaeArgs* a, cudaStream_
       p.epi.rope = w->rope;
       p.epi.rope_div = 1;
       p.epi.rope_mod = kVaeTok;
+      p.epi.rope_stride = kVaeTok;
       OASIS_TRY(gemm_launch(p, st));
     }
     OASIS_TRY(attention_full_launch(s.qkv, s.attn, B, kVaeTok, 16, st));
@@ -779,6 +781,7 @@ int oasis_gemm(const OasisGemmArgs* a, oasis_stream_t stream) {
   p.epi.rope_div = a->rope_div > 0 ? a->rope_div : 1;
   p.epi.rope_mod = a->rope_mod > 0 ? a->rope_mod : 1;
   p.epi.rope_dim = a->rope_dim > 0 ? a->rope_dim : 1024;
+  p.epi.rope_stride = a->rope_stride > 0 ? a->rope_stride : p.epi.rope_mod;
   p.block_n = a->block_n;
   p.splits = a->splits;
   p.workspace = a->workspace;

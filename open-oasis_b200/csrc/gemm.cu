@@ -118,10 +118,12 @@ __device__ __forceinline__ void epilogue_math(const EpiParams& e, int r, int nb,
       if (nb < 2 * e.rope_dim) {
         // pairs (2j, 2j+1) of a 64-wide head rotate by the angle of (pos, pair)
         const int pos = (r / e.rope_div) % e.rope_mod;
-        const float4* tab = reinterpret_cast<const float4*>(e.rope + pos * 64 + (nb & 63));
+        // pair quads q0 .. q0 + 7 of these 32 columns; consecutive rows of a warp
+        // read consecutive positions of one quad row
+        const float4* tab = reinterpret_cast<const float4*>(e.rope) + (long long)((nb & 63) >> 2) * e.rope_stride + pos;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const float4 cs = __ldg(tab + j);  // (cos, sin) of two consecutive pairs
+          const float4 cs = __ldg(tab + (long long)j * e.rope_stride);  // (cos, sin) of two consecutive pairs
           const float x0 = v[4 * j], x1 = v[4 * j + 1], x2 = v[4 * j + 2], x3 = v[4 * j + 3];
           v[4 * j] = x0 * cs.x - x1 * cs.y;
           v[4 * j + 1] = x1 * cs.x + x0 * cs.y;

@@ -29,9 +29,10 @@ struct EpiParams {
   const float* gate = nullptr;    // gated residual: gate[(r / rows_per_frame) * ldg + n]
   long long ldg = 0;
   int rows_per_frame = 1;
-  const float* rope = nullptr;    // (cos, sin) pairs: rope[(pos * 32 + pair) * 2 + {0,1}]
+  const float* rope = nullptr;    // rope[(q * rope_stride + pos) * 4 + {0..3}]: (cos, sin) of pairs 2q, 2q+1
   int rope_div = 1;               // pos = (r / rope_div) % rope_mod
   int rope_mod = 1;
+  int rope_stride = 1;            // positions per q row of the table
   int rope_dim = 1024;            // q occupies [0, rope_dim), k [rope_dim, 2 rope_dim)
   int img_grid_w = 32;            // image mode: tokens per patch row
   int img_tokens = 576;           // image mode: tokens per frame

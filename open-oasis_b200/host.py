@@ -175,6 +175,16 @@ def vae_rope_angles(freqs: torch.Tensor) -> torch.Tensor:
     return ang.reshape(VAE_TOKENS, VAE_ROT_DIM)
 
 
+def rope_quad_table(angles: torch.Tensor, pairs: int = 32) -> torch.Tensor:
+    """The layout the GEMM's RoPE epilogue reads: (pairs / 2, positions, 4) with
+    (cos, sin) of pairs 2q and 2q + 1 at [q, pos]. Threads of a warp hold
+    consecutive rows, i.e. consecutive (or equal) positions, so each table load
+    of a warp is one contiguous run."""
+    tab = rope_pair_table(angles, pairs)  # (pos, pairs, 2)
+    pos = tab.shape[0]
+    return tab.reshape(pos, pairs // 2, 4).permute(1, 0, 2).contiguous()
+
+
 def rope_pair_table(angles: torch.Tensor, pairs: int = 32) -> torch.Tensor:
     """(positions, pairs, 2) (cos, sin) per head-dim pair as the kernels read it.
     Pairs beyond the rotated dims get (1, 0)."""

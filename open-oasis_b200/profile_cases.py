@@ -38,8 +38,9 @@ def gemm(a):
     out = torch.empty(M, N, device="cuda", dtype=torch.float32)
     bias = torch.zeros(N, device="cuda")
     gate = torch.randn((M + 143) // 144, N, device="cuda")
-    rope = torch.zeros(144, 32, 2, device="cuda")
+    rope = torch.zeros(16, 144, 4, device="cuda")  # identity rotation, the kernel's table layout
     rope[..., 0] = 1
+    rope[..., 2] = 1
     args = _lib.OasisGemmArgs()
     args.a, args.lda, args.w, args.m, args.n, args.k, args.mode = A.data_ptr(), K, W.data_ptr(), M, N, K, a.mode
     args.out, args.ldo, args.bias = out.data_ptr(), N, bias.data_ptr()

@@ -78,11 +78,12 @@ def _st() -> int:
     return torch.cuda.current_stream().cuda_stream
 
 
-def _gemm(a, w, m, n, k, mode, out, *, bias=None, rope=None, rope_div=1, rope_mod=1, rope_dim=0):
+def _gemm(a, w, m, n, k, mode, out, *, bias=None, rope=None, rope_div=1, rope_mod=1, rope_dim=0, rope_stride=0):
     g = _lib.OasisGemmArgs()
     g.a, g.lda, g.w, g.m, g.n, g.k, g.mode = a.data_ptr(), k, w.data_ptr(), m, n, k, mode
     g.out, g.ldo, g.bias = out.data_ptr(), n, _lib.ptr(bias)
     g.rope, g.rope_div, g.rope_mod, g.rope_dim = _lib.ptr(rope), rope_div, rope_mod, rope_dim
+    g.rope_stride = rope_stride
     _lib.call("oasis_gemm", C.byref(g), _st())
 
 
@@ -126,7 +127,8 @@ def dit_forward_tp(tpw: TPDitWeights, z: torch.Tensor, cond: torch.Tensor, v_out
         off = i * 6144
         _ln(zf, sc.xn, M, sc.adaln, ldm, off, off + D)
         _gemm(sc.xn, w["qkv_w"], M, 3 * dl, D, 6, sc.qkv, rope=full.rope_spatial if spatial else full.rope_temporal,
-              rope_div=1 if spatial else 144, rope_mod=144 if spatial else T, rope_dim=dl)
+              rope_div=1 if spatial else 144, rope_mod=144 if spatial else T, rope_dim=dl,
+              rope_stride=144 if spatial else H.MAX_T)
         if spatial:
             _lib.call("oasis_attention_spatial", sc.qkv.data_ptr(), sc.attn.data_ptr(), F, 144, tpw.heads, _st())
         else:

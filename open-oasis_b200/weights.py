@@ -149,8 +149,8 @@ class DitDeviceWeights:
         self.final_b = f32(sd["final_layer.linear.bias"])
         self.embed_w = f32(H.patch_embed_matrix(sd["x_embedder.proj.weight"]))
         self.embed_b = f32(sd["x_embedder.proj.bias"])
-        self.rope_spatial = f32(H.rope_pair_table(H.spatial_rope_angles(sd["blocks.0.s_attn.rotary_emb.freqs"].float())))
-        self.rope_temporal = f32(H.rope_pair_table(H.temporal_rope_angles(sd["blocks.0.t_attn.rotary_emb.freqs"].float())))
+        self.rope_spatial = f32(H.rope_quad_table(H.spatial_rope_angles(sd["blocks.0.s_attn.rotary_emb.freqs"].float())))
+        self.rope_temporal = f32(H.rope_quad_table(H.temporal_rope_angles(sd["blocks.0.t_attn.rotary_emb.freqs"].float())))
         # host-side conditioning weights stay on the CPU in fp32 (as in the reference)
         self.host = {k: sd[k].float() for k in ("t_embedder.mlp.0.weight", "t_embedder.mlp.0.bias",
                                                  "t_embedder.mlp.2.weight", "t_embedder.mlp.2.bias",
@@ -207,7 +207,7 @@ class VaeDeviceWeights:
         self.pred_b = f32(sd["predictor.bias"])
         # per-token angles from a checkpoint's RoPE table, else the axial frequencies
         ang = sd["rotary_angles"].float() if "rotary_angles" in sd else H.vae_rope_angles(sd["rotary_freqs"].float())
-        self.rope = f32(H.rope_pair_table(ang))
+        self.rope = f32(H.rope_quad_table(ang))
 
         st = _lib.OasisVaeWeights()
         st.num_blocks = nb

@@ -140,3 +140,14 @@ def test_conditioning(g):
     for fn in (O.cond_vector, H.compute_cond):
         np.testing.assert_allclose(fn(torch.tensor([14]), None, sd)[0].numpy(), g["cond_t14_noaction"], atol=1e-5)
         np.testing.assert_allclose(fn(torch.tensor([999]), act, sd)[0].numpy(), g["cond_t999_walk"], atol=1e-5)
+
+
+def test_rope_quad_table_is_the_pair_table_regrouped():
+    """The GEMM epilogue's [16, positions, 4] table holds exactly the (cos, sin)
+    pairs of the pinned [positions, 32, 2] table: quad q, position p = pairs 2q, 2q+1."""
+    ang = H.spatial_rope_angles(H.default_spatial_freqs())
+    pair, quad = H.rope_pair_table(ang), H.rope_quad_table(ang)
+    assert quad.shape == (16, 144, 4)
+    for q in (0, 5, 15):
+        for p in (0, 77, 143):
+            assert torch.equal(quad[q, p], torch.cat([pair[p, 2 * q], pair[p, 2 * q + 1]]))

@@ -22,7 +22,7 @@ def _s():
 
 
 def gemm(a, w, mode, out, *, bias=None, resid=None, gate=None, ldg=0, rows_per_frame=1, rope=None,
-         rope_div=1, rope_mod=1, rope_dim=0, block_n=0, splits=0, ws=None):
+         rope_div=1, rope_mod=1, rope_dim=0, rope_stride=0, block_n=0, splits=0, ws=None):
     M, K = a.shape
     N = w.shape[0]
     args = _lib.OasisGemmArgs()
@@ -33,6 +33,7 @@ def gemm(a, w, mode, out, *, bias=None, resid=None, gate=None, ldg=0, rows_per_f
     args.resid, args.ldr = _lib.ptr(resid), N
     args.gate, args.ldg, args.rows_per_frame = _lib.ptr(gate), ldg, rows_per_frame
     args.rope, args.rope_div, args.rope_mod, args.rope_dim = _lib.ptr(rope), rope_div, rope_mod, rope_dim
+    args.rope_stride = rope_stride
     args.block_n, args.splits = block_n, splits
     if ws is not None:
         args.workspace, args.workspace_bytes = ws.data_ptr(), ws.numel()
@@ -144,7 +145,8 @@ def test_gemm_rope(kind):
     bias = torch.randn(N, device=DEV) * 0.1 if kind == "vae" else None
     tab_d = tab.to(DEV)
     out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
-    gemm(a, w, 6, out, bias=bias, rope=tab_d, rope_div=div, rope_mod=mod)
+    quad = tab.reshape(tab.shape[0], 16, 4).permute(1, 0, 2).contiguous().to(DEV)  # [16, positions, 4]
+    gemm(a, w, 6, out, bias=bias, rope=quad, rope_div=div, rope_mod=mod, rope_stride=tab.shape[0])
     x = a.float() @ w.float().T + (bias if bias is not None else 0)
     pos = (torch.arange(M, device=DEV) // div) % mod
     ref = _rope_ref(x, tab_d, pos)
@@ -161,7 +163,8 @@ def test_tensor_parallel_shard_shapes(n):
     tab = H.rope_pair_table(H.temporal_rope_angles(H.default_temporal_freqs())).to(DEV)
     w = rand_bf16(3 * HD, D, scale=0.05, seed=22)
     qkv = torch.empty(M, 3 * HD, device=DEV, dtype=torch.bfloat16)
-    gemm(a, w, 6, qkv, rope=tab, rope_div=144, rope_mod=3, rope_dim=HD)
+    quad = tab.reshape(tab.shape[0], 16, 4).permute(1, 0, 2).contiguous()
+    gemm(a, w, 6, qkv, rope=quad, rope_div=144, rope_mod=3, rope_dim=HD, rope_stride=tab.shape[0])
     pos = (torch.arange(M, device=DEV) // 144) % 3
     ref = _rope_ref(a.float() @ w.float().T, tab, pos, hd=HD)
     assert rel_l2(qkv.float(), ref) < 5e-3
