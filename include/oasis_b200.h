@@ -265,6 +265,7 @@ int oasis_generate_frame_kv(const OasisDitWeights* w, const OasisVaeWeights* vw,
  *                  head-dim pairs 2q and 2q + 1
  *   7 IMAGE        VAE predictor: scatter 20x20x3 patches into [frames, 3, 360, 640],
  *                  clamped to [-1, 1]
+ *   8 GATED_RESID_LN as 4, then the next LayerNorm of the updated rows (ln_* fields)
  * K must be a multiple of 64 and N of 16. Split-K needs `workspace`. */
 typedef struct OasisGemmArgs {
   const void* a; long long lda; /* bf16 */
@@ -281,6 +282,10 @@ typedef struct OasisGemmArgs {
   void* workspace; size_t workspace_bytes;
   int rope_dim; /* ROPE: width of the q (and k) section; 0 = 1024 (16 heads) */
   int rope_stride; /* ROPE: positions per row of the [16, positions, 4] table; 0 = rope_mod */
+  /* GATED_RESID_LN (8): the LayerNorm + adaLN modulate of the new rows, written as
+   * bf16 [M, 1024] to ln_out: (z - mean) rstd ln_mod[f ln_ld_mod + ln_scale_off + n]
+   * + ln_mod[f ln_ld_mod + ln_shift_off + n], f = r / rows_per_frame (N = 1024). */
+  void* ln_out; const float* ln_mod; long long ln_ld_mod, ln_shift_off, ln_scale_off; float ln_eps;
 } OasisGemmArgs;
 
 int oasis_gemm(const OasisGemmArgs* a, oasis_stream_t stream);

@@ -94,7 +94,8 @@ class OasisGemmArgs(C.Structure):
                 ("ldr", C.c_longlong), ("gate", fp), ("ldg", C.c_longlong), ("rows_per_frame", C.c_int),
                 ("rope", fp), ("rope_div", C.c_int), ("rope_mod", C.c_int), ("block_n", C.c_int),
                 ("splits", C.c_int), ("workspace", vp), ("workspace_bytes", C.c_size_t), ("rope_dim", C.c_int),
-                ("rope_stride", C.c_int)]
+                ("rope_stride", C.c_int), ("ln_out", vp), ("ln_mod", fp), ("ln_ld_mod", C.c_longlong),
+                ("ln_shift_off", C.c_longlong), ("ln_scale_off", C.c_longlong), ("ln_eps", C.c_float)]
 
 
 class OasisLayerNormArgs(C.Structure):

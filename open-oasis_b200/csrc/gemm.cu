@@ -57,7 +57,10 @@ struct Cfg {
   static constexpr int TMEM_COLS = 2 * BN;  // two accumulators; 128/256/512 (power of 2)
   static constexpr int STG_BYTES = kEpiWarps * kStgBytes * NBUF;
   static constexpr int BAR_BYTES = 512;
-  static constexpr int SMEM = 1024 /*align slack*/ + STAGES * STAGE_BYTES + STG_BYTES + BAR_BYTES;
+  // row-statistic exchange of the LN epilogue: [2 row blocks][4 quarters][2 halves][32 rows] float2
+  static constexpr int LN_BYTES = BN == 256 ? 2 * 4 * 2 * 32 * 8 : 0;
+  static constexpr int SMEM = 1024 /*align slack*/ + STAGES * STAGE_BYTES + STG_BYTES + BAR_BYTES + LN_BYTES;
+  static_assert(SMEM <= 232448, "shared memory per CTA");
 };
 
 #ifdef OASIS_GEMM_PROF
@@ -81,7 +84,8 @@ struct SplitK {
 __host__ __device__ constexpr bool bf16_out(int mode) {
   return mode == kEpiBF16 || mode == kEpiGeluTanhBF16 || mode == kEpiGeluErfBF16 || mode == kEpiRopeBF16;
 }
-__host__ __device__ constexpr bool reads_resid(int mode) { return mode == kEpiGatedResid || mode == kEpiResid; }
+__host__ __device__ constexpr bool gated(int mode) { return mode == kEpiGatedResid || mode == kEpiGatedResidLN; }
+__host__ __device__ constexpr bool reads_resid(int mode) { return gated(mode) || mode == kEpiResid; }
 
 // Residual prefetch for one 32-column group of row r (zeros past the last row).
 __device__ __forceinline__ void load_resid(const EpiParams& e, int r, int nb, int M, float4 (&res)[8]) {
@@ -133,8 +137,9 @@ __device__ __forceinline__ void epilogue_math(const EpiParams& e, int r, int nb,
       }
       break;
     case kEpiGatedResid:
+    case kEpiGatedResidLN:
     case kEpiResid:
-      if (e.mode == kEpiGatedResid) {
+      if (gated(e.mode)) {
         const float4* g = reinterpret_cast<const float4*>(e.gate + (long long)(r / e.rows_per_frame) * e.ldg + nb);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -288,7 +293,7 @@ __device__ __forceinline__ void epilogue_tile_resid(const EpiParams& e, const CU
                                                     const CUtensorMap* tm_res, uint8_t* stg, int nbuf, uint64_t* rbar,
                                                     uint32_t& rphase, uint32_t t_acc, int M, int N, int BN, int m0q,
                                                     int n0, int half, int lane, uint64_t* acc_bar,
-                                                    uint32_t acc_parity, bool& ok) {
+                                                    uint32_t acc_parity, bool& ok, float* stats = nullptr) {
   const int r = m0q + lane;
   const int nchunks = BN / 32;
   int mine = 0;  // this warp's chunks: c = half + kGroups i, i < mine
@@ -319,7 +324,7 @@ __device__ __forceinline__ void epilogue_tile_resid(const EpiParams& e, const CU
     const int nb = n0 + c * 32;
     uint8_t* buf = stg + b * kStgBytes;
     float4 gate[8];  // issued before the waits so its latency overlaps them
-    if (e.mode == kEpiGatedResid) {
+    if (gated(e.mode)) {
       const float4* g = reinterpret_cast<const float4*>(e.gate + (long long)((r < M ? r : M - 1) / e.rows_per_frame) * e.ldg + nb);
 #pragma unroll
       for (int j = 0; j < 8; ++j) gate[j] = __ldg(g + j);
@@ -336,7 +341,20 @@ __device__ __forceinline__ void epilogue_tile_resid(const EpiParams& e, const CU
     float4 res[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) res[j] = *reinterpret_cast<const float4*>(row + ((j ^ (lane & 7)) << 4));
-    epilogue_math(e, r, nb, v, res, e.mode == kEpiGatedResid ? gate : nullptr);
+    epilogue_math(e, r, nb, v, res, gated(e.mode) ? gate : nullptr);
+    if (stats) {  // row statistics of the new values: chunk mean / M2, then Chan's combination
+      float cm = 0.f;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) cm += v[j];
+      cm *= (1.f / 32.f);
+      float c2 = 0.f;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) c2 = fmaf(v[j] - cm, v[j] - cm, c2);
+      const float na = stats[0], nn = na + 32.f, d = cm - stats[1];
+      stats[1] += d * (32.f / nn);
+      stats[2] += c2 + d * d * (na * 32.f / nn);
+      stats[0] = nn;
+    }
     stage_write(buf, lane, false, 0, v);
     stage_commit(tm_out, buf, lane, m0q, nb);
     if (i + nbuf < mine) {  // refill this buffer with chunk i + nbuf once the store has read it
@@ -348,6 +366,56 @@ __device__ __forceinline__ void epilogue_tile_resid(const EpiParams& e, const CU
       __syncwarp();
     }
   }
+}
+
+// LayerNorm pass of the kEpiGatedResidLN epilogue, run by each epilogue warp once
+// all n-tiles of its 128-row block are written: half `half` of the lane quarter
+// normalises columns [half 512, half 512 + 512) of its 32 rows in 64-column
+// chunks (two 32-column fp32 boxes of the new z TMA-loaded into the staging
+// buffers, bf16 result stored from the first one with the xn tensor map).
+__device__ __forceinline__ bool ln_pass(const EpiParams& e, const LnParams& ln, const CUtensorMap* tm_z,
+                                       const CUtensorMap* tm_x,
+                                       uint8_t* stg, uint64_t* rbar, uint32_t& rphase, int M, int m0q, int half,
+                                       int lane, float mean, float rstd) {
+  const int r = m0q + lane;
+  const long long frame = (long long)((r < M ? r : M - 1) / e.rows_per_frame);
+  const float* mul = ln.mod + frame * ln.ld_mod + ln.scale_off;
+  const float* add = ln.mod + frame * ln.ld_mod + ln.shift_off;
+#pragma unroll 1
+  for (int ch = 0; ch < 8; ++ch) {
+    const int c0 = half * 512 + ch * 64;
+    if (lane == 0) {
+      bulk_wait_read0();  // the previous chunk's store has read the staging buffer
+      for (int b = 0; b < 2; ++b) {
+        mbar_arrive_expect_tx(&rbar[b], kStgBytes);
+        tma_load_2d(stg + b * kStgBytes, tm_z, &rbar[b], c0 + b * 32, m0q);
+      }
+    }
+    __syncwarp();
+    float v[2][32];
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+      if (!mbar_wait(&rbar[b], (rphase >> b) & 1, kDevTimeoutAccFull)) return false;
+      rphase ^= 1u << b;
+      const uint8_t* row = stg + b * kStgBytes + lane * 128;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 x = *reinterpret_cast<const float4*>(row + ((j ^ (lane & 7)) << 4));
+        const int c = c0 + b * 32 + 4 * j;
+        const float4 mm = __ldg(reinterpret_cast<const float4*>(mul + c));
+        const float4 aa = __ldg(reinterpret_cast<const float4*>(add + c));
+        v[b][4 * j] = (x.x - mean) * rstd * mm.x + aa.x;
+        v[b][4 * j + 1] = (x.y - mean) * rstd * mm.y + aa.y;
+        v[b][4 * j + 2] = (x.z - mean) * rstd * mm.z + aa.z;
+        v[b][4 * j + 3] = (x.w - mean) * rstd * mm.w + aa.w;
+      }
+    }
+    __syncwarp();  // both buffers read before the first is overwritten
+    stage_write(stg, lane, true, 0, v[0]);
+    stage_write(stg, lane, true, 4, v[1]);
+    stage_commit(tm_x, stg, lane, m0q, c0);
+  }
+  return true;
 }
 
 // Split-K fix-up. The `splits` CTAs of a tile form one thread-block cluster;
@@ -408,12 +476,29 @@ __device__ __forceinline__ void splitk_cluster_reduce(const EpiParams& e, const 
   }
 }
 
-template <int BN>
+// The k-th unit (tile x split index) this CTA processes, or -1 when none is left.
+// The LN-fused epilogue takes whole 128-row blocks instead: m-blocks blockIdx.x,
+// + gridDim.x, ..., each with all its n-tiles in order, so that one CTA writes
+// every column of its rows.
+__device__ __forceinline__ int unit_at(int k, bool row_blocks, int units, int n_tiles, int m_tiles) {
+  if (!row_blocks) {
+    const int u = blockIdx.x + k * gridDim.x;
+    return u < units ? u : -1;
+  }
+  const int mb = blockIdx.x + (k / n_tiles) * gridDim.x;
+  return mb < m_tiles ? mb * n_tiles + k % n_tiles : -1;
+}
+
+// kLN: the kEpiGatedResidLN instantiation (whole-row blocks, row statistics and
+// the LayerNorm pass); kept separate so the other epilogues' register budget is
+// not shared with it.
+template <int BN, bool kLN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
-                const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR, const int M,
+                const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR,
+                const __grid_constant__ CUtensorMap tmX, const int M,
                 const int N, const int K,
-                const EpiParams epi, const SplitK sk) {
+                const EpiParams epi, const SplitK sk, const LnParams lnp) {
   using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -424,6 +509,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   uint64_t* rbar = reinterpret_cast<uint64_t*>(tmem_base_slot + 4);  // [kEpiWarps][2], 8-byte aligned
+  float2* lnx = reinterpret_cast<float2*>(full + C::BAR_BYTES / 8);   // LN_BYTES: (mean, M2) per row half
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -435,12 +521,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int units = m_tiles * n_tiles * splits;
   const int kb_total = K / (BK * C::KA);  // stages of K
   const int kb_per_split = kb_total / splits;  // host guarantees divisibility
+  constexpr bool row_blocks = kLN;
 
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmW);
     if (epi.mode != kEpiImage) prefetch_tmap(&tmO);
     if (reads_resid(epi.mode)) prefetch_tmap(&tmR);
+    if (row_blocks) prefetch_tmap(&tmX);
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -481,8 +569,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       // stages' W tiles before waiting for the upstream kernel (programmatic
       // dependent launch), then add the A tiles once its output is visible.
       int pre = 0;
-      if ((int)blockIdx.x < units) {
-        const int tile = blockIdx.x / splits, split = blockIdx.x - tile * splits;
+      const int u_first = unit_at(0, row_blocks, units, n_tiles, m_tiles);
+      if (u_first >= 0) {
+        const int tile = u_first / splits, split = u_first - tile * splits;
         const int n0 = (tile % n_tiles) * BN, kb0 = split * kb_per_split;
         pre = kb_per_split < C::STAGES ? kb_per_split : C::STAGES;
         for (int i = 0; i < pre; ++i) {
@@ -491,13 +580,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       pdl_wait();
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      for (int k = 0, u; ok && (u = unit_at(k, row_blocks, units, n_tiles, m_tiles)) >= 0; ++k) {
         const int tile = u / splits, split = u - tile * splits;
         const int m0 = (tile / n_tiles) * BM, n0 = (tile % n_tiles) * BN;
         const int kb0 = split * kb_per_split;
         for (int kb = kb0; kb < kb0 + kb_per_split; ++kb) {
           uint8_t* sa = smem + stage * C::STAGE_BYTES;
-          if (u == (int)blockIdx.x && kb - kb0 < pre) {
+          if (k == 0 && kb - kb0 < pre) {
             load_a(sa, &full[stage], kb, m0);  // W already in flight
           } else {
             bool got;
@@ -527,7 +616,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #ifdef OASIS_GEMM_PROF
       const long long loop_t0 = clock64();
 #endif
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      for (int k = 0; ok && unit_at(k, row_blocks, units, n_tiles, m_tiles) >= 0; ++k) {
         bool got;
         {
           PROF_T0();
@@ -585,13 +674,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+    float stats[3] = {0.f, 0.f, 0.f};  // LN epilogue: this thread's row (count, mean, M2) so far
+    int mblk = 0;
+    for (int k = 0, u; ok && (u = unit_at(k, row_blocks, units, n_tiles, m_tiles)) >= 0; ++k) {
       const int tile = u / splits, split = u - tile * splits;
       const int m0q = (tile / n_tiles) * BM + quarter * 32, n0 = (tile % n_tiles) * BN;
       const uint32_t t_acc = tmem_base + lane_off + acc * BN;
       if (resid_tma)
         epilogue_tile_resid(epi, &tmO, &tmR, stg, C::NBUF, my_rbar, rphase, t_acc, M, N, BN, m0q, n0, half, lane,
-                            &acc_full[acc], acc_phase, ok);
+                            &acc_full[acc], acc_phase, ok, kLN ? stats : nullptr);
       else
         epilogue_tile(epi, sk, &tmO, stg, C::NBUF, sbuf, t_acc, M, N, BN, m0q, n0, tile, split, quarter, half,
                       lane, &acc_full[acc], acc_phase, ok);
@@ -601,6 +692,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
+      if constexpr (kLN && C::LN_BYTES > 0) {
+        if (tile % n_tiles == n_tiles - 1) {
+          // every column of these rows is written: combine the two halves' row
+          // statistics (512 columns each) and normalise into the LN output
+          if (lane == 0) bulk_wait0();  // this warp's z stores have completed
+          __syncwarp();
+          float2* slot = lnx + (mblk & 1) * 256 + quarter * 64;
+          slot[half * 32 + lane] = make_float2(stats[1], stats[2]);
+          named_barrier_sync(1 + quarter, 64);
+          const float2 o = slot[(half ^ 1) * 32 + lane];
+          const float d = stats[1] - o.x;
+          const float mean = 0.5f * (stats[1] + o.x);
+          const float m2 = stats[2] + o.y + d * d * 256.f;  // n_a n_b / n = 512 x 512 / 1024
+          const float rstd = rsqrtf(m2 * (1.f / 1024.f) + lnp.eps);
+          if (!ln_pass(epi, lnp, &tmR, &tmX, stg, my_rbar, rphase, M, m0q, half, lane, mean, rstd)) {
+            ok = false;
+            break;
+          }
+          stats[0] = stats[1] = stats[2] = 0.f;
+          ++mblk;
+        }
+      }
     }
     if (lane == 0) bulk_wait0();  // stores complete before the staging memory goes away
   }
@@ -687,14 +800,14 @@ int make_out_map(CUtensorMap* map, void* ptr, long long M, long long N, long lon
 
 int g_num_sms[64] = {0};
 
-template <int BN>
+template <int BN, bool kLN>
 int launch_bn(const GemmProblem& p, int splits, cudaStream_t stream) {
   using C = Cfg<BN>;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN, kLN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return set_error(OASIS_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     attr_set[dev & 63] = true;
   }
@@ -709,6 +822,8 @@ int launch_bn(const GemmProblem& p, int splits, cudaStream_t stream) {
     OASIS_TRY(make_out_map(&tr, const_cast<float*>(p.epi.resid), p.M, p.N, p.epi.ldr, false));  // same box as the output
   else
     tr = to;
+  CUtensorMap tx = to;
+  if (p.epi.mode == kEpiGatedResidLN) OASIS_TRY(make_out_map(&tx, p.ln.out, p.M, p.N, p.N, true));
   const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
   SplitK sk{nullptr, splits};
   if (splits > 1) {
@@ -718,12 +833,14 @@ int launch_bn(const GemmProblem& p, int splits, cudaStream_t stream) {
                        p.workspace_bytes);
     sk.partials = static_cast<float*>(p.workspace);
     // one CTA per (tile, split); the splits of a tile are one cluster
-    launch_pdl_cluster(gemm_kernel<BN>, dim3(tiles * splits), dim3(kThreads), C::SMEM, stream, splits, ta, tw, to,
-                       tr, p.M, p.N, p.K, p.epi, sk);
+    launch_pdl_cluster(gemm_kernel<BN, kLN>, dim3(tiles * splits), dim3(kThreads), C::SMEM, stream, splits, ta, tw, to,
+                       tr, tx, p.M, p.N, p.K, p.epi, sk, p.ln);
     return check_launch("gemm_kernel");
   }
-  const int grid = tiles < num_sms() ? tiles : num_sms();
-  launch_pdl(gemm_kernel<BN>, dim3(grid), dim3(kThreads), C::SMEM, stream, ta, tw, to, tr, p.M, p.N, p.K, p.epi, sk);
+  const int work = p.epi.mode == kEpiGatedResidLN ? (p.M + BM - 1) / BM : tiles;  // row blocks or tiles
+  const int grid = work < num_sms() ? work : num_sms();
+  launch_pdl(gemm_kernel<BN, kLN>, dim3(grid), dim3(kThreads), C::SMEM, stream, ta, tw, to, tr, tx, p.M, p.N, p.K, p.epi,
+             sk, p.ln);
   return check_launch("gemm_kernel");
 }
 
@@ -795,9 +912,14 @@ int gemm_launch(const GemmProblem& p, cudaStream_t stream) {
   OASIS_REQUIRE(p.N % 16 == 0, "GEMM: N=%d must be a multiple of 16", p.N);
   OASIS_REQUIRE(p.epi.out, "GEMM: null output");
   OASIS_REQUIRE(p.lda >= p.K, "GEMM: lda < K");
-  if (p.epi.mode == kEpiGatedResid || p.epi.mode == kEpiResid)
-    OASIS_REQUIRE(p.epi.resid, "GEMM: residual epilogue without residual input");
-  if (p.epi.mode == kEpiGatedResid) OASIS_REQUIRE(p.epi.gate && p.epi.rows_per_frame > 0, "GEMM: gate missing");
+  if (reads_resid(p.epi.mode)) OASIS_REQUIRE(p.epi.resid, "GEMM: residual epilogue without residual input");
+  if (gated(p.epi.mode)) OASIS_REQUIRE(p.epi.gate && p.epi.rows_per_frame > 0, "GEMM: gate missing");
+  if (p.epi.mode == kEpiGatedResidLN) {
+    OASIS_REQUIRE(p.N == 1024 && p.epi.ldo == 1024 && p.epi.ldr == 1024, "GEMM: the LN epilogue needs N = 1024 rows");
+    OASIS_REQUIRE(p.ln.out && p.ln.mod, "GEMM: LN epilogue without output or modulation table");
+    OASIS_REQUIRE(p.block_n == 0 || p.block_n == 256, "GEMM: the LN epilogue uses 256-wide tiles");
+    OASIS_REQUIRE(p.splits <= 1, "GEMM: the LN epilogue does not split K");
+  }
   if (p.epi.mode == kEpiRopeBF16) OASIS_REQUIRE(p.epi.rope && p.epi.rope_mod > 0 && p.epi.rope_div > 0, "GEMM: rope table missing");
   Plan pl = choose_plan(p.M, p.N, p.K);
   // fp32-output epilogues (32-column chunks) can use 32-wide tiles: at a few
@@ -808,16 +930,22 @@ int gemm_launch(const GemmProblem& p, cudaStream_t stream) {
   if (p.block_n) pl.bn = p.block_n;
   if (p.splits) pl.splits = p.splits;
   if (pl.splits > 1 && !p.workspace) pl.splits = 1;
+  if (p.epi.mode == kEpiGatedResidLN) {  // whole rows per CTA, 4 tiles of 256
+    pl.bn = 256;
+    pl.splits = 1;
+  }
   OASIS_REQUIRE(pl.bn != 32 || !bf16_out(p.epi.mode), "GEMM: block_n=32 needs an fp32 epilogue");
   if (pl.bn <= 128 && p.K % (2 * BK)) pl.bn = 256;  // narrower tiles stage K in 128-wide steps
   const int k_stages = p.K / (pl.bn <= 128 ? 2 * BK : BK);
   OASIS_REQUIRE(pl.splits >= 1 && pl.splits <= 8, "GEMM: splits=%d outside [1, 8] (one cluster per tile)", pl.splits);
   OASIS_REQUIRE(k_stages % pl.splits == 0, "GEMM: splits=%d must divide the %d K stages", pl.splits, k_stages);
   switch (pl.bn) {
-    case 32: return launch_bn<32>(p, pl.splits, stream);
-    case 64: return launch_bn<64>(p, pl.splits, stream);
-    case 128: return launch_bn<128>(p, pl.splits, stream);
-    case 256: return launch_bn<256>(p, pl.splits, stream);
+    case 32: return launch_bn<32, false>(p, pl.splits, stream);
+    case 64: return launch_bn<64, false>(p, pl.splits, stream);
+    case 128: return launch_bn<128, false>(p, pl.splits, stream);
+    case 256:
+      if (p.epi.mode == kEpiGatedResidLN) return launch_bn<256, true>(p, pl.splits, stream);
+      return launch_bn<256, false>(p, pl.splits, stream);
     default: return set_error(OASIS_ERR_INVALID_ARG, "GEMM: block_n=%d unsupported", pl.bn);
   }
 }

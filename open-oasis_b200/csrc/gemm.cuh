@@ -17,6 +17,8 @@ enum EpiMode : int {
   kEpiResid = 5,        // out_f32 = resid + acc + bias
   kEpiRopeBF16 = 6,     // out_bf16 = rope(acc + bias) on the q and k thirds of a qkv row
   kEpiImage = 7,        // VAE predictor: unpatchify 20x20x3 patches into a clamped image
+  kEpiGatedResidLN = 8, // kEpiGatedResid, then LayerNorm + adaLN modulate of the new rows (N = 1024):
+                        //   ln_out_bf16[r, n] = (z - mean_r) rstd_r ln_mod[f, scale + n] + ln_mod[f, shift + n]
 };
 
 struct EpiParams {
@@ -39,12 +41,24 @@ struct EpiParams {
   int img_patch = 20;             // image mode: patch edge in pixels
 };
 
+// kEpiGatedResidLN: the next sub-block's LayerNorm fused into the epilogue (kept
+// out of EpiParams, whose fields the epilogue holds in registers).
+struct LnParams {
+  void* out = nullptr;         // bf16 [M, 1024]
+  const float* mod = nullptr;  // adaLN table; frame f = r / rows_per_frame
+  long long ld_mod = 0;
+  long long shift_off = 0;
+  long long scale_off = 0;     // (1 + scale) already folded into the table
+  float eps = 1e-6f;
+};
+
 struct GemmProblem {
   const void* A = nullptr;  // bf16 [M, K], row stride lda elements
   long long lda = 0;
   const void* W = nullptr;  // bf16 [N, K] (nn.Linear layout), row stride K
   int M = 0, N = 0, K = 0;
   EpiParams epi;
+  LnParams ln;              // kEpiGatedResidLN only
   int block_n = 0;          // 0 = heuristic, else 64/128/256
   int splits = 0;           // 0 = heuristic, 1 = no split-K
   void* workspace = nullptr;  // split-K partial tiles (may be null -> no split)

@@ -179,6 +179,40 @@ def test_tensor_parallel_shard_shapes(n):
     assert rel_l2(h.float(), F.gelu(a.float() @ w1.float().T + b1, approximate="tanh")) < 5e-3
 
 
+@pytest.mark.parametrize("M,K", [(1152, 4096), (300, 1024), (4608, 1024), (2 * 148 * 128 + 200, 1024)])
+def test_gemm_gated_residual_layernorm(M, K):
+    """Mode 8: the gated residual update of z plus the next sub-block's LayerNorm +
+    adaLN modulate of the updated rows, written as bf16 (whole 1024-wide rows per
+    CTA, row statistics combined across the row's four tiles; the last case gives
+    every CTA three row blocks)."""
+    N, P = 1024, 144
+    frames = (M + P - 1) // P
+    a, w = rand_bf16(M, K, seed=41), rand_bf16(N, K, scale=0.05, seed=42)
+    bias = torch.randn(N, device=DEV) * 0.1
+    ldm = 4096
+    mod = torch.randn(frames, ldm, device=DEV) * 0.5
+    mod[:, 1024:2048] += 1.0  # (1 + scale) as the adaLN table holds it
+    gate_off, shift_off, scale_off = 2048, 0, 1024
+    z0 = torch.randn(M, N, device=DEV) * 2 + 0.3
+    z = z0.clone()
+    xn = torch.full((M, N), float("nan"), device=DEV, dtype=torch.bfloat16)
+    g = _lib.OasisGemmArgs()
+    g.a, g.lda, g.w, g.m, g.n, g.k, g.mode = a.data_ptr(), K, w.data_ptr(), M, N, K, 8
+    g.out, g.ldo, g.bias, g.resid, g.ldr = z.data_ptr(), N, bias.data_ptr(), z.data_ptr(), N
+    g.gate, g.ldg, g.rows_per_frame = mod[:, gate_off:].data_ptr(), ldm, P
+    g.ln_out, g.ln_mod, g.ln_ld_mod, g.ln_shift_off, g.ln_scale_off = xn.data_ptr(), mod.data_ptr(), ldm, shift_off, scale_off
+    _lib.call("oasis_gemm", C.byref(g), _s())
+    torch.cuda.synchronize()
+    assert _lib.load().oasis_device_error(1) == 0
+    fr = torch.arange(M, device=DEV) // P
+    z_ref = z0 + mod[fr, gate_off:gate_off + N] * (a.float() @ w.float().T + bias)
+    assert rel_l2(z, z_ref) < 1e-5
+    ln = F.layer_norm(z_ref, (N,), eps=1e-6)
+    xn_ref = ln * mod[fr, scale_off:scale_off + N] + mod[fr, shift_off:shift_off + N]
+    assert not torch.isnan(xn.float()).any()
+    assert rel_l2(xn.float(), xn_ref) < 5e-3, rel_l2(xn.float(), xn_ref)
+
+
 def test_gemm_image():
     B = 2
     M, N, K = B * 576, 1200, 1024
