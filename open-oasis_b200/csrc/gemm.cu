@@ -478,15 +478,17 @@ __device__ __forceinline__ void splitk_cluster_reduce(const EpiParams& e, const 
 
 // The k-th unit (tile x split index) this CTA processes, or -1 when none is left.
 // The LN-fused epilogue takes whole 128-row blocks instead: m-blocks blockIdx.x,
-// + gridDim.x, ..., each with all its n-tiles in order, so that one CTA writes
-// every column of its rows.
+// + gridDim.x, ..., each with all its n-tiles, so that one CTA writes every
+// column of its rows.
 __device__ __forceinline__ int unit_at(int k, bool row_blocks, int units, int n_tiles, int m_tiles) {
   if (!row_blocks) {
     const int u = blockIdx.x + k * gridDim.x;
     return u < units ? u : -1;
   }
+  // n-tiles in a rotated order (starting at blockIdx.x % n_tiles) so that the
+  // CTAs do not all stream the same weight slice at the same time
   const int mb = blockIdx.x + (k / n_tiles) * gridDim.x;
-  return mb < m_tiles ? mb * n_tiles + k % n_tiles : -1;
+  return mb < m_tiles ? mb * n_tiles + (k + blockIdx.x) % n_tiles : -1;
 }
 
 // kLN: the kEpiGatedResidLN instantiation (whole-row blocks, row statistics and
@@ -693,7 +695,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
       if constexpr (kLN && C::LN_BYTES > 0) {
-        if (tile % n_tiles == n_tiles - 1) {
+        if (k % n_tiles == n_tiles - 1) {  // the row block's last tile in this CTA's order
           // every column of these rows is written: combine the two halves' row
           // statistics (512 columns each) and normalise into the LN output
           if (lane == 0) bulk_wait0();  // this warp's z stores have completed
