@@ -50,6 +50,8 @@ typedef void* oasis_stream_t; /* cudaStream_t */
 
 /* Message of the last failing call on this host thread ("" if none). */
 const char* oasis_last_error(void);
+/* The same message under the name the boundary specification uses. */
+const char* oasis_get_last_error(void);
 /* Reads (and with reset != 0 clears) the device error word; synchronizes the device. */
 int oasis_device_error(int reset);
 /* Number of kernels this library has launched from the host so far (graph

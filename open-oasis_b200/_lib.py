@@ -108,6 +108,7 @@ class OasisLayerNormArgs(C.Structure):
 # name -> (restype, argtypes). Every symbol the header declares.
 SIGNATURES = {
     "oasis_last_error": (C.c_char_p, []),
+    "oasis_get_last_error": (C.c_char_p, []),
     "oasis_device_error": (C.c_int, [C.c_int]),
     "oasis_version": (C.c_char_p, []),
     "oasis_launch_count": (C.c_ulonglong, []),

@@ -655,6 +655,8 @@ extern "C" {
 
 const char* oasis_last_error(void) { return g_msg; }
 
+const char* oasis_get_last_error(void) { return g_msg; }
+
 int oasis_device_error(int reset) {
   const int a = read_device_error(reset);
   const int b = read_device_error_tc(reset);
