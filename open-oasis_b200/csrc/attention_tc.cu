@@ -13,17 +13,19 @@
 // Per key block j (online softmax; P V of a block is accumulated after the next
 // block's softmax, across unit boundaries too):
 //   S_j  = Q K_j^T       tcgen05.mma M=128 N=KB K=64, fp32 in TMEM (two buffers)
-//   P_j  = exp2(S_j * c - m_j)   4 softmax warps, one TMEM lane (query row) per
-//                                thread, bf16 P written to shared memory in the
-//                                K-major 128-byte-swizzled operand layout
+//   P_j  = exp2(S_j * c - m_j)   softmax warps, one TMEM lane (query row) per
+//                                thread (SWQ threads per row, each with a share
+//                                of the columns), S read from TMEM once, bf16 P
+//                                written to shared memory in the K-major
+//                                128-byte-swizzled operand layout
 //   PV_j = P_j V_j       tcgen05.mma M=128 N=64 K=KB with V as an MN-major
 //                        operand (V rows are key-major as they sit in memory)
 //   O    = O alpha_j + PV_j  in registers (alpha_j rescales to the new max)
 // Warp 0 streams Q (one buffer: the next unit's Q loads while the last block of
 // the current unit is in softmax) and K/V blocks (3-stage ring) with
-// TMA, warp 1 owns TMEM and issues the MMAs from one thread, two warps per TMEM
-// lane quarter do the softmax and the output. Persistent over units. Every wait is bounded and
-// records a code in this file's device error word.
+// TMA, warp 1 owns TMEM and issues the MMAs from one thread, SWQ warps per TMEM
+// lane quarter do the softmax and the output. Persistent over units. Every wait
+// is bounded and records a code in this file's device error word.
 #include <cuda.h>
 
 #include "common.cuh"
@@ -35,9 +37,10 @@ namespace oasis {
 namespace {
 
 constexpr int kTcRows = 128;    // query rows per unit = TMEM lanes
-// Warp 0 TMA, warp 1 MMA, warps 4 .. 4 + 4 SWQ softmax: SWQ warps share each TMEM
-// lane quarter (32 query rows), splitting the key columns of a block and the 64
-// output dims between them.
+// Warp 0 TMA, warp 1 MMA, then 4 SWQ softmax warps from warp 4 (from warp 2 when
+// SWQ = 4): SWQ warps share each TMEM lane quarter (32 query rows), splitting
+// the key columns of a block and the 64 output dims between them. SWQ = 2
+// (measured: 4 ties at three more warps and spills).
 #ifndef OASIS_TC_SWQ
 #define OASIS_TC_SWQ 2
 #endif
@@ -45,8 +48,8 @@ constexpr int kTcSWQ = OASIS_TC_SWQ;
 constexpr int kTcSoftWarp0 = kTcSWQ >= 4 ? 2 : 4;
 constexpr int kTcThreads = 32 * (kTcSoftWarp0 + 4 * kTcSWQ);
 constexpr int kTcSCols = 192;    // TMEM columns reserved per S buffer (KB <= 192)
-// (all callers use KB = 144: shared memory then holds two Q tiles, two K/V stages
-// and two P tiles within the 227 KB limit)
+// (all callers use KB = 144: shared memory then holds one Q tile, three K/V
+// stages and two P tiles within the 227 KB limit)
 constexpr int kTcPVCol = 384;    // PV buffers at columns 384 and 448
 
 template <int KB>
