@@ -92,3 +92,35 @@ def test_workspace_sizes_scale_with_batch():
     assert 0 < a < b
     assert lib.oasis_step_workspace_size(1, 2) > a
     assert lib.oasis_vae_workspace_size(2) > lib.oasis_vae_workspace_size(1) > 0
+
+
+def test_new_entry_points_validate_without_a_gpu():
+    """Context caching, the tcgen05 attention and the LN-fused GEMM epilogue reject
+    bad arguments with a status and a message before touching the device."""
+    lib = _lib.load()
+    w = _lib.OasisDitWeights()
+    assert lib.oasis_kv_cache_size(0, 3) == 0 and lib.oasis_kv_cache_size(2, 0) == 0
+    assert lib.oasis_kv_cache_size(2, 3) == 16 * 2 * 3 * 144 * 3072 * 2
+    d = _lib.OasisDitArgs(1, 0, 16, 16, 16, 0, 16, 1 << 20)  # zero context frames
+    assert lib.oasis_dit_precompute_past(C.byref(w), C.byref(d), 16, 1 << 30, None) == -1
+    assert b"frames" in lib.oasis_last_error()
+    d = _lib.OasisDitArgs(1, 2, 16, 16, 16, 1, 16, 1 << 20)  # the current frame must be one frame
+    assert lib.oasis_dit_forward_current(C.byref(w), C.byref(d), 16, 1 << 30, 1, None) == -1
+    assert b"frames must be 1" in lib.oasis_last_error()
+    d = _lib.OasisDitArgs(1, 1, 16, 16, 16, 1, 16, 1 << 20)
+    assert lib.oasis_dit_forward_current(C.byref(w), C.byref(d), 16, 16, 3, None) == -3  # cache too small
+    assert b"kv cache" in lib.oasis_last_error()
+    assert lib.oasis_attention_tc(16, 16, 2, 100, 16, None) == -1
+    assert b"seq=100" in lib.oasis_last_error()
+    assert lib.oasis_attention_temporal_cached(16, 16, 16, 1, 40, 16, None) == -1
+    g = _lib.OasisGemmArgs()
+    g.a, g.w, g.out, g.resid, g.gate = 16, 16, 16, 16, 16
+    g.m, g.n, g.k, g.mode, g.rows_per_frame = 256, 512, 1024, 8, 144
+    assert lib.oasis_gemm(C.byref(g), None) == -1  # the LN epilogue needs N = 1024
+    assert b"N = 1024" in lib.oasis_last_error()
+    g.n, g.ldo, g.ldr = 1024, 1024, 1024
+    assert lib.oasis_gemm(C.byref(g), None) == -1  # ... and an output and a modulation table
+    assert b"modulation" in lib.oasis_last_error()
+    g.mode = 9
+    assert lib.oasis_gemm(C.byref(g), None) == -1
+    assert lib.oasis_get_last_error() == lib.oasis_last_error()
