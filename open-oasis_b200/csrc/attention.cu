@@ -650,11 +650,10 @@ int attention_full_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, int grou
   // (multiples of 144): measured 225 -> 207 us for 512 DiT frames and
   // 400 -> 243 us for 64 VAE frames against the mma.sync kernels below, which
   // serve other lengths. OASIS_ATTN_TC=0 selects the mma.sync kernels.
-  static const int tc_mode = [] {
+  static const bool use_tc = [] {
     const char* e = getenv("OASIS_ATTN_TC");
-    return e ? (e[0] == '1' ? 1 : 0) : -1;
+    return !(e && e[0] == '0');
   }();
-  const bool use_tc = tc_mode != 0;
   if (use_tc && attention_tc_supported(seq)) return attention_tc_launch(qkv, out, groups, seq, H, s);
   if (seq == kSpatialSeq) {
     constexpr int smem = 2 * 3 * kSpatialTile * 2;
