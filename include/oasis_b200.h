@@ -251,6 +251,37 @@ size_t oasis_frame_kv_workspace_size(int batch, int frames, int steps);
 int oasis_generate_frame_kv(const OasisDitWeights* w, const OasisVaeWeights* vw, const OasisFrameArgs* a,
                             oasis_stream_t stream);
 
+/* ---------------------------------------------------- tensor parallelism --- */
+/* n-way tensor parallelism of the DiT forward (the reference's multi-chip scheme,
+ * oasis_inference.py:289-305, 569-626, 1153-1201). `shard` holds this rank's
+ * slices: for its heads = 16 / n heads (HD = 64 heads columns) qkv_w [3 HD, 1024]
+ * (its q, k and v rows), out_w [1024, HD], fc1_w [4 HD, 1024] + fc1_b [4 HD],
+ * fc2_w [1024, 4 HD]; out_b, fc2_b, adaLN, final layer, embed and RoPE are the
+ * full (replicated) tensors. After each row-parallel projection (O, FC2) the fp32
+ * partial [B T 144, 1024] in `partial` is summed over the ranks by the caller's
+ * `allreduce` (issued in order on `stream`: ncclAllReduce, torch.distributed, a
+ * peer-memory kernel), then bias, gate and residual are applied. z, cond and
+ * v_out are replicated and have the oasis_dit_forward layouts (v_out: last
+ * frame). Returns the first non-zero status of a kernel or of `allreduce`. */
+typedef int (*oasis_allreduce_fn)(float* buf, size_t count, void* user, oasis_stream_t stream);
+
+typedef struct OasisTpArgs {
+  int batch;
+  int frames;
+  int heads;         /* this rank's heads: 16 / n */
+  float* z;          /* [B, T, 144, 1024] fp32, overwritten */
+  const float* cond; /* [B, T, 1024] */
+  float* v_out;      /* [B, 144, 64] */
+  float* partial;    /* [B T 144, 1024] fp32, the collective's buffer */
+  oasis_allreduce_fn allreduce;
+  void* allreduce_user;
+  void* workspace;
+  size_t workspace_bytes;
+} OasisTpArgs;
+
+size_t oasis_tp_workspace_size(int batch, int frames, int heads);
+int oasis_dit_forward_tp(const OasisDitWeights* shard, const OasisTpArgs* a, oasis_stream_t stream);
+
 /* ------------------------------------------------------------ op level --- */
 
 /* tcgen05 GEMM: acc = A[M,K] . W[N,K]^T (bf16 in, fp32 accumulate) + bias, then

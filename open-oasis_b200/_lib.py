@@ -98,6 +98,16 @@ class OasisGemmArgs(C.Structure):
                 ("ln_shift_off", C.c_longlong), ("ln_scale_off", C.c_longlong), ("ln_eps", C.c_float)]
 
 
+# int (*)(float* buf, size_t count, void* user, cudaStream_t stream)
+ALLREDUCE_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p)
+
+
+class OasisTpArgs(C.Structure):
+    _fields_ = [("batch", C.c_int), ("frames", C.c_int), ("heads", C.c_int), ("z", fp), ("cond", fp),
+                ("v_out", fp), ("partial", fp), ("allreduce", ALLREDUCE_FN), ("allreduce_user", vp),
+                ("workspace", vp), ("workspace_bytes", C.c_size_t)]
+
+
 class OasisLayerNormArgs(C.Structure):
     _fields_ = [("x", fp), ("y", vp), ("rows_out", C.c_int), ("P", C.c_int), ("in_group", C.c_longlong),
                 ("in_off", C.c_longlong), ("frame_mul", C.c_longlong), ("frame_add", C.c_longlong),
@@ -124,6 +134,8 @@ SIGNATURES = {
     "oasis_frame_workspace_size": (C.c_size_t, [C.c_int, C.c_int, C.c_int]),
     "oasis_generate_frame": (C.c_int, [C.POINTER(OasisDitWeights), C.POINTER(OasisVaeWeights),
                                        C.POINTER(OasisFrameArgs), vp]),
+    "oasis_tp_workspace_size": (C.c_size_t, [C.c_int, C.c_int, C.c_int]),
+    "oasis_dit_forward_tp": (C.c_int, [C.POINTER(OasisDitWeights), C.POINTER(OasisTpArgs), vp]),
     "oasis_kv_cache_size": (C.c_size_t, [C.c_int, C.c_int]),
     "oasis_dit_precompute_past": (C.c_int, [C.POINTER(OasisDitWeights), C.POINTER(OasisDitArgs), vp, C.c_size_t, vp]),
     "oasis_dit_forward_current": (C.c_int, [C.POINTER(OasisDitWeights), C.POINTER(OasisDitArgs), vp, C.c_size_t,

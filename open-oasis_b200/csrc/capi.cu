@@ -497,6 +497,143 @@ int generate_frame_impl(const OasisDitWeights* w, const OasisVaeWeights* vw, con
   return vae_decode_impl(vw, &va, st);
 }
 
+// ---- tensor parallelism ----
+
+struct TpScratch {
+  __nv_bfloat16* silu;
+  float* adaln;
+  __nv_bfloat16* xn;
+  __nv_bfloat16* qkv;   // [M, 3 HD]
+  __nv_bfloat16* attn;  // [M, HD]
+  __nv_bfloat16* h;     // [M, 4 HD]
+  void* splitk;
+  size_t splitk_bytes;
+};
+
+size_t carve_tp(Carve& c, int B, int T, int heads, TpScratch* s) {
+  const size_t F = (size_t)B * T, M = F * kP, HD = (size_t)heads * 64;
+  TpScratch d;
+  d.silu = c.take<__nv_bfloat16>(F * kD);
+  d.adaln = c.take<float>(F * OASIS_ADALN_ROWS);
+  d.xn = c.take<__nv_bfloat16>(M * kD);
+  d.qkv = c.take<__nv_bfloat16>(M * 3 * HD);
+  d.attn = c.take<__nv_bfloat16>(M * HD);
+  d.h = c.take<__nv_bfloat16>(M * 4 * HD);
+  size_t m = 0;
+  auto upd = [&](size_t x) { m = x > m ? x : m; };
+  upd(gemm_workspace_bytes((int)M, (int)(3 * HD), kD));
+  upd(gemm_workspace_bytes((int)M, kD, (int)HD));
+  upd(gemm_workspace_bytes((int)M, (int)(4 * HD), kD));
+  upd(gemm_workspace_bytes((int)M, kD, (int)(4 * HD)));
+  upd(gemm_workspace_bytes((int)F, OASIS_ADALN_ROWS, kD));
+  upd(gemm_workspace_bytes(B * kP, kOut, kD));
+  d.splitk_bytes = m;
+  d.splitk = m ? c.take<uint8_t>(m) : nullptr;
+  if (s) *s = d;
+  return c.used;
+}
+
+int tp_forward_impl(const OasisDitWeights* w, const OasisTpArgs* a, cudaStream_t st) {
+  OASIS_REQUIRE(w && a, "dit_forward_tp: null argument");
+  const int B = a->batch, T = a->frames, H = a->heads;
+  OASIS_REQUIRE(B > 0 && T > 0 && T <= OASIS_MAX_FRAMES, "dit_forward_tp: batch=%d frames=%d", B, T);
+  OASIS_REQUIRE(H >= 1 && H <= 16 && 16 % H == 0, "dit_forward_tp: heads=%d must divide 16", H);
+  OASIS_REQUIRE(a->z && a->cond && a->v_out && a->partial && a->allreduce, "dit_forward_tp: null tensor or collective");
+  OASIS_REQUIRE(w->num_subblocks >= 0 && w->num_subblocks <= OASIS_DIT_SUBBLOCKS, "dit_forward_tp: num_subblocks");
+  Carve c(a->workspace, a->workspace_bytes);
+  TpScratch s;
+  carve_tp(c, B, T, H, &s);
+  if (!a->workspace || !c.ok())
+    return set_error(OASIS_ERR_WORKSPACE, "dit_forward_tp: workspace %zu bytes < %zu", a->workspace_bytes, c.used);
+  const int F = B * T, M = F * kP, HD = H * 64;
+  const long long ldm = (long long)w->num_subblocks * OASIS_ADALN_WIDTH + 2 * kD;
+  OASIS_TRY(compute_adaln(w, a->cond, F, s.silu, s.adaln, s.splitk, s.splitk_bytes, st));
+  float* z = a->z;
+  auto reduce = [&](const char* what) -> int {
+    const int rc = a->allreduce(a->partial, (size_t)M * kD, a->allreduce_user, st);
+    if (rc != 0) return set_error(rc < 0 ? rc : OASIS_ERR_CUDA, "dit_forward_tp: allreduce after %s returned %d", what, rc);
+    return OASIS_OK;
+  };
+  for (int i = 0; i < w->num_subblocks; ++i) {
+    const OasisDitSubBlock& sb = w->sub[i];
+    const bool spatial = (i % 2) == 0;
+    const long long off = (long long)i * OASIS_ADALN_WIDTH;
+    LayerNormParams ln;
+    ln.rows_out = M;
+    ln.P = kP;
+    ln.in_group = kP;
+    ln.mod = s.adaln;
+    ln.ld_mod = ldm;
+    ln.shift_off = off;
+    ln.scale_off = off + kD;
+    OASIS_TRY(layernorm_launch(z, s.xn, ln, st));
+    {
+      GemmProblem p = gemm(s.xn, sb.qkv_w, M, 3 * HD, kD, s.splitk, s.splitk_bytes);
+      p.epi.mode = kEpiRopeBF16;
+      p.epi.out = s.qkv;
+      p.epi.ldo = 3 * HD;
+      p.epi.rope = spatial ? w->rope_spatial : w->rope_temporal;
+      p.epi.rope_div = spatial ? 1 : kP;
+      p.epi.rope_mod = spatial ? kP : T;
+      p.epi.rope_stride = spatial ? kP : OASIS_MAX_FRAMES;
+      p.epi.rope_dim = HD;
+      OASIS_TRY(gemm_launch(p, st));
+    }
+    if (spatial)
+      OASIS_TRY(attention_full_launch(s.qkv, s.attn, F, kP, H, st));
+    else
+      OASIS_TRY(attention_temporal_launch(s.qkv, s.attn, B, T, kP, H, st));
+    {
+      GemmProblem p = gemm(s.attn, sb.out_w, M, kD, HD, s.splitk, s.splitk_bytes);
+      p.epi.mode = kEpiF32;
+      p.epi.out = a->partial;
+      p.epi.ldo = kD;
+      OASIS_TRY(gemm_launch(p, st));
+    }
+    OASIS_TRY(reduce("O"));
+    OASIS_TRY(gated_residual_launch(z, a->partial, sb.out_b, s.adaln + off + 2 * kD, ldm, kP, M, st));
+    ln.shift_off = off + 3 * kD;
+    ln.scale_off = off + 4 * kD;
+    OASIS_TRY(layernorm_launch(z, s.xn, ln, st));
+    {
+      GemmProblem p = gemm(s.xn, sb.fc1_w, M, 4 * HD, kD, s.splitk, s.splitk_bytes);
+      p.epi.mode = kEpiGeluTanhBF16;
+      p.epi.out = s.h;
+      p.epi.ldo = 4 * HD;
+      p.epi.bias = sb.fc1_b;
+      OASIS_TRY(gemm_launch(p, st));
+    }
+    {
+      GemmProblem p = gemm(s.h, sb.fc2_w, M, kD, 4 * HD, s.splitk, s.splitk_bytes);
+      p.epi.mode = kEpiF32;
+      p.epi.out = a->partial;
+      p.epi.ldo = kD;
+      OASIS_TRY(gemm_launch(p, st));
+    }
+    OASIS_TRY(reduce("FC2"));
+    OASIS_TRY(gated_residual_launch(z, a->partial, sb.fc2_b, s.adaln + off + 5 * kD, ldm, kP, M, st));
+  }
+  const long long foff = (long long)w->num_subblocks * OASIS_ADALN_WIDTH;
+  LayerNormParams ln;
+  ln.P = kP;
+  ln.mod = s.adaln;
+  ln.ld_mod = ldm;
+  ln.shift_off = foff;
+  ln.scale_off = foff + kD;
+  ln.rows_out = B * kP;
+  ln.in_group = (long long)T * kP;
+  ln.in_off = (long long)(T - 1) * kP;
+  ln.frame_mul = T;
+  ln.frame_add = T - 1;
+  OASIS_TRY(layernorm_launch(z, s.xn, ln, st));
+  GemmProblem p = gemm(s.xn, w->final_w, B * kP, kOut, kD, s.splitk, s.splitk_bytes);
+  p.epi.mode = kEpiF32;
+  p.epi.out = a->v_out;
+  p.epi.ldo = kOut;
+  p.epi.bias = w->final_b;
+  return gemm_launch(p, st);
+}
+
 // ---- context caching (precompute_past_state / dit_forward_currentonly) ----
 
 size_t kv_cache_bytes(int B, int Tp) { return (size_t)(OASIS_DIT_SUBBLOCKS / 2) * kv_slot_elems(B, Tp) * 2; }
@@ -753,6 +890,17 @@ int oasis_generate_frame(const OasisDitWeights* w, const OasisVaeWeights* vw, co
                          oasis_stream_t stream) {
   g_msg[0] = 0;
   return generate_frame_impl(w, vw, a, S(stream));
+}
+
+size_t oasis_tp_workspace_size(int batch, int frames, int heads) {
+  if (batch <= 0 || frames <= 0 || heads <= 0) return 0;
+  Carve c(nullptr, 0);
+  return carve_tp(c, batch, frames, heads, nullptr) + 256;
+}
+
+int oasis_dit_forward_tp(const OasisDitWeights* shard, const OasisTpArgs* a, oasis_stream_t stream) {
+  g_msg[0] = 0;
+  return tp_forward_impl(shard, a, S(stream));
 }
 
 size_t oasis_kv_cache_size(int batch, int past_frames) {

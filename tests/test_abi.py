@@ -33,7 +33,8 @@ def test_library_exports_every_declared_symbol():
 
 
 STRUCTS = ["OasisDitSubBlock", "OasisDitWeights", "OasisVaeBlock", "OasisVaeWeights", "OasisDitArgs",
-           "OasisDdimCoeffs", "OasisStepArgs", "OasisFrameArgs", "OasisVaeArgs", "OasisGemmArgs", "OasisLayerNormArgs"]
+           "OasisDdimCoeffs", "OasisStepArgs", "OasisFrameArgs", "OasisVaeArgs", "OasisGemmArgs", "OasisLayerNormArgs",
+           "OasisTpArgs"]
 
 
 def test_ctypes_layouts_match_c():
@@ -124,3 +125,22 @@ def test_new_entry_points_validate_without_a_gpu():
     g.mode = 9
     assert lib.oasis_gemm(C.byref(g), None) == -1
     assert lib.oasis_get_last_error() == lib.oasis_last_error()
+
+
+def test_tensor_parallel_entry_validates_without_a_gpu():
+    """oasis_dit_forward_tp rejects a head count that does not divide 16, a missing
+    collective and a short workspace before touching the device."""
+    lib = _lib.load()
+    assert lib.oasis_tp_workspace_size(0, 2, 8) == 0
+    assert lib.oasis_tp_workspace_size(2, 2, 8) > lib.oasis_tp_workspace_size(1, 2, 8) > 0
+    w = _lib.OasisDitWeights()
+    cb = _lib.ALLREDUCE_FN(lambda buf, n, user, st: 0)
+    a = _lib.OasisTpArgs(1, 2, 3, 16, 16, 16, 16, cb, None, 16, 1 << 30)
+    assert lib.oasis_dit_forward_tp(C.byref(w), C.byref(a), None) == -1
+    assert b"heads=3" in lib.oasis_last_error()
+    a = _lib.OasisTpArgs(1, 2, 8, 16, 16, 16, 16, _lib.ALLREDUCE_FN(), None, 16, 1 << 30)
+    assert lib.oasis_dit_forward_tp(C.byref(w), C.byref(a), None) == -1
+    assert b"collective" in lib.oasis_last_error()
+    a = _lib.OasisTpArgs(1, 2, 8, 16, 16, 16, 16, cb, None, 16, 16)
+    assert lib.oasis_dit_forward_tp(C.byref(w), C.byref(a), None) == -3
+    assert b"workspace" in lib.oasis_last_error()
