@@ -44,7 +44,8 @@ typedef void* oasis_stream_t; /* cudaStream_t */
 #define OASIS_ADALN_WIDTH 6144       /* per sub-block adaLN output (shift, 1+scale, gate) x (msa, mlp) */
 #define OASIS_ADALN_ROWS (OASIS_DIT_SUBBLOCKS * OASIS_ADALN_WIDTH + 2048) /* + final (shift, 1+scale) */
 #define OASIS_MAX_FRAMES 32          /* temporal positions of rope_temporal (T <= 32) */
-#define OASIS_VAE_BLOCKS 12
+#define OASIS_VAE_BLOCKS 12          /* max ViT blocks of the VAE decoder and of its encoder */
+#define OASIS_VAE_ENC_K 1216         /* patch_embed GEMM depth: 3 x 20 x 20 = 1200 pixels, zero-padded to 19 x 64 */
 
 /* ---------------------------------------------------------------- errors -- */
 
@@ -115,6 +116,23 @@ typedef struct OasisVaeWeights {
   const float* pred_b;                      /* [1200] */
   const float* rope;                        /* [16, 576, 4] as rope_spatial; pairs >= 16 are (1, 0) */
 } OasisVaeWeights;
+
+/* VAE encoder weights (the `encoder.*` half of the VAE checkpoint that
+ * oasis_inference.py:499-503 locates; used by vae.encode at :1744-1756).
+ * Layout: patch_embed conv 20x20/20 (3 -> 1024) as a GEMM over each patch's
+ * (c, p, q)-ordered 1200 pixels, num_blocks pre-LN ViT blocks with the same
+ * structure, pixel RoPE and GELU as the decoder's, the final LayerNorm, then
+ * quant_conv (1024 -> 32: posterior mean | logvar). */
+typedef struct OasisVaeEncoderWeights {
+  const void* patch_w;    /* bf16 [1024, OASIS_VAE_ENC_K] (conv weight flattened, zero-padded 1200 -> K) */
+  const float* patch_b;   /* [1024] */
+  int num_blocks;         /* depth of the encoder (from the checkpoint's encoder.* keys) */
+  OasisVaeBlock blk[OASIS_VAE_BLOCKS];
+  const float* norm_w; const float* norm_b; /* final encoder LayerNorm [1024] */
+  const void* quant_w;                      /* bf16 [32, 1024] */
+  const float* quant_b;                     /* [32] */
+  const float* rope;                        /* [16, 576, 4], as OasisVaeWeights.rope */
+} OasisVaeEncoderWeights;
 
 /* ---------------------------------------------------------- composite ---- */
 
@@ -193,6 +211,25 @@ typedef struct OasisVaeArgs {
 
 size_t oasis_vae_workspace_size(int batch);
 int oasis_vae_decode(const OasisVaeWeights* w, const OasisVaeArgs* a, oasis_stream_t stream);
+
+/* VAE encode of B prompt images. Replaces `vae.encode(x).mean * SCALING_FACTOR`
+ * (oasis_inference.py:1748-1751) and the patch re-layout before the context
+ * patch embed (:1752-1754, 1806-1809).
+ *   image  [B, 3, 360, 640] fp32 in [-1, 1]
+ *   latent [B, 576, 16] fp32 posterior mean x 0.07843137255 (may be NULL)
+ *   chunk  [B, 144, 64] fp32 the same latent in the DiT's (p, q, c) patch layout,
+ *          ready for oasis_patch_embed (may be NULL; not both) */
+typedef struct OasisVaeEncodeArgs {
+  int batch;
+  const float* image;
+  float* latent;
+  float* chunk;
+  void* workspace;
+  size_t workspace_bytes;
+} OasisVaeEncodeArgs;
+
+size_t oasis_vae_encoder_workspace_size(int batch);
+int oasis_vae_encode(const OasisVaeEncoderWeights* w, const OasisVaeEncodeArgs* a, oasis_stream_t stream);
 
 /* One generated frame for B sessions (run_full_frame, oasis_inference.py:2175-2232):
  * `steps` DDIM steps through the DiT, then the bridge and the VAE decode. The

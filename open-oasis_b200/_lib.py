@@ -14,6 +14,7 @@ LIB_PATH = os.path.join(HERE, "liboasis_b200.so")
 OASIS_DIT_SUBBLOCKS = 32
 OASIS_ADALN_WIDTH = 6144
 OASIS_VAE_BLOCKS = 12
+OASIS_VAE_ENC_K = 1216
 
 ERRORS = {
     -1: "OASIS_ERR_INVALID_ARG",
@@ -82,6 +83,17 @@ class OasisVaeArgs(C.Structure):
                 ("workspace_bytes", C.c_size_t)]
 
 
+class OasisVaeEncoderWeights(C.Structure):
+    _fields_ = [("patch_w", vp), ("patch_b", fp), ("num_blocks", C.c_int),
+                ("blk", OasisVaeBlock * OASIS_VAE_BLOCKS), ("norm_w", fp), ("norm_b", fp),
+                ("quant_w", vp), ("quant_b", fp), ("rope", fp)]
+
+
+class OasisVaeEncodeArgs(C.Structure):
+    _fields_ = [("batch", C.c_int), ("image", fp), ("latent", fp), ("chunk", fp), ("workspace", vp),
+                ("workspace_bytes", C.c_size_t)]
+
+
 class OasisFrameArgs(C.Structure):
     _fields_ = [("batch", C.c_int), ("frames", C.c_int), ("steps", C.c_int), ("chunk", fp), ("context_z", fp),
                 ("cond", fp), ("coeffs", C.POINTER(OasisDdimCoeffs)), ("image", fp), ("skip_decode", C.c_int),
@@ -131,6 +143,8 @@ SIGNATURES = {
     "oasis_bridge_unpatchify": (C.c_int, [fp, fp, C.c_int, vp]),
     "oasis_vae_workspace_size": (C.c_size_t, [C.c_int]),
     "oasis_vae_decode": (C.c_int, [C.POINTER(OasisVaeWeights), C.POINTER(OasisVaeArgs), vp]),
+    "oasis_vae_encoder_workspace_size": (C.c_size_t, [C.c_int]),
+    "oasis_vae_encode": (C.c_int, [C.POINTER(OasisVaeEncoderWeights), C.POINTER(OasisVaeEncodeArgs), vp]),
     "oasis_frame_workspace_size": (C.c_size_t, [C.c_int, C.c_int, C.c_int]),
     "oasis_generate_frame": (C.c_int, [C.POINTER(OasisDitWeights), C.POINTER(OasisVaeWeights),
                                        C.POINTER(OasisFrameArgs), vp]),

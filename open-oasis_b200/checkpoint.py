@@ -41,6 +41,11 @@ VAE_BLOCK_KEYS = ["norm1.weight", "norm1.bias", "attn.qkv.weight", "attn.qkv.bia
                   "attn.proj.bias", "norm2.weight", "norm2.bias", "mlp.fc1.weight", "mlp.fc1.bias",
                   "mlp.fc2.weight", "mlp.fc2.bias"]
 VAE_ROTARY_BUFFER = "decoder.0.attn.rotary_freqs"
+# The encoder half of the same file (vae.encode, oasis_inference.py:1748-1751). Its
+# module definition is not in the reference; these names follow the decoder's.
+VAE_ENC_REQUIRED = ["patch_embed.proj.weight", "patch_embed.proj.bias", "enc_norm.weight", "enc_norm.bias",
+                    "quant_conv.weight", "quant_conv.bias"]
+VAE_ENC_ROTARY_BUFFER = "encoder.0.attn.rotary_freqs"
 
 
 def _load(path: str) -> dict:
@@ -103,6 +108,26 @@ def load_vae_checkpoint(path: str, rotary_table: torch.Tensor | None = None) -> 
         raise KeyError(f"{path}: not an Oasis VAE checkpoint ({n} decoder blocks); missing {missing[:8]}"
                        f"{' ...' if len(missing) > 8 else ''}")
     table = rotary_table if rotary_table is not None else sd.get(VAE_ROTARY_BUFFER)
+    if table is not None:
+        sd["rotary_angles"] = rotary_angles_from_table(table)
+    elif "rotary_freqs" not in sd:
+        sd["rotary_freqs"] = H.default_vae_freqs()
+    return sd
+
+
+def load_vae_encoder_checkpoint(path: str, rotary_table: torch.Tensor | None = None) -> dict:
+    """VAE encoder state dict from the same safetensors file (the one
+    `_find_weights_by_prefix("encoder.")` finds, oasis_inference.py:499-503).
+    Pixel RoPE as in load_vae_checkpoint, from `encoder.0.attn.rotary_freqs` when
+    the file holds it."""
+    sd = _load(path)
+    n = _count(sd, "encoder.")
+    want = list(VAE_ENC_REQUIRED) + [f"encoder.{i}.{k}" for i in range(n) for k in VAE_BLOCK_KEYS]
+    missing = [k for k in want if k not in sd]
+    if n == 0 or missing:
+        raise KeyError(f"{path}: not an Oasis VAE encoder checkpoint ({n} encoder blocks); missing {missing[:8]}"
+                       f"{' ...' if len(missing) > 8 else ''}")
+    table = rotary_table if rotary_table is not None else sd.get(VAE_ENC_ROTARY_BUFFER, sd.get(VAE_ROTARY_BUFFER))
     if table is not None:
         sd["rotary_angles"] = rotary_angles_from_table(table)
     elif "rotary_freqs" not in sd:

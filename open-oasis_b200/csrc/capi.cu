@@ -341,25 +341,18 @@ size_t carve_vae(Carve& c, int B, VaeScratch* s) {
   return c.used;
 }
 
-int vae_decode_impl(const OasisVaeWeights* w, const OasisVaeArgs* a, cudaStream_t st) {
-  OASIS_REQUIRE(w && a, "vae_decode: null argument");
-  const int B = a->batch;
-  OASIS_REQUIRE(B > 0, "vae_decode: batch=%d", B);
-  OASIS_REQUIRE(a->latent && a->image, "vae_decode: null tensor");
-  Carve c(a->workspace, a->workspace_bytes);
-  VaeScratch s;
-  carve_vae(c, B, &s);
-  if (!a->workspace || !c.ok())
-    return set_error(OASIS_ERR_WORKSPACE, "vae_decode: workspace %zu bytes < %zu", a->workspace_bytes, c.used);
-  const int R = B * kVaeTok;
-  OASIS_TRY(post_quant_launch(a->latent, w->post_quant_w, w->post_quant_b, s.z, R, st));
+// num_blocks pre-LN ViT blocks over the residual stream s.z [B * 576, 1024]
+// (decoder: oasis_inference.py:1546-1618; the encoder has the same blocks), then the
+// final LayerNorm (norm_w, norm_b) into s.xn as the next GEMM's operand.
+int vae_block_stack(const OasisVaeBlock* blk, int nb, const float* rope, const float* norm_w, const float* norm_b,
+                    int R, const VaeScratch& s, cudaStream_t st) {
   LayerNormParams ln;
   ln.rows_out = R;
   ln.P = R;
   ln.in_group = R;
-  OASIS_REQUIRE(w->num_blocks >= 0 && w->num_blocks <= OASIS_VAE_BLOCKS, "vae_decode: num_blocks=%d", w->num_blocks);
-  for (int i = 0; i < w->num_blocks; ++i) {
-    const OasisVaeBlock& b = w->blk[i];
+  const int B = R / kVaeTok;
+  for (int i = 0; i < nb; ++i) {
+    const OasisVaeBlock& b = blk[i];
     ln.affine_w = b.norm1_w;
     ln.affine_b = b.norm1_b;
     OASIS_TRY(layernorm_launch(s.z, s.xn, ln, st));
@@ -369,7 +362,7 @@ int vae_decode_impl(const OasisVaeWeights* w, const OasisVaeArgs* a, cudaStream_
       p.epi.out = s.qkv;
       p.epi.ldo = 3 * kD;
       p.epi.bias = b.qkv_b;
-      p.epi.rope = w->rope;
+      p.epi.rope = rope;
       p.epi.rope_div = 1;
       p.epi.rope_mod = kVaeTok;
       p.epi.rope_stride = kVaeTok;
@@ -408,9 +401,25 @@ int vae_decode_impl(const OasisVaeWeights* w, const OasisVaeArgs* a, cudaStream_
       OASIS_TRY(gemm_launch(p, st));
     }
   }
-  ln.affine_w = w->norm_w;
-  ln.affine_b = w->norm_b;
-  OASIS_TRY(layernorm_launch(s.z, s.xn, ln, st));
+  ln.affine_w = norm_w;
+  ln.affine_b = norm_b;
+  return layernorm_launch(s.z, s.xn, ln, st);
+}
+
+int vae_decode_impl(const OasisVaeWeights* w, const OasisVaeArgs* a, cudaStream_t st) {
+  OASIS_REQUIRE(w && a, "vae_decode: null argument");
+  const int B = a->batch;
+  OASIS_REQUIRE(B > 0, "vae_decode: batch=%d", B);
+  OASIS_REQUIRE(a->latent && a->image, "vae_decode: null tensor");
+  Carve c(a->workspace, a->workspace_bytes);
+  VaeScratch s;
+  carve_vae(c, B, &s);
+  if (!a->workspace || !c.ok())
+    return set_error(OASIS_ERR_WORKSPACE, "vae_decode: workspace %zu bytes < %zu", a->workspace_bytes, c.used);
+  const int R = B * kVaeTok;
+  OASIS_TRY(post_quant_launch(a->latent, w->post_quant_w, w->post_quant_b, s.z, R, st));
+  OASIS_REQUIRE(w->num_blocks >= 0 && w->num_blocks <= OASIS_VAE_BLOCKS, "vae_decode: num_blocks=%d", w->num_blocks);
+  OASIS_TRY(vae_block_stack(w->blk, w->num_blocks, w->rope, w->norm_w, w->norm_b, R, s, st));
   GemmProblem p = gemm(s.xn, w->pred_w, R, 1200, kD, s.splitk, s.splitk_bytes);
   p.epi.mode = kEpiImage;
   p.epi.out = a->image;
@@ -421,6 +430,66 @@ int vae_decode_impl(const OasisVaeWeights* w, const OasisVaeArgs* a, cudaStream_
   return gemm_launch(p, st);
 }
 
+
+// VAE encoder scratch: the decoder's (the blocks are the same) plus the patch rows
+// [B * 576, OASIS_VAE_ENC_K] bf16 and the moments [B * 576, 32] fp32.
+size_t carve_vae_enc(Carve& c, int B, VaeScratch* s, __nv_bfloat16** patches, float** moments) {
+  VaeScratch d;
+  carve_vae(c, B, &d);
+  const size_t R = (size_t)B * kVaeTok;
+  __nv_bfloat16* p = c.take<__nv_bfloat16>(R * OASIS_VAE_ENC_K);
+  float* m = c.take<float>(R * 32);
+  // the split-K area must also cover the encoder's own GEMMs (patch embed, quant)
+  size_t need = gemm_workspace_bytes((int)R, kD, OASIS_VAE_ENC_K);
+  const size_t q = gemm_workspace_bytes((int)R, 32, kD);
+  need = q > need ? q : need;
+  if (need > d.splitk_bytes) {
+    d.splitk = c.take<uint8_t>(need);
+    d.splitk_bytes = need;
+  }
+  if (s) *s = d;
+  if (patches) *patches = p;
+  if (moments) *moments = m;
+  return c.used;
+}
+
+int vae_encode_impl(const OasisVaeEncoderWeights* w, const OasisVaeEncodeArgs* a, cudaStream_t st) {
+  OASIS_REQUIRE(w && a, "vae_encode: null argument");
+  const int B = a->batch;
+  OASIS_REQUIRE(B > 0, "vae_encode: batch=%d", B);
+  OASIS_REQUIRE(a->image && (a->latent || a->chunk), "vae_encode: null image, or neither latent nor chunk");
+  OASIS_REQUIRE(w->num_blocks >= 0 && w->num_blocks <= OASIS_VAE_BLOCKS, "vae_encode: num_blocks=%d", w->num_blocks);
+  OASIS_REQUIRE(w->patch_w && w->quant_w && w->norm_w && w->norm_b && (w->num_blocks == 0 || w->rope),
+                "vae_encode: null weight");
+  Carve c(a->workspace, a->workspace_bytes);
+  VaeScratch s;
+  __nv_bfloat16* patches;
+  float* moments;
+  carve_vae_enc(c, B, &s, &patches, &moments);
+  if (!a->workspace || !c.ok())
+    return set_error(OASIS_ERR_WORKSPACE, "vae_encode: workspace %zu bytes < %zu", a->workspace_bytes, c.used);
+  const int R = B * kVaeTok;
+  OASIS_TRY(image_patchify_launch(a->image, patches, B, OASIS_VAE_ENC_K, st));
+  {
+    GemmProblem p = gemm(patches, w->patch_w, R, kD, OASIS_VAE_ENC_K, s.splitk, s.splitk_bytes);
+    p.epi.mode = kEpiF32;
+    p.epi.out = s.z;
+    p.epi.ldo = kD;
+    p.epi.bias = w->patch_b;
+    OASIS_TRY(gemm_launch(p, st));
+  }
+  OASIS_TRY(vae_block_stack(w->blk, w->num_blocks, w->rope, w->norm_w, w->norm_b, R, s, st));
+  {
+    GemmProblem p = gemm(s.xn, w->quant_w, R, 32, kD, s.splitk, s.splitk_bytes);
+    p.epi.mode = kEpiF32;
+    p.block_n = 32;  // one tile spans the 32 moments
+    p.epi.out = moments;
+    p.epi.ldo = 32;
+    p.epi.bias = w->quant_b;
+    OASIS_TRY(gemm_launch(p, st));
+  }
+  return moments_to_latent_launch(moments, a->latent, a->chunk, B, kScalingFactor, st);
+}
 
 constexpr int kMaxFrameSteps = 64;
 
@@ -879,6 +948,17 @@ size_t oasis_vae_workspace_size(int batch) {
 int oasis_vae_decode(const OasisVaeWeights* w, const OasisVaeArgs* a, oasis_stream_t stream) {
   g_msg[0] = 0;
   return vae_decode_impl(w, a, S(stream));
+}
+
+size_t oasis_vae_encoder_workspace_size(int batch) {
+  if (batch <= 0) return 0;
+  Carve c(nullptr, 0);
+  return carve_vae_enc(c, batch, nullptr, nullptr, nullptr) + 256;
+}
+
+int oasis_vae_encode(const OasisVaeEncoderWeights* w, const OasisVaeEncodeArgs* a, oasis_stream_t stream) {
+  g_msg[0] = 0;
+  return vae_encode_impl(w, a, S(stream));
 }
 
 size_t oasis_frame_workspace_size(int batch, int frames, int steps) {

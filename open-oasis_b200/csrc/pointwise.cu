@@ -1,6 +1,7 @@
 // Memory-bound kernels of the frame path: LayerNorm (+adaLN modulate or affine),
 // SiLU of the conditioning, the noisy-chunk patch embed, the DDIM update, the
-// DiT->VAE bridge (unpatchify + 1/scaling) and the VAE post-quant projection.
+// DiT->VAE bridge (unpatchify + 1/scaling), the VAE post-quant projection and
+// the VAE encoder's image patchify and posterior-mean readout.
 //
 // All are HBM-bound row/element kernels: fp32 vectorised loads (float4),
 // warp-shuffle reductions, bf16 stores where the consumer is a GEMM operand.
@@ -222,6 +223,62 @@ __global__ void __launch_bounds__(256) gated_residual_kernel(float* __restrict__
   }
 }
 
+// VAE encoder input: image [B, 3, 360, 640] fp32 -> patch rows [B * 576, kp] bf16,
+// the 20x20 stride-20 patch_embed conv as a GEMM operand. Row = token (i, j) of the
+// 18 x 32 grid; column k = c * 400 + p * 20 + q (the conv weight's flattening order),
+// zero for 1200 <= k < kp. Each thread writes 8 columns (one 16-byte store).
+__global__ void __launch_bounds__(256) image_patchify_kernel(const float* __restrict__ img,
+                                                             __nv_bfloat16* __restrict__ out, int batch, int kp) {
+  pdl_trigger();
+  pdl_wait();
+  const int vec = kp >> 3;
+  const long long n = (long long)batch * 576 * vec;
+  long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  for (; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const int k0 = (int)(i % vec) * 8;
+    const long long r = i / vec;
+    const int tok = (int)(r % 576);
+    const long long b = r / 576;
+    const int ti = tok >> 5, tj = tok & 31;
+    __align__(16) __nv_bfloat16 v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int k = k0 + e;
+      float x = 0.f;
+      if (k < 1200) {
+        const int c = k / 400, pq = k % 400, pp = pq / 20, qq = pq % 20;
+        x = __ldg(img + ((b * 3 + c) * 360 + ti * 20 + pp) * 640 + tj * 20 + qq);
+      }
+      v[e] = __float2bfloat16(x);
+    }
+    *reinterpret_cast<uint4*>(out + r * kp + k0) = *reinterpret_cast<const uint4*>(v);
+  }
+}
+
+// VAE encoder output: moments [B * 576, 32] fp32 (mean | logvar of the posterior)
+// -> latent [B, 576, 16] = mean * scale and, if chunk != NULL, the same latent in
+// the DiT's patch layout: chunk[b, h*16 + w, p*32 + q*16 + c] = latent[b, (2h+p)*32 + 2w+q, c]
+// (the inverse of bridge_kernel without the 1/scale).
+__global__ void moments_to_latent_kernel(const float* __restrict__ mom, float* __restrict__ lat,
+                                         float* __restrict__ chunk, int batch, float scale) {
+  pdl_trigger();
+  pdl_wait();
+  const long long n = (long long)batch * 576 * 16;
+  long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  for (; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const int c = i & 15;
+    const long long t = i >> 4;
+    const float x = mom[t * 32 + c] * scale;
+    if (lat) lat[i] = x;
+    if (chunk) {
+      const int tok = t % 576;
+      const long long b = t / 576;
+      const int row = tok >> 5, col = tok & 31;
+      chunk[(b * 144 + (row >> 1) * 16 + (col >> 1)) * 64 + (row & 1) * 32 + (col & 1) * 16 + c] = x;
+    }
+  }
+}
+
 }  // namespace
 
 int gated_residual_launch(float* z, const float* x, const float* bias, const float* gate, long long ldg,
@@ -279,6 +336,23 @@ int post_quant_launch(const float* lat, const float* w, const float* b, float* z
   if (rows == 0) return OASIS_OK;
   launch_pdl(post_quant_kernel, dim3(rows), dim3(256), 0, s, lat, w, b, z, rows);
   return check_launch("post_quant_kernel");
+}
+
+int image_patchify_launch(const float* img, __nv_bfloat16* out, int batch, int kp, cudaStream_t s) {
+  OASIS_REQUIRE(img && out && batch >= 0, "image_patchify: bad arguments");
+  OASIS_REQUIRE(kp >= 1200 && kp % 8 == 0, "image_patchify: kp=%d", kp);
+  if (batch == 0) return OASIS_OK;
+  launch_pdl(image_patchify_kernel, dim3(grid_for((long long)batch * 576 * (kp / 8), 256)), dim3(256), 0, s, img, out,
+             batch, kp);
+  return check_launch("image_patchify_kernel");
+}
+
+int moments_to_latent_launch(const float* mom, float* lat, float* chunk, int batch, float scale, cudaStream_t s) {
+  OASIS_REQUIRE(mom && (lat || chunk) && batch >= 0, "moments_to_latent: bad arguments");
+  if (batch == 0) return OASIS_OK;
+  launch_pdl(moments_to_latent_kernel, dim3(grid_for((long long)batch * 576 * 16, 256)), dim3(256), 0, s, mom, lat,
+             chunk, batch, scale);
+  return check_launch("moments_to_latent_kernel");
 }
 
 }  // namespace oasis

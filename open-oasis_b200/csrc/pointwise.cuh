@@ -50,6 +50,10 @@ int bridge_launch(const float* chunk, float* latent, int batch, float inv_scale,
 int gated_residual_launch(float* z, const float* x, const float* bias, const float* gate, long long ldg,
                           int rows_per_frame, int rows, cudaStream_t s);
 int post_quant_launch(const float* lat, const float* w, const float* b, float* z, int rows, cudaStream_t s);
+// VAE encoder: image [B, 3, 360, 640] -> bf16 patch rows [B * 576, kp] (kp >= 1200, zero-padded);
+// moments [B * 576, 32] -> latent [B, 576, 16] and/or chunk [B, 144, 64], both scaled by `scale`.
+int image_patchify_launch(const float* img, __nv_bfloat16* out, int batch, int kp, cudaStream_t s);
+int moments_to_latent_launch(const float* mom, float* lat, float* chunk, int batch, float scale, cudaStream_t s);
 
 // Attention over a packed qkv buffer [rows, 3 * 1024] bf16 (q | k | v, 16 heads x 64).
 // Full (non-causal) attention within groups of `seq` consecutive rows.

@@ -15,7 +15,7 @@ import torch
 
 from . import _lib
 from . import host as H
-from .weights import DitDeviceWeights, VaeDeviceWeights
+from .weights import DitDeviceWeights, VaeDeviceWeights, VaeEncoderDeviceWeights
 
 
 def _stream(stream=None) -> int:
@@ -167,6 +167,34 @@ def vae_decode(vw: VaeDeviceWeights, latent: torch.Tensor, image: torch.Tensor, 
     a = _lib.OasisVaeArgs(B, latent.data_ptr(), image.data_ptr(), ws.data_ptr(), ws.numel())
     _lib.call("oasis_vae_decode", vw.ref(), C.byref(a), _stream(stream))
     return image
+
+
+def vae_encoder_workspace_bytes(batch: int) -> int:
+    return int(_lib.load().oasis_vae_encoder_workspace_size(batch))
+
+
+def vae_encode(ew: VaeEncoderDeviceWeights, image: torch.Tensor, ws: torch.Tensor, latent: torch.Tensor | None = None,
+               chunk: torch.Tensor | None = None, stream=None) -> tuple[torch.Tensor | None, torch.Tensor | None]:
+    """image [B, 3, 360, 640] in [-1, 1] -> latent [B, 576, 16] (posterior mean x
+    scaling factor) and/or chunk [B, 144, 64] (the same latent in the DiT's patch
+    layout, ready for patch_embed as a context frame)."""
+    _check_cuda(image, "image")
+    B = image.shape[0]
+    if tuple(image.shape) != (B, 3, H.VAE_H * H.VAE_PATCH, H.VAE_W * H.VAE_PATCH):
+        raise ValueError("image must be [B, 3, 360, 640]")
+    if latent is None and chunk is None:
+        raise ValueError("vae_encode needs a latent or a chunk output")
+    if latent is not None:
+        _check_cuda(latent, "latent")
+        if tuple(latent.shape) != (B, H.VAE_TOKENS, H.VAE_LATENT):
+            raise ValueError("latent must be [B, 576, 16]")
+    if chunk is not None:
+        _check_cuda(chunk, "chunk")
+        if tuple(chunk.shape) != (B, H.N_PATCHES, H.OUT_DIM):
+            raise ValueError("chunk must be [B, 144, 64]")
+    a = _lib.OasisVaeEncodeArgs(B, image.data_ptr(), _lib.ptr(latent), _lib.ptr(chunk), ws.data_ptr(), ws.numel())
+    _lib.call("oasis_vae_encode", ew.ref(), C.byref(a), _stream(stream))
+    return latent, chunk
 
 
 def frame_workspace_bytes(batch: int, frames: int, steps: int) -> int:

@@ -36,6 +36,8 @@ SCALING_FACTOR = 0.07843137255
 MAX_T = 32
 
 VAE_DEPTH = 12
+VAE_ENC_DEPTH = 6  # encoder depth for random init; a checkpoint's encoder.* keys set the real one
+VAE_ENC_K = 1216  # patch_embed GEMM depth: 1200 pixels zero-padded to a multiple of 64
 VAE_DIM = 1024
 VAE_HEADS = 16
 VAE_LATENT = 16

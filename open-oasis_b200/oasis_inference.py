@@ -14,6 +14,8 @@ Mapping (reference file:line -> here):
   prealloc_vae_scratch     :763   -> prealloc_vae_scratch(device, batch=1)
   vae_decode_forward       :1546  -> vae_decode_forward(vae_dev, vae_scr, ...)
   bridge_unpatchify        :1697  -> bridge_unpatchify(dit_output, bridge, bridge_tmp, vae_input)
+  vae.encode(x).mean * SCALING_FACTOR  :1748-1751
+                                  -> vae_encode(enc_dev, x) with enc_dev = preload_vae_encoder_weights(...)
 
 Differences a caller sees (all deliberate, B200-first):
   * token rows are exactly 144 per frame (the reference pads to 160); SEQ = 144 T;
@@ -34,7 +36,7 @@ from . import checkpoint as CK
 from . import engine as E
 from . import host as H
 from .host import sigmoid_beta_schedule, timestep_embedding  # noqa: F401  (reference names)
-from .weights import DitDeviceWeights, VaeDeviceWeights
+from .weights import DitDeviceWeights, VaeDeviceWeights, VaeEncoderDeviceWeights
 
 TILE = 32
 D_MODEL = H.D_MODEL
@@ -184,3 +186,27 @@ def bridge_unpatchify(dit_output, bridge=None, bridge_tmp=None, vae_input=None) 
     if vae_input is None:
         vae_input = torch.empty(B, H.VAE_TOKENS, H.VAE_LATENT, device=dit_output.device)
     return E.bridge_unpatchify(dit_output.contiguous(), vae_input)
+
+
+def preload_vae_encoder_weights(vae_state_dict, device="cuda", rotary_table=None) -> VaeEncoderDeviceWeights:
+    """Packs the VAE encoder (state dict, or the path of the VAE safetensors file).
+    The reference runs the encoder on the CPU (load_vae_cpu, oasis_inference.py:1738)."""
+    if isinstance(vae_state_dict, str):
+        vae_state_dict = CK.load_vae_encoder_checkpoint(vae_state_dict, rotary_table)
+    return VaeEncoderDeviceWeights(vae_state_dict, device)
+
+
+def vae_encode(enc_dev: VaeEncoderDeviceWeights, x: torch.Tensor, ws: torch.Tensor | None = None,
+               chunk: torch.Tensor | None = None) -> torch.Tensor:
+    """`vae.encode(x).mean * SCALING_FACTOR` (oasis_inference.py:1748-1751):
+    x (B, 3, 360, 640) in [-1, 1] -> prompt latent (B, 576, 16). If `chunk`
+    (B, 144, 64) is given, the same latent is also written there in the DiT's
+    patch layout (the reference's rearrange + patchify before the context
+    patch embed, :1752-1754, 1806-1809)."""
+    x = x.to(enc_dev.device, torch.float32).contiguous()
+    B = x.shape[0]
+    if ws is None:
+        ws = E.workspace(E.vae_encoder_workspace_bytes(B), enc_dev.device)
+    latent = torch.empty(B, H.VAE_TOKENS, H.VAE_LATENT, device=enc_dev.device)
+    E.vae_encode(enc_dev, x, ws, latent=latent, chunk=chunk)
+    return latent

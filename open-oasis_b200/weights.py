@@ -101,6 +101,45 @@ def init_vae_weights(seed: int = 2, n_blocks: int = H.VAE_DEPTH, std: float = 0.
     return sd
 
 
+def init_vae_encoder_weights(seed: int = 4, n_blocks: int = H.VAE_ENC_DEPTH, std: float = 0.02,
+                             bias_std: float = 0.0, norm_std: float = 0.0) -> dict[str, torch.Tensor]:
+    """Reference-keyed fp32 CPU state dict of the VAE encoder (the `encoder.*`,
+    `patch_embed.*`, `enc_norm.*` and `quant_conv.*` keys of the VAE checkpoint)."""
+    g = _gen(seed)
+
+    def w(*shape):
+        return torch.randn(*shape, generator=g) * std
+
+    def b(n):
+        return torch.randn(n, generator=g) * bias_std if bias_std > 0 else torch.zeros(n)
+
+    def nw(n):
+        return 1.0 + (torch.randn(n, generator=g) * norm_std if norm_std > 0 else torch.zeros(n))
+
+    D = H.VAE_DIM
+    sd = {"patch_embed.proj.weight": w(D, 3, H.VAE_PATCH, H.VAE_PATCH), "patch_embed.proj.bias": b(D)}
+    for i in range(n_blocks):
+        p = f"encoder.{i}"
+        sd[f"{p}.norm1.weight"] = nw(D)
+        sd[f"{p}.norm1.bias"] = b(D)
+        sd[f"{p}.attn.qkv.weight"] = w(3 * D, D)
+        sd[f"{p}.attn.qkv.bias"] = b(3 * D)
+        sd[f"{p}.attn.proj.weight"] = w(D, D)
+        sd[f"{p}.attn.proj.bias"] = b(D)
+        sd[f"{p}.norm2.weight"] = nw(D)
+        sd[f"{p}.norm2.bias"] = b(D)
+        sd[f"{p}.mlp.fc1.weight"] = w(4 * D, D)
+        sd[f"{p}.mlp.fc1.bias"] = b(4 * D)
+        sd[f"{p}.mlp.fc2.weight"] = w(D, 4 * D)
+        sd[f"{p}.mlp.fc2.bias"] = b(D)
+    sd["enc_norm.weight"] = nw(D)
+    sd["enc_norm.bias"] = b(D)
+    sd["quant_conv.weight"] = w(2 * H.VAE_LATENT, D)
+    sd["quant_conv.bias"] = b(2 * H.VAE_LATENT)
+    sd["rotary_freqs"] = H.default_vae_freqs()
+    return sd
+
+
 def count_blocks(sd: dict, prefix: str = "blocks.") -> int:
     ids = {int(k.split(".")[1]) for k in sd if k.startswith(prefix)}
     return max(ids) + 1 if ids else 0
@@ -217,6 +256,57 @@ class VaeDeviceWeights:
             for k, v in blk.items():
                 setattr(st.blk[i], k, v.data_ptr())
         for k in ("norm_w", "norm_b", "pred_w", "pred_b", "rope"):
+            setattr(st, k, getattr(self, k).data_ptr())
+        self.struct = st
+
+    def ref(self):
+        return C.byref(self.struct)
+
+
+class VaeEncoderDeviceWeights:
+    """VAE encoder weights on one GPU + the ctypes OasisVaeEncoderWeights struct
+    (the reference keeps the encoder on the CPU, oasis_inference.py:1738-1751)."""
+
+    def __init__(self, sd: dict, device: torch.device | str = "cuda"):
+        dev = torch.device(device)
+        self.device = dev
+        nb = count_blocks(sd, "encoder.")
+        if nb > _lib.OASIS_VAE_BLOCKS:
+            raise ValueError(f"VAE encoder with {nb} blocks; the library holds at most {_lib.OASIS_VAE_BLOCKS}")
+        self.n_blocks = nb
+
+        def bf(t):
+            return t.to(dev, torch.bfloat16).contiguous()
+
+        def f32(t):
+            return t.to(dev, torch.float32).contiguous()
+
+        pw = sd["patch_embed.proj.weight"].float().reshape(H.VAE_DIM, H.VAE_PATCH_DIM)  # (c, p, q) order
+        self.patch_w = bf(torch.nn.functional.pad(pw, (0, H.VAE_ENC_K - H.VAE_PATCH_DIM)))
+        self.patch_b = f32(sd["patch_embed.proj.bias"])
+        self.blocks = []
+        for i in range(nb):
+            p = f"encoder.{i}"
+            self.blocks.append(dict(
+                norm1_w=f32(sd[f"{p}.norm1.weight"]), norm1_b=f32(sd[f"{p}.norm1.bias"]),
+                qkv_w=bf(sd[f"{p}.attn.qkv.weight"]), qkv_b=f32(sd[f"{p}.attn.qkv.bias"]),
+                proj_w=bf(sd[f"{p}.attn.proj.weight"]), proj_b=f32(sd[f"{p}.attn.proj.bias"]),
+                norm2_w=f32(sd[f"{p}.norm2.weight"]), norm2_b=f32(sd[f"{p}.norm2.bias"]),
+                fc1_w=bf(sd[f"{p}.mlp.fc1.weight"]), fc1_b=f32(sd[f"{p}.mlp.fc1.bias"]),
+                fc2_w=bf(sd[f"{p}.mlp.fc2.weight"]), fc2_b=f32(sd[f"{p}.mlp.fc2.bias"])))
+        self.norm_w = f32(sd["enc_norm.weight"])
+        self.norm_b = f32(sd["enc_norm.bias"])
+        self.quant_w = bf(sd["quant_conv.weight"].reshape(2 * H.VAE_LATENT, H.VAE_DIM))
+        self.quant_b = f32(sd["quant_conv.bias"])
+        ang = sd["rotary_angles"].float() if "rotary_angles" in sd else H.vae_rope_angles(sd["rotary_freqs"].float())
+        self.rope = f32(H.rope_quad_table(ang))
+
+        st = _lib.OasisVaeEncoderWeights()
+        st.num_blocks = nb
+        for i, blk in enumerate(self.blocks):
+            for k, v in blk.items():
+                setattr(st.blk[i], k, v.data_ptr())
+        for k in ("patch_w", "patch_b", "norm_w", "norm_b", "quant_w", "quant_b", "rope"):
             setattr(st, k, getattr(self, k).data_ptr())
         self.struct = st
 

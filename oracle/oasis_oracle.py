@@ -18,6 +18,10 @@ Semantic choices (where the reference and the benchmark spec differ):
     160 rows and does not mask the pad keys);
   * DiT MLP GELU is tanh; VAE MLP GELU is exact erf (the timm Mlp default that the
     reference's stub reproduces, oasis_inference.py:35-42);
+  * the VAE encoder (`vae.encode`, whose module file vae.py the reference does not
+    ship) is restated as the decoder's mirror image under the checkpoint's
+    encoder.* / patch_embed / enc_norm / quant_conv keys: its architecture is an
+    assumption, unpinned;
   * RoPE frequencies are the fixed vectors built in open-oasis_b200/host.py's
     defaults (the learned checkpoint vectors are absent) and are passed in.
 """
@@ -223,18 +227,16 @@ def vae_unpatchify(patches: torch.Tensor) -> torch.Tensor:
     return x.reshape(b, 3, 360, 640)
 
 
-def n_vae_blocks(sd: dict) -> int:
-    return max(int(k.split(".")[1]) for k in sd if k.startswith("decoder.")) + 1
+def n_vae_blocks(sd: dict, prefix: str = "decoder") -> int:
+    ids = [int(k.split(".")[1]) for k in sd if k.startswith(prefix + ".")]
+    return max(ids) + 1 if ids else 0
 
 
-def vae_decode(latent: torch.Tensor, sd: dict) -> torch.Tensor:
-    """latent (B, 576, 16) -> image (B, 3, 360, 640) clamped to [-1, 1]."""
-    b = latent.shape[0]
-    # (576, 32): a checkpoint's per-token RoPE table, else the axial frequencies
-    fr = sd["rotary_angles"].float() if "rotary_angles" in sd else vae_rope_freqs(sd["rotary_freqs"].float())
-    x = F.linear(latent, sd["post_quant_conv.weight"], sd["post_quant_conv.bias"])
-    for i in range(n_vae_blocks(sd)):
-        p = f"decoder.{i}"
+def _vae_blocks(x: torch.Tensor, sd: dict, prefix: str, fr: torch.Tensor) -> torch.Tensor:
+    """The pre-LN ViT blocks `{prefix}.{i}` over x (B, 576, 1024) (oasis_inference.py:1546-1618)."""
+    b = x.shape[0]
+    for i in range(n_vae_blocks(sd, prefix)):
+        p = f"{prefix}.{i}"
         h = F.layer_norm(x, (D,), sd[f"{p}.norm1.weight"], sd[f"{p}.norm1.bias"], eps=1e-6)
         qkv = F.linear(h, sd[f"{p}.attn.qkv.weight"], sd[f"{p}.attn.qkv.bias"])
         q, k, v = [t.reshape(b, VAE_TOK, HEADS, DH).transpose(1, 2) for t in qkv.chunk(3, dim=-1)]
@@ -244,9 +246,43 @@ def vae_decode(latent: torch.Tensor, sd: dict) -> torch.Tensor:
         h = F.layer_norm(x, (D,), sd[f"{p}.norm2.weight"], sd[f"{p}.norm2.bias"], eps=1e-6)
         h = F.gelu(F.linear(h, sd[f"{p}.mlp.fc1.weight"], sd[f"{p}.mlp.fc1.bias"]))
         x = x + F.linear(h, sd[f"{p}.mlp.fc2.weight"], sd[f"{p}.mlp.fc2.bias"])
+    return x
+
+
+def _vae_rope(sd: dict) -> torch.Tensor:
+    """(576, 32): a checkpoint's per-token RoPE table, else the axial frequencies."""
+    return sd["rotary_angles"].float() if "rotary_angles" in sd else vae_rope_freqs(sd["rotary_freqs"].float())
+
+
+def vae_decode(latent: torch.Tensor, sd: dict) -> torch.Tensor:
+    """latent (B, 576, 16) -> image (B, 3, 360, 640) clamped to [-1, 1]."""
+    x = F.linear(latent, sd["post_quant_conv.weight"], sd["post_quant_conv.bias"])
+    x = _vae_blocks(x, sd, "decoder", _vae_rope(sd))
     x = F.layer_norm(x, (D,), sd["dec_norm.weight"], sd["dec_norm.bias"], eps=1e-6)
     pred = F.linear(x, sd["predictor.weight"], sd["predictor.bias"])
     return vae_unpatchify(pred).clamp(-1, 1)
+
+
+def vae_encode(image: torch.Tensor, sd: dict) -> torch.Tensor:
+    """`vae.encode(image).mean * SCALING_FACTOR` (oasis_inference.py:1748-1751):
+    image (B, 3, 360, 640) in [-1, 1] -> latent (B, 576, 16). The encoder mirrors
+    the decoder: patch_embed conv 20x20/20 (3 -> 1024), the `encoder.{i}` ViT
+    blocks, enc_norm, quant_conv (1024 -> 32 = mean | logvar); the posterior mean
+    is the first 16 channels."""
+    b = image.shape[0]
+    x = F.conv2d(image.float(), sd["patch_embed.proj.weight"], sd["patch_embed.proj.bias"], stride=20)
+    x = x.permute(0, 2, 3, 1).reshape(b, VAE_TOK, D)
+    x = _vae_blocks(x, sd, "encoder", _vae_rope(sd))
+    x = F.layer_norm(x, (D,), sd["enc_norm.weight"], sd["enc_norm.bias"], eps=1e-6)
+    moments = F.linear(x, sd["quant_conv.weight"].reshape(32, D), sd["quant_conv.bias"])
+    return moments[..., :16] * SCALING_FACTOR
+
+
+def latent_to_chunk(latent: torch.Tensor) -> torch.Tensor:
+    """(B, 576, 16) latent tokens -> (B, 144, 64) DiT patches: the
+    `b (h w) c -> b c h w` rearrange (oasis_inference.py:1752-1754) then patchify."""
+    b = latent.shape[0]
+    return patchify(latent.reshape(b, VAE_H, VAE_W, 16).permute(0, 3, 1, 2))
 
 
 def generate_frame(chunk: torch.Tensor, context_z: torch.Tensor | None, conds: list[torch.Tensor],

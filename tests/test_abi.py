@@ -34,7 +34,7 @@ def test_library_exports_every_declared_symbol():
 
 STRUCTS = ["OasisDitSubBlock", "OasisDitWeights", "OasisVaeBlock", "OasisVaeWeights", "OasisDitArgs",
            "OasisDdimCoeffs", "OasisStepArgs", "OasisFrameArgs", "OasisVaeArgs", "OasisGemmArgs", "OasisLayerNormArgs",
-           "OasisTpArgs"]
+           "OasisTpArgs", "OasisVaeEncoderWeights", "OasisVaeEncodeArgs"]
 
 
 def test_ctypes_layouts_match_c():
@@ -143,4 +143,23 @@ def test_tensor_parallel_entry_validates_without_a_gpu():
     assert b"collective" in lib.oasis_last_error()
     a = _lib.OasisTpArgs(1, 2, 8, 16, 16, 16, 16, cb, None, 16, 16)
     assert lib.oasis_dit_forward_tp(C.byref(w), C.byref(a), None) == -3
+    assert b"workspace" in lib.oasis_last_error()
+
+
+def test_vae_encoder_entry_validates_without_a_gpu():
+    lib = _lib.load()
+    assert lib.oasis_vae_encoder_workspace_size(0) == 0
+    assert lib.oasis_vae_encoder_workspace_size(2) > lib.oasis_vae_encoder_workspace_size(1) > 0
+    w = _lib.OasisVaeEncoderWeights()
+    a = _lib.OasisVaeEncodeArgs(1, 16, None, None, 16, 1 << 30)  # no output
+    assert lib.oasis_vae_encode(C.byref(w), C.byref(a), None) == -1
+    assert b"neither latent nor chunk" in lib.oasis_last_error()
+    w.num_blocks = 13
+    a = _lib.OasisVaeEncodeArgs(1, 16, 16, None, 16, 1 << 30)
+    assert lib.oasis_vae_encode(C.byref(w), C.byref(a), None) == -1
+    assert b"num_blocks=13" in lib.oasis_last_error()
+    w.num_blocks = 0
+    w.patch_w = w.quant_w = w.norm_w = w.norm_b = 16
+    a = _lib.OasisVaeEncodeArgs(1, 16, 16, None, 16, 16)
+    assert lib.oasis_vae_encode(C.byref(w), C.byref(a), None) == -3
     assert b"workspace" in lib.oasis_last_error()
