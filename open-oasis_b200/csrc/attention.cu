@@ -657,7 +657,7 @@ int attention_full_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, int grou
   if (use_tc && attention_tc_supported(seq)) return attention_tc_launch(qkv, out, groups, seq, H, s);
   if (seq == kSpatialSeq) {
     constexpr int smem = 2 * 3 * kSpatialTile * 2;
-    static bool attr[64] = {false};
+    static std::atomic<bool> attr[64];  // per device
     int dev = 0;
     cudaGetDevice(&dev);
     if (!attr[dev & 63]) {

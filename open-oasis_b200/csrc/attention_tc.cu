@@ -462,7 +462,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 template <int KB>
 int launch_tc(const __nv_bfloat16* qkv, __nv_bfloat16* out, int groups, int seq, int H, cudaStream_t s) {
   using C = TcCfg<KB>;
-  static bool attr[64] = {false};
+  static std::atomic<bool> attr[64];  // per device
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr[dev & 63]) {

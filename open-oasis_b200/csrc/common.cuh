@@ -6,6 +6,7 @@
 // alloc/mma/commit/ld, and a device-side error word the host can read back.
 #pragma once
 
+#include <atomic>
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>

@@ -800,12 +800,12 @@ int make_out_map(CUtensorMap* map, void* ptr, long long M, long long N, long lon
   return OASIS_OK;
 }
 
-int g_num_sms[64] = {0};
+std::atomic<int> g_num_sms[64];  // per device, zero until first queried
 
 template <int BN, bool kLN>
 int launch_bn(const GemmProblem& p, int splits, cudaStream_t stream) {
   using C = Cfg<BN>;
-  static bool attr_set[64] = {false};
+  static std::atomic<bool> attr_set[64];  // per device; host threads may launch concurrently
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev & 63]) {
