@@ -163,3 +163,13 @@ def test_vae_encoder_entry_validates_without_a_gpu():
     a = _lib.OasisVaeEncodeArgs(1, 16, 16, None, 16, 16)
     assert lib.oasis_vae_encode(C.byref(w), C.byref(a), None) == -3
     assert b"workspace" in lib.oasis_last_error()
+
+
+def test_frame_count_bounds():
+    """T is bounded by the temporal RoPE table (OASIS_MAX_FRAMES = 32 positions)."""
+    lib = _lib.load()
+    w = _lib.OasisDitWeights()
+    for T in (0, 33):
+        d = _lib.OasisDitArgs(1, T, 16, 16, 16, 1, 16, 1 << 40)
+        assert lib.oasis_dit_forward(C.byref(w), C.byref(d), None) == -1
+        assert b"frames" in lib.oasis_last_error() or b"T=" in lib.oasis_last_error(), lib.oasis_last_error()

@@ -42,7 +42,7 @@ def _inputs(B, T, seed=0):
     return z, cond
 
 
-@pytest.mark.parametrize("B,T", [(1, 1), (1, 2), (2, 3), (1, 8)])
+@pytest.mark.parametrize("B,T", [(1, 1), (1, 2), (2, 3), (1, 8), (1, 32)])  # T = 32: the RoPE table's last position
 def test_dit_forward_small(dit_small, B, T):
     sd, dw = dit_small
     z, cond = _inputs(B, T)
