@@ -261,8 +261,8 @@ def gemm_roofline(M, reps, peaks):
     del a, w, out, resid
     return {"bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
             "frac": round(achieved / peaks["bf16_tflops"], 3), "traffic": GEMM_TRAFFIC_BYTES_PER_LAUNCH,
-            "kernel": f"gemm_kernel<256> FC1+GELU launch, M={M} N=4096 K=1024 (2MNK FLOP / CUDA-event time, "
-                      "avg of 10 launches)",
+            "kernel": f"gemm_pair_kernel FC1+GELU launch (256 x 256 tiles on CTA pairs), M={M} N=4096 K=1024 "
+                      "(2MNK FLOP / CUDA-event time, avg of 10 launches)",
             "peak_source": f"bf16_tflops (burst, kernel timed alone) of {peaks['source']}",
             "all_dit_shapes_tflops": round(total_f / total_ms / 1e9, 1), "per_shape": per, "M": M}
 

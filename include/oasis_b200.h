@@ -347,7 +347,7 @@ typedef struct OasisGemmArgs {
   const float* resid; long long ldr;
   const float* gate; long long ldg; int rows_per_frame;
   const float* rope; int rope_div; int rope_mod;
-  int block_n; /* 0 = heuristic, else 64 / 128 / 256 */
+  int block_n; /* 0 = heuristic, else 32 / 64 / 128 / 256, or 512: 256 x 256 tiles on a 2-CTA pair */
   int splits;  /* 0 = heuristic, 1 = none */
   void* workspace; size_t workspace_bytes;
   int rope_dim; /* ROPE: width of the q (and k) section; 0 = 1024 (16 heads) */

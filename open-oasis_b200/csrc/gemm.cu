@@ -736,6 +736,202 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// CTA-pair GEMM: 256 x 256 output tiles, one 2-CTA cluster per tile.
+// ---------------------------------------------------------------------------
+// Each CTA of the pair stages its own 128 rows of A and its own 128 rows of W
+// (so a pair reads A and W once per 256 x 256 tile: a third less L2 -> shared
+// traffic per FLOP than a 128 x 256 tile per CTA). The leader (rank 0) issues
+// cta_group::2 MMAs of M = 256, N = 256 that read both CTAs' shared memory and
+// accumulate into both CTAs' TMEM (rank r holds rows [128 r, 128 r + 128) of the
+// tile). TMA completion of both CTAs' loads counts on the leader's `full`
+// barrier; the MMA commit arrives on the `empty` and `acc_full` barriers of both
+// CTAs; both CTAs' epilogue warps release an accumulator on the leader's
+// `acc_empty`. No TMA multicast. Every wait is bounded as in gemm_kernel.
+struct PairCfg {
+  static constexpr int BNP = 256;                 // output columns per tile
+  static constexpr int A_BYTES = BM * BK * 2;     // this CTA's 128 A rows x 64 K
+  static constexpr int B_BYTES = 128 * BK * 2;    // this CTA's 128 W rows x 64 K
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = 5;
+  static constexpr int NBUF = 2;
+  static constexpr int TMEM_COLS = 2 * BNP;       // two accumulators
+  static constexpr int STG_BYTES = kEpiWarps * kStgBytes * NBUF;
+  static constexpr int BAR_BYTES = 512;
+  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + STG_BYTES + BAR_BYTES;
+  static_assert(SMEM <= 232448, "shared memory per CTA");
+  static_assert(2 * STAGES + 4 + 2 * kEpiWarps + 2 <= BAR_BYTES / 8, "barrier area");
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+                     const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR, const int M,
+                     const int N, const int K, const EpiParams epi) {
+  using C = PairCfg;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* staging = smem + C::STAGES * C::STAGE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(staging + C::STG_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* acc_full = empty + C::STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* rbar = reinterpret_cast<uint64_t*>(tmem_base_slot + 4);  // [kEpiWarps][2]
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  pdl_trigger();
+
+  const int m_tiles = (M + 2 * BM - 1) / (2 * BM);
+  const int n_tiles = (N + C::BNP - 1) / C::BNP;
+  const int units = m_tiles * n_tiles;
+  const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+  const int kb_total = K / BK;
+
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmW);
+    prefetch_tmap(&tmO);
+    if (reads_resid(epi.mode)) prefetch_tmap(&tmR);
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 2 * kEpiWarps);  // both CTAs' epilogue warps (used on the leader)
+    }
+    for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&rbar[i], 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_base_slot, C::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  // barriers initialised and TMEM allocated in both CTAs before either uses the other's
+  tc_fence_before();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_slot;
+  if (warp != 0) pdl_wait();
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int pre = 0;
+      // W is never written by an earlier kernel: start its first stages before
+      // waiting for the upstream kernel, then add the A tiles
+      if (pair < units) {
+        const int n0 = (pair % n_tiles) * C::BNP + (int)rank * 128;
+        pre = kb_total < C::STAGES ? kb_total : C::STAGES;
+        for (int i = 0; i < pre; ++i) {
+          if (leader) mbar_arrive_expect_tx(&full[i], 2 * C::STAGE_BYTES);
+          tma_load_2d_pair(smem + i * C::STAGE_BYTES + C::A_BYTES, &tmW, mapa_shared(smem_u32(&full[i]), 0),
+                           i * BK, n0);
+        }
+      }
+      pdl_wait();
+      for (int k = 0, u = pair; ok && u < units; ++k, u += pairs) {
+        const int m0 = (u / n_tiles) * 2 * BM + (int)rank * BM;
+        const int n0 = (u % n_tiles) * C::BNP + (int)rank * 128;
+        for (int kb = 0; kb < kb_total; ++kb) {
+          uint8_t* sa = smem + stage * C::STAGE_BYTES;
+          const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
+          if (k == 0 && kb < pre) {
+            tma_load_2d_pair(sa, &tmA, bar, kb * BK, m0);  // W already in flight
+          } else {
+            if (!mbar_wait(&empty[stage], phase ^ 1, kDevTimeoutSmemEmpty)) {
+              ok = false;
+              break;
+            }
+            if (leader) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
+            tma_load_2d_pair(sa, &tmA, bar, kb * BK, m0);
+            tma_load_2d_pair(sa + C::A_BYTES, &tmW, bar, kb * BK, n0);
+          }
+          if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (leader only) ----------------
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(2 * BM, C::BNP);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int u = pair; ok && u < units; u += pairs) {
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, kDevTimeoutAccEmpty)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * C::BNP;
+        for (int kb = 0; kb < kb_total; ++kb) {
+          if (!mbar_wait(&full[stage], phase, kDevTimeoutTmaFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * C::STAGE_BYTES);
+          const uint64_t adesc = smem_desc_sw128(a_addr);
+          const uint64_t bdesc = smem_desc_sw128(a_addr + C::A_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            tc_mma_bf16_pair(d_tmem, adesc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2), idesc,
+                             (kb > 0 || k > 0) ? 1u : 0u);
+          tc_commit_pair(&empty[stage], 0x3);
+          if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        tc_commit_pair(&acc_full[acc], 0x3);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+    }
+  } else {
+    // ---------------- Epilogue (warps 2..9, both CTAs) ----------------
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    uint8_t* stg = staging + (warp - 2) * kStgBytes * C::NBUF;
+    uint64_t* my_rbar = rbar + 2 * (warp - 2);
+    const bool resid_tma = reads_resid(epi.mode);
+    const SplitK nosplit{nullptr, 1};
+    int sbuf = 0;
+    uint32_t rphase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    for (int u = pair; ok && u < units; u += pairs) {
+      const int m0q = (u / n_tiles) * 2 * BM + (int)rank * BM + quarter * 32, n0 = (u % n_tiles) * C::BNP;
+      const uint32_t t_acc = tmem_base + lane_off + acc * C::BNP;
+      if (resid_tma)
+        epilogue_tile_resid(epi, &tmO, &tmR, stg, C::NBUF, my_rbar, rphase, t_acc, M, N, C::BNP, m0q, n0, half, lane,
+                            &acc_full[acc], acc_phase, ok);
+      else
+        epilogue_tile(epi, nosplit, &tmO, stg, C::NBUF, sbuf, t_acc, M, N, C::BNP, m0q, n0, u, 0, quarter, half,
+                      lane, &acc_full[acc], acc_phase, ok);
+      if (!ok) break;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[acc]), 0));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+    if (lane == 0) bulk_wait0();  // stores complete before the staging memory goes away
+  }
+
+  // neither CTA frees TMEM or exits while the other may still signal its barriers
+  tc_fence_before();
+  cluster_sync_all();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+}
+
+// ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
@@ -846,6 +1042,51 @@ int launch_bn(const GemmProblem& p, int splits, cudaStream_t stream) {
   return check_launch("gemm_kernel");
 }
 
+// 256 x 256 tiles on CTA pairs (gemm_pair_kernel); no split-K, no LN epilogue.
+int launch_pair(const GemmProblem& p, cudaStream_t stream) {
+  using C = PairCfg;
+  static std::atomic<bool> attr_set[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return set_error(OASIS_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    attr_set[dev & 63] = true;
+  }
+  CUtensorMap ta, tw, to, tr;
+  OASIS_TRY(make_map(&ta, p.A, p.M, p.K, p.lda, BM, 1));
+  OASIS_TRY(make_map(&tw, p.W, p.N, p.K, p.K, 128, 1));
+  OASIS_TRY(make_out_map(&to, p.epi.out, p.M, p.N, p.epi.ldo, bf16_out(p.epi.mode)));
+  if (reads_resid(p.epi.mode))
+    OASIS_TRY(make_out_map(&tr, const_cast<float*>(p.epi.resid), p.M, p.N, p.epi.ldr, false));
+  else
+    tr = to;
+  const int units = ((p.M + 2 * BM - 1) / (2 * BM)) * ((p.N + C::BNP - 1) / C::BNP);
+  const int max_pairs = num_sms() / 2;
+  const int pairs = units < max_pairs ? units : max_pairs;
+  launch_pdl_cluster(gemm_pair_kernel, dim3(2 * pairs), dim3(kThreads), C::SMEM, stream, 2, ta, tw, to, tr, p.M, p.N,
+                     p.K, p.epi);
+  return check_launch("gemm_pair_kernel");
+}
+
+// Which large GEMMs run on CTA pairs. Isolated launches at C4 shapes (TFLOP/s,
+// single 128 x 256 tiles -> pairs): FC2 1158 -> 1370-1445, O ~860 -> 830-905,
+// FC1 ~1100-1200 either way, QKV 1107 -> 1038-1110; the whole C4 frame, per MHz
+// of SM clock under the power cap: no pairs 0.139 frames/s/MHz, pairs for the
+// fp32 residual epilogues only 0.148, pairs everywhere 0.153-0.155 (the lower
+// L2 -> shared traffic buys clock). Default: every eligible GEMM.
+// OASIS_GEMM_PAIR=0: never; =resid: the residual epilogues only.
+enum PairMode { kPairOff = 0, kPairResid = 1, kPairAll = 2 };
+int pair_mode() {
+  static const int m = [] {
+    const char* e = getenv("OASIS_GEMM_PAIR");
+    if (e && e[0] == '0') return (int)kPairOff;
+    if (e && e[0] == 'r') return (int)kPairResid;
+    return (int)kPairAll;
+  }();
+  return m;
+}
+
 struct Plan {
   int bn;
   int splits;
@@ -931,6 +1172,11 @@ int gemm_launch(const GemmProblem& p, cudaStream_t stream) {
   if (pl.bn == 64 && !bf16_out(p.epi.mode) && p.epi.mode != kEpiImage &&
       ((p.M + BM - 1) / BM) * ((p.N + 63) / 64) < num_sms() / 2)
     pl.bn = 32;
+  if (p.block_n == 512) {  // explicit request: 256 x 256 tiles on a CTA pair
+    OASIS_REQUIRE(p.splits <= 1 && p.epi.mode != kEpiImage && p.epi.mode != kEpiGatedResidLN,
+                  "GEMM: CTA-pair tiles take no split-K, image or LN epilogue");
+    return launch_pair(p, stream);
+  }
   if (p.block_n) pl.bn = p.block_n;
   if (p.splits) pl.splits = p.splits;
   if (pl.splits > 1 && !p.workspace) pl.splits = 1;
@@ -943,6 +1189,13 @@ int gemm_launch(const GemmProblem& p, cudaStream_t stream) {
   const int k_stages = p.K / (pl.bn <= 128 ? 2 * BK : BK);
   OASIS_REQUIRE(pl.splits >= 1 && pl.splits <= 8, "GEMM: splits=%d outside [1, 8] (one cluster per tile)", pl.splits);
   OASIS_REQUIRE(k_stages % pl.splits == 0, "GEMM: splits=%d must divide the %d K stages", pl.splits, k_stages);
+  // Large problems: 256 x 256 tiles on CTA pairs, when there are enough of them
+  // to fill the GPU (one pair per two SMs).
+  const int pm = pair_mode();
+  if (!p.block_n && pl.bn == 256 && pl.splits == 1 && pm != kPairOff && p.epi.mode != kEpiImage &&
+      p.epi.mode != kEpiGatedResidLN && (pm == kPairAll || reads_resid(p.epi.mode)) && p.N % 256 == 0 &&
+      ((p.M + 2 * BM - 1) / (2 * BM)) * (p.N / 256) >= num_sms() / 2)
+    return launch_pair(p, stream);
   switch (pl.bn) {
     case 32: return launch_bn<32, false>(p, pl.splits, stream);
     case 64: return launch_bn<64, false>(p, pl.splits, stream);

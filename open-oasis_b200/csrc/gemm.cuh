@@ -59,7 +59,7 @@ struct GemmProblem {
   int M = 0, N = 0, K = 0;
   EpiParams epi;
   LnParams ln;              // kEpiGatedResidLN only
-  int block_n = 0;          // 0 = heuristic, else 64/128/256
+  int block_n = 0;          // 0 = heuristic, else 32/64/128/256, or 512: 256 x 256 tiles on a CTA pair
   int splits = 0;           // 0 = heuristic, 1 = no split-K
   void* workspace = nullptr;  // split-K partial tiles (may be null -> no split)
   size_t workspace_bytes = 0;

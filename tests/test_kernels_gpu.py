@@ -52,6 +52,9 @@ def rand_bf16(*shape, scale=1.0, seed=0):
     (577, 1024, 4096, 128, 1), (2, 2048, 1024, 64, 2), (1152, 64, 1024, 64, 1), (4608, 1024, 4096, 0, 0),
     (73, 1200, 1024, 128, 1), (512, 1024, 1024, 64, 8), (300, 1024, 4096, 32, 2), (300, 1024, 1024, 32, 1),
     (300, 1216, 192, 64, 1), (130, 1024, 4096, 64, 1),
+    # block_n 512: 256 x 256 tiles on CTA pairs (one stage; ragged M and N; several tiles per pair)
+    (256, 256, 64, 512, 1), (1000, 4096, 1024, 512, 1), (300, 1200, 320, 512, 1), (20000, 4096, 1024, 512, 1),
+    (577, 1024, 4096, 512, 1),
 ])
 def test_gemm_f32(M, N, K, block_n, splits):
     a = rand_bf16(M, K, seed=1)
@@ -75,12 +78,13 @@ def test_gemm_splitk_deterministic():
 
 
 @pytest.mark.parametrize("mode", [1, 2, 3])
-def test_gemm_bf16_epilogues(mode):
+@pytest.mark.parametrize("block_n", [0, 512])
+def test_gemm_bf16_epilogues(mode, block_n):
     M, N, K = 700, 4096, 1024
     a, w = rand_bf16(M, K, seed=5), rand_bf16(N, K, scale=0.05, seed=6)
     bias = torch.randn(N, device=DEV) * 0.1
     out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
-    gemm(a, w, mode, out, bias=bias)
+    gemm(a, w, mode, out, bias=bias, block_n=block_n)
     ref = a.float() @ w.float().T + bias
     if mode == 2:
         ref = F.gelu(ref, approximate="tanh")
@@ -89,7 +93,8 @@ def test_gemm_bf16_epilogues(mode):
     assert rel_l2(out.float(), ref) < 5e-3
 
 
-@pytest.mark.parametrize("M,block_n,splits", [(288, 0, 0), (1152, 256, 1), (300, 64, 4)])
+@pytest.mark.parametrize("M,block_n,splits", [(288, 0, 0), (1152, 256, 1), (300, 64, 4), (1152, 512, 1),
+                                                (40000, 512, 1)])
 def test_gemm_gated_residual(M, block_n, splits):
     N, K, P = 1024, 1024, 144
     frames = (M + P - 1) // P
@@ -106,6 +111,18 @@ def test_gemm_gated_residual(M, block_n, splits):
     gate = table[torch.arange(M, device=DEV) // P, off:off + N]
     ref = resid + gate * (a.float() @ w.float().T + bias)
     assert rel_l2(z, ref) < 1e-5
+
+
+def test_gemm_pair_matches_single_cta_tiles():
+    """The heuristic sends a C4-sized FC1 to CTA pairs; the result matches 128 x 256 tiles."""
+    M, N, K = 73728, 4096, 1024
+    a, w = rand_bf16(M, K, seed=11), rand_bf16(N, K, scale=0.05, seed=12)
+    bias = torch.randn(N, device=DEV) * 0.1
+    o_pair = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    o_one = torch.empty_like(o_pair)
+    gemm(a, w, 2, o_pair, bias=bias)
+    gemm(a, w, 2, o_one, bias=bias, block_n=256)
+    assert rel_l2(o_pair.float(), o_one.float()) < 1e-3
 
 
 def test_gemm_residual():
@@ -132,7 +149,8 @@ def _rope_ref(x, tab, pos, hd=1024):
 
 
 @pytest.mark.parametrize("kind", ["spatial", "temporal", "vae"])
-def test_gemm_rope(kind):
+@pytest.mark.parametrize("block_n", [0, 512])
+def test_gemm_rope(kind, block_n):
     if kind == "spatial":
         M, tab, div, mod = 2 * 144 * 3, H.rope_pair_table(H.spatial_rope_angles(H.default_spatial_freqs())), 1, 144
     elif kind == "temporal":
@@ -146,7 +164,7 @@ def test_gemm_rope(kind):
     tab_d = tab.to(DEV)
     out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
     quad = tab.reshape(tab.shape[0], 16, 4).permute(1, 0, 2).contiguous().to(DEV)  # [16, positions, 4]
-    gemm(a, w, 6, out, bias=bias, rope=quad, rope_div=div, rope_mod=mod, rope_stride=tab.shape[0])
+    gemm(a, w, 6, out, bias=bias, rope=quad, rope_div=div, rope_mod=mod, rope_stride=tab.shape[0], block_n=block_n)
     x = a.float() @ w.float().T + (bias if bias is not None else 0)
     pos = (torch.arange(M, device=DEV) // div) % mod
     ref = _rope_ref(x, tab_d, pos)
