@@ -38,6 +38,33 @@ def test_shards_reassemble_the_projections():
         assert torch.allclose(parts, (x @ w1.T) @ w2.T)
 
 
+def test_shard_struct_points_at_the_shards():
+    """The OasisDitWeights handed to oasis_dit_forward_tp: sub-block pointers are
+    this rank's shards (1/n of the QKV / FC1 rows, O / FC2 columns), everything
+    else is the replicated full struct."""
+    from oasis_b200.weights import init_dit_weights
+
+    sd = init_dit_weights(seed=3, n_blocks=2)
+    n, r = 4, 1
+    tpw = TP.TPDitWeights(sd, n, r, "cpu")
+    st, full = tpw.struct, tpw.full.struct
+    assert tpw.heads == 4 and st.num_subblocks == full.num_subblocks == 4
+    for f in ("adaln_w", "adaln_b", "final_w", "final_b", "embed_w", "embed_b", "rope_spatial", "rope_temporal"):
+        assert getattr(st, f) == getattr(full, f), f
+    for i, blk in enumerate(tpw.sub):
+        for k, t in blk.items():
+            assert getattr(st.sub[i], k) == t.data_ptr(), (i, k)
+        assert tuple(blk["qkv_w"].shape) == (3 * 1024 // n, 1024)
+        assert tuple(blk["out_w"].shape) == (1024, 1024 // n)
+        assert tuple(blk["fc1_w"].shape) == (4096 // n, 1024) and tuple(blk["fc1_b"].shape) == (4096 // n,)
+        assert tuple(blk["fc2_w"].shape) == (1024, 4096 // n)
+    # rank r's q rows are heads [16 r / n, 16 (r + 1) / n) of the checkpoint's q block
+    q = sd["blocks.0.s_attn.to_qkv.weight"][:1024]
+    assert torch.equal(tpw.sub[0]["qkv_w"][:256].float(), q[256:512].to(torch.bfloat16).float())
+    with pytest.raises(ValueError):
+        TP.TPDitWeights(sd, 3, 0, "cpu")
+
+
 def _free_port() -> int:
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
