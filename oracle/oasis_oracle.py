@@ -10,8 +10,13 @@ module load). Each function cites the reference lines it follows. The reference
 ships no golden tensors; the host-side pieces (timestep embedding, schedule,
 RoPE math, patch layouts, bridge matrices, VAE unpatchify) are pinned against
 fixtures generated from the reference's own functions (tests/golden/). The
-device dataflow (sub-block, attention, DDIM, VAE blocks) has no reference-side
-fixture: that part of parity is unpinned and checked against this restatement.
+sub-block formula (LN + adaLN modulate, QKV, spatial attention, O + gated
+residual, MLP) is pinned against the PyTorch reference section of the
+reference's own sub-block test, run on its seeded inputs
+(reference_subblock.npz): with that test's 160-row unmasked attention the
+oracle's sub_block_core matches to 7e-9 relative. RoPE, temporal attention,
+DDIM and the VAE blocks have no reference-side fixture: that part of parity is
+unpinned and checked against this restatement.
 
 Semantic choices (where the reference and the benchmark spec differ):
   * spatial attention runs over exactly the 144 real tokens (the reference pads to
@@ -130,31 +135,60 @@ def _attn(q, k, v, mask=None):
     return torch.softmax(s, dim=-1) @ v
 
 
+def sub_block_core(x: torch.Tensor, mods, qkv_w: torch.Tensor, out_w: torch.Tensor, out_b, fc1_w: torch.Tensor,
+                   fc1_b, fc2_w: torch.Tensor, fc2_b, attend) -> torch.Tensor:
+    """One DiT sub-block on token rows x [..., 1024] (oasis_inference.py:1053-1201;
+    the formula of tests/test_dit_block.py:524-569): LN (no affine, eps 1e-6) and
+    adaLN modulate, QKV (no bias), attention (`attend(qkv) -> o`, same rows as x),
+    O projection + bias and the gated residual, LN and modulate, FC1 + GELU-tanh,
+    FC2, gated residual. mods = (shift, scale, gate) x (msa, mlp), broadcastable to x."""
+    sh_a, sc_a, g_a, sh_m, sc_m, g_m = mods
+    h = _ln(x) * (1 + sc_a) + sh_a
+    o = attend(F.linear(h, qkv_w))
+    x = x + g_a * F.linear(o, out_w, out_b)
+    h = _ln(x) * (1 + sc_m) + sh_m
+    h = F.gelu(F.linear(h, fc1_w, fc1_b), approximate="tanh")
+    return x + g_m * F.linear(h, fc2_w, fc2_b)
+
+
+def spatial_attend_padded(qkv: torch.Tensor, pad_rows: int) -> torch.Tensor:
+    """The reference test's spatial attention for one frame (tests/test_dit_block.py:
+    537-549): qkv [144, 3072] split into 16 heads, q, k, v zero-padded to 144 +
+    pad_rows rows, unmasked softmax(q k^T / 8) v, the 144 real rows kept. With
+    pad_rows = 16 the zero keys take softmax weight (the reference's 160-row
+    layout); pad_rows = 0 is the 144-token attention this build implements."""
+    q, k, v = [t.reshape(P, HEADS, DH).permute(1, 0, 2) for t in qkv.chunk(3, dim=-1)]
+    if pad_rows:
+        q, k, v = [F.pad(t, (0, 0, 0, pad_rows)) for t in (q, k, v)]
+    return _attn(q, k, v)[:, :P].permute(1, 0, 2).reshape(P, D)
+
+
 def dit_sub_block(x: torch.Tensor, silu_c: torch.Tensor, sd: dict, prefix: str, kind: str,
                   s_freqs: torch.Tensor, t_freqs: torch.Tensor) -> torch.Tensor:
     """x [B, T, 144, 1024], silu_c [B, T, 1024] -> x after one spatial/temporal sub-block."""
     B, T = x.shape[:2]
     mod = F.linear(silu_c, sd[f"{prefix}_adaLN_modulation.1.weight"], sd[f"{prefix}_adaLN_modulation.1.bias"])
-    sh_a, sc_a, g_a, sh_m, sc_m, g_m = [m[:, :, None, :] for m in mod.chunk(6, dim=-1)]
-    h = _ln(x) * (1 + sc_a) + sh_a
-    qkv = F.linear(h, sd[f"{prefix}_attn.to_qkv.weight"])
-    q, k, v = [t.reshape(B, T, P, HEADS, DH) for t in qkv.chunk(3, dim=-1)]
-    if kind == "s":
-        fr = axial_freqs(s_freqs, FH, FW)  # (144, 64)
-        q, k = apply_rotary(fr[:, None, :], q), apply_rotary(fr[:, None, :], k)
-        q, k, v = [t.permute(0, 1, 3, 2, 4) for t in (q, k, v)]  # B T H P Dh
-        o = _attn(q, k, v).permute(0, 1, 3, 2, 4)
-    else:
-        fr = temporal_freqs(t_freqs, T)  # (T, 64)
-        q, k = apply_rotary(fr[:, None, None, :], q), apply_rotary(fr[:, None, None, :], k)
-        q, k, v = [t.permute(0, 2, 3, 1, 4) for t in (q, k, v)]  # B P H T Dh
-        causal = torch.tril(torch.ones(T, T, dtype=torch.bool))
-        o = _attn(q, k, v, causal).permute(0, 3, 1, 2, 4)
-    o = o.reshape(B, T, P, D)
-    x = x + g_a * F.linear(o, sd[f"{prefix}_attn.to_out.weight"], sd[f"{prefix}_attn.to_out.bias"])
-    h = _ln(x) * (1 + sc_m) + sh_m
-    h = F.gelu(F.linear(h, sd[f"{prefix}_mlp.fc1.weight"], sd[f"{prefix}_mlp.fc1.bias"]), approximate="tanh")
-    return x + g_m * F.linear(h, sd[f"{prefix}_mlp.fc2.weight"], sd[f"{prefix}_mlp.fc2.bias"])
+    mods = [m[:, :, None, :] for m in mod.chunk(6, dim=-1)]
+
+    def attend(qkv):
+        q, k, v = [t.reshape(B, T, P, HEADS, DH) for t in qkv.chunk(3, dim=-1)]
+        if kind == "s":
+            fr = axial_freqs(s_freqs, FH, FW)  # (144, 64)
+            q, k = apply_rotary(fr[:, None, :], q), apply_rotary(fr[:, None, :], k)
+            q, k, v = [t.permute(0, 1, 3, 2, 4) for t in (q, k, v)]  # B T H P Dh
+            o = _attn(q, k, v).permute(0, 1, 3, 2, 4)
+        else:
+            fr = temporal_freqs(t_freqs, T)  # (T, 64)
+            q, k = apply_rotary(fr[:, None, None, :], q), apply_rotary(fr[:, None, None, :], k)
+            q, k, v = [t.permute(0, 2, 3, 1, 4) for t in (q, k, v)]  # B P H T Dh
+            causal = torch.tril(torch.ones(T, T, dtype=torch.bool))
+            o = _attn(q, k, v, causal).permute(0, 3, 1, 2, 4)
+        return o.reshape(B, T, P, D)
+
+    return sub_block_core(x, mods, sd[f"{prefix}_attn.to_qkv.weight"], sd[f"{prefix}_attn.to_out.weight"],
+                          sd[f"{prefix}_attn.to_out.bias"], sd[f"{prefix}_mlp.fc1.weight"],
+                          sd[f"{prefix}_mlp.fc1.bias"], sd[f"{prefix}_mlp.fc2.weight"], sd[f"{prefix}_mlp.fc2.bias"],
+                          attend)
 
 
 def n_dit_blocks(sd: dict) -> int:
