@@ -14,9 +14,12 @@ sub-block formula (LN + adaLN modulate, QKV, spatial attention, O + gated
 residual, MLP) is pinned against the PyTorch reference section of the
 reference's own sub-block test, run on its seeded inputs
 (reference_subblock.npz): with that test's 160-row unmasked attention the
-oracle's sub_block_core matches to 7e-9 relative. RoPE, temporal attention,
-DDIM and the VAE blocks have no reference-side fixture: that part of parity is
-unpinned and checked against this restatement.
+oracle's sub_block_core matches to 7e-9 relative. RoPE (axial and temporal) is
+pinned against the reference test's restatement of rotary-embedding-torch
+(reference_rope.npz), and the DDIM schedule, coefficients and update against the
+reference's own main-block code run at 4 steps (reference_ddim.npz). Causal
+temporal attention and the VAE blocks have no reference-side fixture: that part
+of parity is unpinned and checked against this restatement.
 
 Semantic choices (where the reference and the benchmark spec differ):
   * spatial attention runs over exactly the 144 real tokens (the reference pads to

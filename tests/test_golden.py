@@ -6,7 +6,7 @@ import numpy as np
 import pytest
 import torch
 
-from tests.helpers import GOLDEN, GOLDEN_SUBBLOCK
+from tests.helpers import GOLDEN, GOLDEN_DDIM, GOLDEN_ROPE, GOLDEN_SUBBLOCK
 from oracle import oasis_oracle as O
 from oasis_b200 import host as H
 from tests.golden.make_golden import cond_weights, conv_weights
@@ -205,3 +205,42 @@ def test_sub_block_matches_reference_test_formula(pad_rows):
         # the attention output is rescaled by the softmax mass of the real keys;
         # the residual stream keeps the sub-block output close
         assert 1e-2 < proj_rel < 0.2 and rel < 1e-3, (rel, proj_rel)  # measured 6.7e-2 and 8.5e-5
+
+
+def test_rope_matches_rotary_embedding_torch_restatement():
+    """The oracle's axial (9 x 16 grid) and temporal RoPE against the reference's
+    restatement of rotary-embedding-torch (tests/test_rope.py: get_axial_freqs,
+    apply_rotary_emb, rotate_queries_or_keys), run on the same frequencies and
+    seeded queries."""
+    g = np.load(GOLDEN_ROPE)
+    gen = torch.Generator().manual_seed(int(g["seed"]))
+    q = torch.randn(1, 16, 9, 16, 64, generator=gen)
+    qt = torch.randn(2, 144, 16, 8, 64, generator=gen)
+    assert q.double().sum().item() == float(g["q_sum"]) and qt.double().sum().item() == float(g["qt_sum"])
+    s_freqs, t_freqs = torch.from_numpy(g["s_freqs"]), torch.from_numpy(g["t_freqs"])
+    axial = O.axial_freqs(s_freqs, 9, 16).reshape(9, 16, 64)
+    assert torch.allclose(axial, torch.from_numpy(g["axial"]), atol=1e-6)
+    q_rot = O.apply_rotary(axial, q)
+    assert torch.allclose(q_rot[0, :2], torch.from_numpy(g["q_rot_heads01"]), atol=1e-5)
+    assert np.allclose(q_rot.double().sum(dim=(0, 2, 3, 4)).numpy(), g["q_rot_sum_by_head"], atol=1e-3)
+    qt_rot = O.apply_rotary(O.temporal_freqs(t_freqs, 8), qt)
+    assert torch.allclose(qt_rot[0, :4], torch.from_numpy(g["qt_rot_rows"]), atol=1e-5)
+    assert np.allclose(qt_rot.double().sum(dim=(0, 1, 2, 4)).numpy(), g["qt_rot_sum_by_t"], atol=1e-3)
+
+
+def test_ddim_schedule_and_update_match_reference_main_block():
+    """DDIM at 4 steps with the reference's sigmoid schedule: the per-step levels and
+    the six coefficients of host.ddim_schedule (which the kernels receive), and the
+    oracle's update chained over the 4 steps, against the reference's own
+    coefficient loop and ddim_step_fn run on the same chunk and v-predictions."""
+    g = np.load(GOLDEN_DDIM)
+    sched = H.ddim_schedule(4, "sigmoid")
+    assert [s.noise_level for s in sched] == list(g["levels"])
+    np.testing.assert_allclose(np.array([s.as_tuple() for s in sched]), g["coeffs"], rtol=2e-6, atol=1e-9)
+    chunk = torch.from_numpy(g["chunk0"])
+    for i, s in enumerate(sched):
+        at, an = s.at_sqrt ** 2, s.an_sqrt ** 2
+        chunk = O.ddim_update(chunk, torch.from_numpy(g["v"][i]), at, an)
+        ref = torch.from_numpy(g["chunks"][i])
+        rel = ((chunk - ref).norm() / ref.norm()).item()
+        assert rel < 1e-6, (i, rel)  # measured 3e-8 .. 6e-8 (fp32)
