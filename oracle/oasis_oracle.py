@@ -17,9 +17,11 @@ reference's own sub-block test, run on its seeded inputs
 oracle's sub_block_core matches to 7e-9 relative. RoPE (axial and temporal) is
 pinned against the reference test's restatement of rotary-embedding-torch
 (reference_rope.npz), and the DDIM schedule, coefficients and update against the
-reference's own main-block code run at 4 steps (reference_ddim.npz). Causal
-temporal attention and the VAE blocks have no reference-side fixture: that part
-of parity is unpinned and checked against this restatement.
+reference's own main-block code run at 4 steps (reference_ddim.npz), and the
+causal temporal mask against the reference's packed causal bias
+(reference_temporal_mask.npz). The VAE blocks have no reference-side fixture
+(vae.py is absent): that part of parity is unpinned and checked against this
+restatement.
 
 Semantic choices (where the reference and the benchmark spec differ):
   * spatial attention runs over exactly the 144 real tokens (the reference pads to

@@ -10,6 +10,7 @@ GOLDEN = os.path.join(ROOT, "tests", "golden", "reference_host.npz")
 GOLDEN_SUBBLOCK = os.path.join(ROOT, "tests", "golden", "reference_subblock.npz")
 GOLDEN_ROPE = os.path.join(ROOT, "tests", "golden", "reference_rope.npz")
 GOLDEN_DDIM = os.path.join(ROOT, "tests", "golden", "reference_ddim.npz")
+GOLDEN_TEMPORAL_MASK = os.path.join(ROOT, "tests", "golden", "reference_temporal_mask.npz")
 
 # Parity bar of the benchmark spec for bf16 kernels against the fp32 oracle.
 REL_L2_TOL = 1e-2

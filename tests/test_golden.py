@@ -6,7 +6,7 @@ import numpy as np
 import pytest
 import torch
 
-from tests.helpers import GOLDEN, GOLDEN_DDIM, GOLDEN_ROPE, GOLDEN_SUBBLOCK
+from tests.helpers import GOLDEN, GOLDEN_DDIM, GOLDEN_ROPE, GOLDEN_SUBBLOCK, GOLDEN_TEMPORAL_MASK
 from oracle import oasis_oracle as O
 from oasis_b200 import host as H
 from tests.golden.make_golden import cond_weights, conv_weights
@@ -244,3 +244,20 @@ def test_ddim_schedule_and_update_match_reference_main_block():
         ref = torch.from_numpy(g["chunks"][i])
         rel = ((chunk - ref).norm() / ref.norm()).item()
         assert rel < 1e-6, (i, rel)  # measured 3e-8 .. 6e-8 (fp32)
+
+
+@pytest.mark.parametrize("T", [2, 4, 8])
+def test_temporal_attention_matches_reference_causal_bias(T):
+    """The oracle's causal temporal attention (a tril mask per (patch, head)) against
+    the reference's formulation: 32 packed rows of 32 / T (patch, head) groups and
+    softmax(q k^T / 8 + bias) v with its block-diagonal causal bias."""
+    bias = torch.from_numpy(np.load(GOLDEN_TEMPORAL_MASK)[f"bias_T{T}"])
+    groups = 32 // T
+    keep = bias == 0
+    assert torch.equal(keep, torch.block_diag(*[torch.tril(torch.ones(T, T))] * groups).bool())
+    gen = torch.Generator().manual_seed(T)
+    q, k, v = [torch.randn(32, 64, generator=gen) for _ in range(3)]
+    packed = torch.softmax(q @ k.T / 8 + bias, dim=-1) @ v
+    causal = torch.tril(torch.ones(T, T, dtype=torch.bool))
+    per_group = O._attn(q.view(groups, T, 64), k.view(groups, T, 64), v.view(groups, T, 64), causal).reshape(32, 64)
+    assert torch.allclose(per_group, packed, atol=1e-6)
