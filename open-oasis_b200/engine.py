@@ -348,6 +348,28 @@ class VideoEngine:
         self.fe.context_z.copy_(context_z)
         self.ctx_cond.copy_(ctx_cond)
 
+    def set_prompt(self, ew: VaeEncoderDeviceWeights, image: torch.Tensor, prompt_cond: torch.Tensor,
+                   ws: torch.Tensor | None = None):
+        """Starts the loop from B prompt images [B, 3, 360, 640] in [-1, 1] (the
+        reference encodes the prompt on the CPU and fills every context slot with
+        its patch embedding, oasis_inference.py:1744-1754, 1806-1813, 2248-2252):
+        the VAE encoder writes the latent in the DiT's patch layout, which is
+        patch-embedded into each of the T - 1 context slots; the conditioning
+        window is filled with `prompt_cond` [B, 1024] (the context conditioning,
+        stabilisation level and no action)."""
+        B, T, dev = self.B, self.T, self.dw.device
+        if tuple(prompt_cond.shape) != (B, H.D_MODEL):
+            raise ValueError(f"prompt_cond must be [{B}, {H.D_MODEL}]")
+        chunk = torch.empty(B, H.N_PATCHES, H.OUT_DIM, device=dev)
+        if ws is None:
+            ws = workspace(vae_encoder_workspace_bytes(B), dev)
+        vae_encode(ew, image, ws, chunk=chunk)
+        for slot in range(T - 1):
+            patch_embed(self.dw, chunk.view(-1, H.OUT_DIM), self.fe.context_z, (T - 1) * H.N_PATCHES,
+                        slot * H.N_PATCHES)
+        self.ctx_cond.copy_(prompt_cond.to(dev).unsqueeze(1).expand(-1, T - 1, -1))
+        return chunk
+
     def _frame_and_roll(self, stream=None):
         fe, T = self.fe, self.T
         fe.cond[:, :, :T - 1].copy_(self.ctx_cond.unsqueeze(0).expand(fe.cond.shape[0], -1, -1, -1))

@@ -106,3 +106,35 @@ def test_vae_encode_matches_oracle(B, n_blocks):
     chunk2 = torch.zeros_like(chunk)
     E.vae_encode(ew, img.to(dev), E.workspace(E.vae_encoder_workspace_bytes(B), dev), chunk=chunk2)
     assert torch.equal(chunk2, chunk)
+
+
+def _prompt_context_case(dev):
+    """VideoEngine.set_prompt on B = 2 prompt images with T = 3: the encoded prompt,
+    patch-embedded into both context slots, against the oracle's encode ->
+    latent_to_chunk -> patch_embed; the conditioning window is the prompt's."""
+    from oasis_b200 import engine as E
+    from oasis_b200.weights import DitDeviceWeights, VaeDeviceWeights, init_dit_weights, init_vae_weights
+
+    dsd = init_dit_weights(seed=1, n_blocks=1, bias_std=0.02)
+    esd = init_vae_encoder_weights(seed=5, n_blocks=1, bias_std=0.02, norm_std=0.1)
+    dw = DitDeviceWeights(dsd, dev)
+    vw = VaeDeviceWeights(init_vae_weights(seed=2, n_blocks=1), dev)
+    ew = VaeEncoderDeviceWeights(esd, dev)
+    B, T = 2, 3
+    img = _image(B, 13)
+    cond = torch.randn(B, 1024, generator=torch.Generator().manual_seed(14))
+    ve = E.VideoEngine(dw, vw, B, T)
+    ve.set_prompt(ew, img.to(dev), cond.to(dev))
+    if dev.type == "cuda":
+        torch.cuda.synchronize()
+    z = O.patch_embed(O.unpatchify(O.latent_to_chunk(O.vae_encode(img, esd))), dsd)  # (B, 144, 1024)
+    ref = z[:, None].expand(B, T - 1, 144, 1024)
+    got = ve.context_z.cpu()
+    assert rel_l2(got, ref) < REL_L2_TOL and cosine(got, ref) > COS_TOL, (rel_l2(got, ref), cosine(got, ref))
+    assert torch.equal(got[:, 0], got[:, 1])
+    assert torch.equal(ve.ctx_cond.cpu(), cond[:, None].expand(B, T - 1, 1024))
+
+
+@pytest.mark.gpu
+def test_video_engine_starts_from_prompt_images():
+    _prompt_context_case(torch.device("cuda"))
