@@ -107,6 +107,25 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def bench_config(args, world: int, per_gpu: int) -> dict:
+    """The workload both arms report (the reference arm runs it on the CPU)."""
+    return {"workload": f"C4: {args.sessions} sessions x T={args.frames} context, 4 DDIM steps + VAE decode per frame",
+            "model": "Oasis-500M DiT (16 blocks) + ViT-VAE decoder (12 blocks), random init N(0,0.02)",
+            "sessions_total": args.sessions, "sessions_per_gpu": per_gpu, "frames_T": args.frames, "ddim_steps": 4,
+            "parallelism": f"dp{world} (independent sessions, no collective)",
+            "l2": "inputs larger than L2 (1.52 GB weights + >1 GB activations per frame); no flush",
+            "graph": "CUDA graph replay of the whole frame"}
+
+
+def merge_clocks(per_rank: list[dict]) -> dict:
+    """One clocks record for the line: rank 0's median and max SM clock, the union
+    of the throttle reasons seen on any GPU, and every rank's median."""
+    first = per_rank[0]
+    reasons = sorted({r for c in per_rank for r in c.get("reasons", [])})
+    return {"sm_mhz": first.get("sm_mhz"), "sm_max_mhz": first.get("sm_max_mhz"), "reasons": reasons,
+            "samples": first.get("samples"), "per_rank_sm_mhz": [c.get("sm_mhz") for c in per_rank]}
+
+
 # --------------------------------------------------------------------------- CPU oracle
 def cpu_oracle_frame_time(frames_t: int, blocks_sample: int = 1, reps: int = 2):
     """fp32 CPU oracle on this host's cores: times `blocks_sample` DiT block pairs of
@@ -153,25 +172,37 @@ def cpu_oracle_frame_time(frames_t: int, blocks_sample: int = 1, reps: int = 2):
 
 def run_reference(args, rank, world):
     """The reference's CPU path (the fp32 oracle port; the reference itself needs
-    Tenstorrent hardware) on this host's cores, rank 0 only."""
+    Tenstorrent hardware) on this host's cores, rank 0 only.
+
+    One step = one timed sample: one DiT block pair of one session (T frames)
+    and one VAE block. A whole frame of one session is extrapolated from it as
+    4 steps x 16 block pairs + 12 VAE blocks, and sessions run one after another
+    on the CPU, so `value` (frames/s over all sessions) is the extrapolated rate
+    while `ms_per_step` is the time the sample actually took."""
     if rank != 0:
         return
     from oracle import oasis_oracle as O  # noqa: F401  (CPU oracle = reference arm)
 
-    per = []
+    per, sample_ms = [], []
     w = max(args.warmup, 0)
     for i in range(w + args.steps):
+        t0 = time.perf_counter()
         f, cores, sample = cpu_oracle_frame_time(args.frames, blocks_sample=1, reps=1)
+        dt = time.perf_counter() - t0
         if i >= w:
             per.append(f)
+            sample_ms.append(dt * 1000)
     frame_s = statistics.median(per)
     value = 1.0 / frame_s  # sessions are processed one after another on the CPU
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": frame_s * 1000 * args.sessions, "higher_is_better": True,
+        "warmup": args.warmup, "ms_per_step": round(statistics.mean(sample_ms), 3), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "C4 per-session frame on CPU (sample, extrapolated)", "sessions": args.sessions,
-                   "frames_T": args.frames},
+        "config": bench_config(args, world, args.sessions // max(world, 1)),
+        "extrapolated": True,
+        "extrapolation": {"sample": sample, "ms_per_frame_one_session": round(frame_s * 1000, 1),
+                          "ms_per_frame_all_sessions": round(frame_s * 1000 * args.sessions, 1),
+                          "scale_sample_to_frame": "4 x 16 block pairs + 12 VAE blocks from 1 pair + 1 block"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -443,7 +474,7 @@ def main():
     torch.cuda.synchronize()
 
     barrier = PAR.barrier
-    clocks = ClockSampler(local) if rank == 0 else None
+    clocks = ClockSampler(local)  # every rank samples its own GPU
     barrier()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
     ev[0].record()
@@ -452,7 +483,7 @@ def main():
     ev[1].record()
     barrier()
     ms = ev[0].elapsed_time(ev[1])
-    clk = clocks.stop() if clocks else None
+    clk = merge_clocks(PAR.gather_objects(clocks.stop()))
     ms_max = PAR.max_over_ranks(ms)
     value = args.sessions * args.steps / (ms_max / 1000.0)
 
@@ -503,12 +534,7 @@ def main():
             "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": max(args.warmup, 3), "ms_per_step": round(ms_max / args.steps, 3), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": f"C4: {args.sessions} sessions x T={T} context, 4 DDIM steps + VAE decode per frame",
-                       "model": "Oasis-500M DiT (16 blocks) + ViT-VAE decoder (12 blocks), random init N(0,0.02)",
-                       "sessions_total": args.sessions, "sessions_per_gpu": B, "frames_T": T, "ddim_steps": 4,
-                       "parallelism": f"dp{world} (independent sessions, no collective)",
-                       "l2": "inputs larger than L2 (1.52 GB weights + >1 GB activations per frame); no flush",
-                       "graph": "CUDA graph replay of the whole frame"},
+            "config": bench_config(args, world, B),
             "ms_per_dit_step": round(ms_steps / 4, 3), "ms_vae_decode": round(ms_dec, 3),
             "dit_tflops_achieved": round(dit_flops / (ms_steps / 1000) / 1e12, 1),
             "clocks": clk,

@@ -360,6 +360,13 @@ typedef struct OasisGemmArgs {
 
 int oasis_gemm(const OasisGemmArgs* a, oasis_stream_t stream);
 size_t oasis_gemm_workspace_size(int m, int n, int k);
+/* The tile plan oasis_gemm would use for a call with a workspace and these
+ * fields: tile width (512 = 256 x 256 tiles on a 2-CTA pair), K splits, whether
+ * it runs on CTA pairs, and the split-K workspace bytes it needs. Any output
+ * pointer may be NULL. Returns OASIS_ERR_INVALID_ARG for overrides oasis_gemm
+ * would reject. No device work; usable without a GPU (148 SMs assumed). */
+int oasis_gemm_plan(int m, int n, int k, int mode, int block_n, int splits, int* bn_out, int* splits_out,
+                    int* pair_out, size_t* splitk_bytes_out);
 
 /* oasis_gemm for callers that cannot allocate device memory (their allocator
  * belongs to a host framework, or allocation is not allowed where they run): the

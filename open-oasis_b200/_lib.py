@@ -159,6 +159,8 @@ SIGNATURES = {
                                           C.POINTER(OasisFrameArgs), vp]),
     "oasis_gemm": (C.c_int, [C.POINTER(OasisGemmArgs), vp]),
     "oasis_gemm_workspace_size": (C.c_size_t, [C.c_int, C.c_int, C.c_int]),
+    "oasis_gemm_plan": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_int),
+                                  C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_size_t)]),
     "oasis_gemm_static_scratch": (C.c_int, [C.POINTER(OasisGemmArgs), vp]),
     "oasis_gemm_static_scratch_capacity": (C.c_size_t, []),
     "oasis_layernorm": (C.c_int, [C.POINTER(OasisLayerNormArgs), vp]),

@@ -75,10 +75,6 @@ __host__ __device__ constexpr uint32_t idesc_tc(int m, int n, bool b_mn_major) {
 
 __device__ int g_tc_error = 0;
 
-#ifdef OASIS_TC_PROF
-// Diagnostic build only: cycles spent in waits, by site, summed over threads that wait.
-__device__ unsigned long long g_tc_prof[16];
-#endif
 
 __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, int code, int site = 0) {
   const uint32_t addr = smem_u32(bar);
@@ -90,11 +86,7 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, int code
       return false;
     }
   }
-#ifdef OASIS_TC_PROF
-  if ((threadIdx.x & 31) == 0) atomicAdd(&g_tc_prof[site], (unsigned long long)(clock64() - t0));
-#else
   (void)site;
-#endif
   return true;
 }
 
@@ -321,9 +313,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       uint8_t* dst = prow + (chunk >> 3) * (kTcRows * 128) + (((chunk & 7) ^ (row_t & 7)) << 4);
       *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
     };
-#ifdef OASIS_TC_PROF
-    const long long prof_t0 = clock64();
-#endif
     for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
       const TcUnit t = tc_unit(u, H, seq, rows, nsub);
       const int r = t.q0 + row_t;
@@ -336,12 +325,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tc_fence_after();
         uint8_t* prow = sP + b * C::P_BYTES + row_t * 128;
         float alpha = 1.f;
-#ifdef OASIS_TC_PROF_SECTIONS
-        long long pt = clock64();
-#define TC_SECTION(i) if (lane == 0) { const long long n_ = clock64(); atomicAdd(&g_tc_prof[i], (unsigned long long)(n_ - pt)); pt = n_; }
-#else
 #define TC_SECTION(i)
-#endif
         if (__any_sync(0xffffffffu, mine)) {  // same rows, same decision in both halves
           const uint32_t sbase = lane_base + b * kTcSCols;
           // this part's S columns into registers with one TMEM round trip
@@ -448,9 +432,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
     }
     if (ok && pending && accumulate(jb - 1, alpha_prev)) finish();
-#ifdef OASIS_TC_PROF
-    if (lane == 0) atomicAdd(&g_tc_prof[10], (unsigned long long)(clock64() - prof_t0));
-#endif
   }
 
   tc_fence_before();
@@ -494,16 +475,6 @@ int attention_tc_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, int groups
   return launch_tc<144>(qkv, out, groups, seq, H, s);  // key blocks of 144 (VAE: 4 per 576-token frame)
 }
 
-#ifdef OASIS_TC_PROF
-extern "C" int oasis_debug_tc_prof(unsigned long long* out16, int reset) {
-  cudaMemcpyFromSymbol(out16, g_tc_prof, sizeof(g_tc_prof));
-  if (reset) {
-    unsigned long long z[16] = {0};
-    cudaMemcpyToSymbol(g_tc_prof, z, sizeof(z));
-  }
-  return 0;
-}
-#endif
 
 int read_device_error_tc(int reset) {
   int v = 0;

@@ -1050,6 +1050,12 @@ int oasis_gemm(const OasisGemmArgs* a, oasis_stream_t stream) {
 
 size_t oasis_gemm_workspace_size(int m, int n, int k) { return gemm_workspace_bytes(m, n, k); }
 
+int oasis_gemm_plan(int m, int n, int k, int mode, int block_n, int splits, int* bn_out, int* splits_out,
+                    int* pair_out, size_t* splitk_bytes_out) {
+  OASIS_REQUIRE(mode >= kEpiF32 && mode <= kEpiGatedResidLN, "gemm_plan: mode=%d", mode);
+  return gemm_plan(m, n, k, mode, block_n, splits, bn_out, splits_out, pair_out, splitk_bytes_out);
+}
+
 int oasis_layernorm(const OasisLayerNormArgs* a, oasis_stream_t stream) {
   OASIS_REQUIRE(a, "layernorm: null args");
   LayerNormParams p;

@@ -63,18 +63,6 @@ struct Cfg {
   static_assert(SMEM <= 232448, "shared memory per CTA");
 };
 
-#ifdef OASIS_GEMM_PROF
-// Diagnostic build only: cycles each role spends waiting, summed over CTAs.
-// [0] MMA on acc_empty, [1] MMA on full, [2] producer on empty, [3] epilogue on
-// acc_full, [4] MMA loop total, [5] epilogue loop total.
-__device__ unsigned long long g_gemm_prof[8];
-#define PROF_T0() const long long _pt0 = clock64()
-#define PROF_ADD(i) \
-  if ((threadIdx.x & 31) == 0) atomicAdd(&g_gemm_prof[i], (unsigned long long)(clock64() - _pt0))
-#else
-#define PROF_T0()
-#define PROF_ADD(i)
-#endif
 
 struct SplitK {
   float* partials;  // [tiles][splits][BM][BN]
@@ -235,9 +223,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& e, const SplitK& 
   if (resid && half < nchunks && n0 + half * W < N) load_resid(e, r, n0 + half * W, M, rcur);
   bool acc_ready;
   {
-    PROF_T0();
     acc_ready = mbar_wait(acc_bar, acc_parity, kDevTimeoutAccFull);
-    PROF_ADD(3);
   }
   if (!acc_ready) {
     ok = false;
@@ -308,9 +294,7 @@ __device__ __forceinline__ void epilogue_tile_resid(const EpiParams& e, const CU
   __syncwarp();
   bool acc_ready;
   {
-    PROF_T0();
     acc_ready = mbar_wait(acc_bar, acc_parity, kDevTimeoutAccFull);
-    PROF_ADD(3);
   }
   if (!acc_ready) {
     ok = false;
@@ -592,11 +576,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             load_a(sa, &full[stage], kb, m0);  // W already in flight
           } else {
             bool got;
-            {
-              PROF_T0();
-              got = mbar_wait(&empty[stage], phase ^ 1, kDevTimeoutSmemEmpty);
-              PROF_ADD(2);
-            }
+            got = mbar_wait(&empty[stage], phase ^ 1, kDevTimeoutSmemEmpty);
             if (!got) { ok = false; break; }
             mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
             load_a(sa, &full[stage], kb, m0);
@@ -615,25 +595,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-#ifdef OASIS_GEMM_PROF
-      const long long loop_t0 = clock64();
-#endif
       for (int k = 0; ok && unit_at(k, row_blocks, units, n_tiles, m_tiles) >= 0; ++k) {
         bool got;
-        {
-          PROF_T0();
-          got = mbar_wait(&acc_empty[acc], acc_phase ^ 1, kDevTimeoutAccEmpty);
-          PROF_ADD(0);
-        }
+        got = mbar_wait(&acc_empty[acc], acc_phase ^ 1, kDevTimeoutAccEmpty);
         if (!got) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = 0; kb < kb_per_split; ++kb) {
-          {
-            PROF_T0();
-            got = mbar_wait(&full[stage], phase, kDevTimeoutTmaFull);
-            PROF_ADD(1);
-          }
+          got = mbar_wait(&full[stage], phase, kDevTimeoutTmaFull);
           if (!got) { ok = false; break; }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smem + stage * C::STAGE_BYTES);
@@ -655,9 +624,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1;
       }
-#ifdef OASIS_GEMM_PROF
-      atomicAdd(&g_gemm_prof[4], (unsigned long long)(clock64() - loop_t0));
-#endif
     }
   } else {
     // ---------------- Epilogue (warps 2..9) ----------------
@@ -1090,22 +1056,68 @@ int pair_mode() {
 struct Plan {
   int bn;
   int splits;
+  bool pair;  // 256 x 256 tiles on a CTA pair
 };
 
 Plan choose_plan(int M, int N, int K) {
   const int sms = num_sms();
   const int mt = (M + BM - 1) / BM;
   const int t256 = mt * ((N + 255) / 256);
-  if (t256 >= sms && N % 256 == 0) return {256, 1};
+  if (t256 >= sms && N % 256 == 0) return {256, 1, false};
   const int t128 = mt * ((N + 127) / 128);
-  if (t128 >= sms) return {128, 1};
+  if (t128 >= sms) return {128, 1, false};
   // Small problems (a handful of sessions): narrow tiles so most SMs stream a
   // slice of the weights. A long K over at most three row tiles (the B = 1 FC2,
   // M = 288, K = 4096) runs as 128-wide tiles x 4 K splits, one cluster per tile
   // (measured 17.2 -> 15.0 us); elsewhere at M = 288-576 split-K measured slower.
   if (mt <= 3 && K >= 4096 && N <= 1024 && (K / 128) % 4 == 0 && mt * ((N + 127) / 128) * 4 <= sms)
-    return {128, 4};
-  return {t128 >= sms / 2 ? 128 : 64, 1};
+    return {128, 4, false};
+  return {t128 >= sms / 2 ? 128 : 64, 1, false};
+}
+
+// The final tile plan of a problem: heuristic choice, the caller's overrides and
+// every rule the launch applies on top. gemm_launch dispatches on it and the
+// workspace queries size from it, so the two cannot disagree.
+int resolve_plan(const GemmProblem& p, Plan* out) {
+  Plan pl = choose_plan(p.M, p.N, p.K);
+  pl.pair = false;
+  // fp32-output epilogues (32-column chunks) can use 32-wide tiles: at a few
+  // hundred rows and N = 1024 that doubles the SMs streaming the weights.
+  if (pl.bn == 64 && !bf16_out(p.epi.mode) && p.epi.mode != kEpiImage &&
+      ((p.M + BM - 1) / BM) * ((p.N + 63) / 64) < num_sms() / 2)
+    pl.bn = 32;
+  if (p.block_n == 512) {  // explicit request: 256 x 256 tiles on a CTA pair
+    OASIS_REQUIRE(p.splits <= 1 && p.epi.mode != kEpiImage && p.epi.mode != kEpiGatedResidLN,
+                  "GEMM: CTA-pair tiles take no split-K, image or LN epilogue");
+    *out = Plan{256, 1, true};
+    return OASIS_OK;
+  }
+  if (p.block_n) pl.bn = p.block_n;
+  if (p.splits) pl.splits = p.splits;
+  if (pl.splits > 1 && !p.workspace) pl.splits = 1;
+  if (p.epi.mode == kEpiGatedResidLN) {  // whole rows per CTA, 4 tiles of 256
+    pl.bn = 256;
+    pl.splits = 1;
+  }
+  OASIS_REQUIRE(pl.bn != 32 || !bf16_out(p.epi.mode), "GEMM: block_n=32 needs an fp32 epilogue");
+  if (pl.bn <= 128 && p.K % (2 * BK)) pl.bn = 256;  // narrower tiles stage K in 128-wide steps
+  const int k_stages = p.K / (pl.bn <= 128 ? 2 * BK : BK);
+  OASIS_REQUIRE(pl.splits >= 1 && pl.splits <= 8, "GEMM: splits=%d outside [1, 8] (one cluster per tile)", pl.splits);
+  OASIS_REQUIRE(k_stages % pl.splits == 0, "GEMM: splits=%d must divide the %d K stages", pl.splits, k_stages);
+  // Large problems: 256 x 256 tiles on CTA pairs, when there are enough of them
+  // to fill the GPU (one pair per two SMs).
+  const int pm = pair_mode();
+  pl.pair = !p.block_n && pl.bn == 256 && pl.splits == 1 && pm != kPairOff && p.epi.mode != kEpiImage &&
+            p.epi.mode != kEpiGatedResidLN && (pm == kPairAll || reads_resid(p.epi.mode)) && p.N % 256 == 0 &&
+            ((p.M + 2 * BM - 1) / (2 * BM)) * (p.N / 256) >= num_sms() / 2;
+  *out = pl;
+  return OASIS_OK;
+}
+
+size_t plan_splitk_bytes(int M, int N, const Plan& pl) {
+  if (pl.pair || pl.splits <= 1) return 0;
+  const size_t tiles = (size_t)((M + BM - 1) / BM) * ((N + pl.bn - 1) / pl.bn);
+  return tiles * pl.splits * BM * pl.bn * sizeof(float);
 }
 
 }  // namespace
@@ -1121,33 +1133,38 @@ int num_sms() {
   return g_num_sms[dev & 63];
 }
 
-#ifdef OASIS_GEMM_PROF
-extern "C" int oasis_debug_gemm_prof(unsigned long long* out8, int reset) {
-  cudaMemcpyFromSymbol(out8, g_gemm_prof, sizeof(g_gemm_prof));
-  if (reset) {
-    unsigned long long z[8] = {0};
-    cudaMemcpyToSymbol(g_gemm_prof, z, sizeof(z));
-  }
-  return 0;
+int gemm_plan(int M, int N, int K, int mode, int block_n, int splits, int* bn, int* splits_out, int* pair,
+              size_t* splitk_bytes) {
+  OASIS_REQUIRE(M > 0 && N > 0 && K > 0 && K % BK == 0, "GEMM plan: bad shape %d x %d x %d", M, N, K);
+  GemmProblem p;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.epi.mode = mode;
+  p.block_n = block_n;
+  p.splits = splits;
+  p.workspace = reinterpret_cast<void*>(uintptr_t(256));  // "a workspace is given": split-K stays allowed
+  Plan pl;
+  OASIS_TRY(resolve_plan(p, &pl));
+  if (bn) *bn = pl.pair ? 512 : pl.bn;
+  if (splits_out) *splits_out = pl.splits;
+  if (pair) *pair = pl.pair ? 1 : 0;
+  if (splitk_bytes) *splitk_bytes = plan_splitk_bytes(M, N, pl);
+  return OASIS_OK;
 }
-#endif
 
 size_t gemm_workspace_bytes(int M, int N, int K) {
-  Plan pl = choose_plan(M, N, K);
-  if (pl.splits <= 1) return 0;
-  const size_t tiles = (size_t)((M + BM - 1) / BM) * ((N + pl.bn - 1) / pl.bn);
-  return tiles * pl.splits * BM * pl.bn * sizeof(float);
+  size_t b = 0;
+  if (M <= 0 || N <= 0 || K <= 0 || K % BK) return 0;
+  if (gemm_plan(M, N, K, kEpiF32, 0, 0, nullptr, nullptr, nullptr, &b) != OASIS_OK) return 0;
+  return b;
 }
 
-size_t gemm_splitk_bytes(int M, int N, int K, int block_n, int splits) {
-  if (M <= 0 || N <= 0 || K <= 0) return 0;
-  Plan pl = choose_plan(M, N, K);
-  if (block_n) pl.bn = block_n;
-  if (splits) pl.splits = splits;
-  if (pl.bn <= 128 && K % (2 * BK)) pl.bn = 256;  // as gemm_launch
-  if (pl.splits <= 1) return 0;
-  const size_t tiles = (size_t)((M + BM - 1) / BM) * ((N + pl.bn - 1) / pl.bn);
-  return tiles * pl.splits * BM * pl.bn * sizeof(float);
+size_t gemm_splitk_bytes(int M, int N, int K, int mode, int block_n, int splits) {
+  size_t b = 0;
+  if (M <= 0 || N <= 0 || K <= 0 || K % BK) return 0;
+  if (gemm_plan(M, N, K, mode, block_n, splits, nullptr, nullptr, nullptr, &b) != OASIS_OK) return 0;
+  return b;
 }
 
 int gemm_launch(const GemmProblem& p, cudaStream_t stream) {
@@ -1166,36 +1183,9 @@ int gemm_launch(const GemmProblem& p, cudaStream_t stream) {
     OASIS_REQUIRE(p.splits <= 1, "GEMM: the LN epilogue does not split K");
   }
   if (p.epi.mode == kEpiRopeBF16) OASIS_REQUIRE(p.epi.rope && p.epi.rope_mod > 0 && p.epi.rope_div > 0, "GEMM: rope table missing");
-  Plan pl = choose_plan(p.M, p.N, p.K);
-  // fp32-output epilogues (32-column chunks) can use 32-wide tiles: at a few
-  // hundred rows and N = 1024 that doubles the SMs streaming the weights.
-  if (pl.bn == 64 && !bf16_out(p.epi.mode) && p.epi.mode != kEpiImage &&
-      ((p.M + BM - 1) / BM) * ((p.N + 63) / 64) < num_sms() / 2)
-    pl.bn = 32;
-  if (p.block_n == 512) {  // explicit request: 256 x 256 tiles on a CTA pair
-    OASIS_REQUIRE(p.splits <= 1 && p.epi.mode != kEpiImage && p.epi.mode != kEpiGatedResidLN,
-                  "GEMM: CTA-pair tiles take no split-K, image or LN epilogue");
-    return launch_pair(p, stream);
-  }
-  if (p.block_n) pl.bn = p.block_n;
-  if (p.splits) pl.splits = p.splits;
-  if (pl.splits > 1 && !p.workspace) pl.splits = 1;
-  if (p.epi.mode == kEpiGatedResidLN) {  // whole rows per CTA, 4 tiles of 256
-    pl.bn = 256;
-    pl.splits = 1;
-  }
-  OASIS_REQUIRE(pl.bn != 32 || !bf16_out(p.epi.mode), "GEMM: block_n=32 needs an fp32 epilogue");
-  if (pl.bn <= 128 && p.K % (2 * BK)) pl.bn = 256;  // narrower tiles stage K in 128-wide steps
-  const int k_stages = p.K / (pl.bn <= 128 ? 2 * BK : BK);
-  OASIS_REQUIRE(pl.splits >= 1 && pl.splits <= 8, "GEMM: splits=%d outside [1, 8] (one cluster per tile)", pl.splits);
-  OASIS_REQUIRE(k_stages % pl.splits == 0, "GEMM: splits=%d must divide the %d K stages", pl.splits, k_stages);
-  // Large problems: 256 x 256 tiles on CTA pairs, when there are enough of them
-  // to fill the GPU (one pair per two SMs).
-  const int pm = pair_mode();
-  if (!p.block_n && pl.bn == 256 && pl.splits == 1 && pm != kPairOff && p.epi.mode != kEpiImage &&
-      p.epi.mode != kEpiGatedResidLN && (pm == kPairAll || reads_resid(p.epi.mode)) && p.N % 256 == 0 &&
-      ((p.M + 2 * BM - 1) / (2 * BM)) * (p.N / 256) >= num_sms() / 2)
-    return launch_pair(p, stream);
+  Plan pl;
+  OASIS_TRY(resolve_plan(p, &pl));
+  if (pl.pair) return launch_pair(p, stream);
   switch (pl.bn) {
     case 32: return launch_bn<32, false>(p, pl.splits, stream);
     case 64: return launch_bn<64, false>(p, pl.splits, stream);

@@ -71,8 +71,15 @@ int gemm_launch(const GemmProblem& p, cudaStream_t stream);
 // Bytes of split-K workspace the heuristic may want for an M x N x K problem.
 size_t gemm_workspace_bytes(int M, int N, int K);
 
-// Split-K workspace bytes a launch with these overrides (0 = heuristic) needs.
-size_t gemm_splitk_bytes(int M, int N, int K, int block_n, int splits);
+// Split-K workspace bytes a launch with this epilogue mode and these overrides
+// (0 = heuristic) needs, given that a workspace is passed.
+size_t gemm_splitk_bytes(int M, int N, int K, int mode, int block_n, int splits);
+
+// The tile plan gemm_launch uses for such a launch (with a workspace): tile width
+// (512 = 256 x 256 tiles on a CTA pair), K splits, pair flag and split-K bytes.
+// Returns 0 or a negative status for overrides the launch would reject.
+int gemm_plan(int M, int N, int K, int mode, int block_n, int splits, int* bn, int* splits_out, int* pair,
+              size_t* splitk_bytes);
 
 int num_sms();
 

@@ -19,7 +19,9 @@
 //    split overwrites its own before the cluster barrier).
 //  * the first call on each device looks the array's device address up (with
 //    that device current) and caches it; make that first call before any stream
-//    capture.
+//    capture. The cache assumes one primary context per device for the life of
+//    the process: after cudaDeviceReset the address may change, so do not call
+//    this entry point again in that process.
 #include <mutex>
 
 #include "../../include/oasis_b200.h"
@@ -63,7 +65,7 @@ extern "C" size_t oasis_gemm_static_scratch_capacity(void) { return oasis::kStat
 
 extern "C" int oasis_gemm_static_scratch(const OasisGemmArgs* a, oasis_stream_t stream) {
   OASIS_REQUIRE(a, "gemm_static_scratch: null args");
-  const size_t need = oasis::gemm_splitk_bytes(a->m, a->n, a->k, a->block_n, a->splits);
+  const size_t need = oasis::gemm_splitk_bytes(a->m, a->n, a->k, a->mode, a->block_n, a->splits);
   if (need > oasis::kStaticScratchBytes)
     return oasis::set_error(OASIS_ERR_WORKSPACE,
                             "gemm_static_scratch: %d x %d x %d needs %zu bytes of split-K scratch, more than the "

@@ -64,6 +64,15 @@ def sum_over_ranks(value: float) -> float:
     return _reduce(value, dist.ReduceOp.SUM)
 
 
+def gather_objects(obj) -> list:
+    """obj of every rank, in rank order (a one-element list without a process group)."""
+    if not dist.is_initialized():
+        return [obj]
+    out = [None] * dist.get_world_size()
+    dist.all_gather_object(out, obj)
+    return out
+
+
 def barrier() -> None:
     if dist.is_initialized():
         dist.barrier()

@@ -1,11 +1,11 @@
 """Small, self-contained launch cases for ncu captures of single kernels.
 
-    python open-oasis_b200/profile_cases.py gemm --m 16384 --n 4096 --k 1024 --mode 2 [--reps 3]
-    python open-oasis_b200/profile_cases.py attn_spatial --groups 512
-    python open-oasis_b200/profile_cases.py attn_temporal --batch 64 --frames 8
-    python open-oasis_b200/profile_cases.py layernorm --rows 73728
-    python open-oasis_b200/profile_cases.py attn_temporal_cached --batch 64 --frames 8
-    python open-oasis_b200/profile_cases.py frame --batch 64 --frames 8 [--kv] --reps 1
+    python profile_cases.py gemm --m 16384 --n 4096 --k 1024 --mode 2 [--reps 3]
+    python profile_cases.py attn_spatial --groups 512
+    python profile_cases.py attn_temporal --batch 64 --frames 8
+    python profile_cases.py layernorm --rows 73728
+    python profile_cases.py attn_temporal_cached --batch 64 --frames 8
+    python profile_cases.py frame --batch 64 --frames 8 [--kv] --reps 1
 
 Each case allocates only what the one kernel needs (a few GB at most), runs it
 `reps` times and exits, so an ncu capture with -k/-c ends by itself quickly.
@@ -19,7 +19,7 @@ import sys
 
 import torch
 
-ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 import __graft_entry__  # noqa: E402
 

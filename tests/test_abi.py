@@ -173,3 +173,37 @@ def test_frame_count_bounds():
         d = _lib.OasisDitArgs(1, T, 16, 16, 16, 1, 16, 1 << 40)
         assert lib.oasis_dit_forward(C.byref(w), C.byref(d), None) == -1
         assert b"frames" in lib.oasis_last_error() or b"T=" in lib.oasis_last_error(), lib.oasis_last_error()
+
+
+def _plan(lib, m, n, k, mode=0, block_n=0, splits=0):
+    bn, sp, pair, by = C.c_int(), C.c_int(), C.c_int(), C.c_size_t()
+    rc = lib.oasis_gemm_plan(m, n, k, mode, block_n, splits, C.byref(bn), C.byref(sp), C.byref(pair), C.byref(by))
+    return rc, bn.value, sp.value, pair.value, by.value
+
+
+def test_gemm_plan_and_workspace_queries_agree():
+    """oasis_gemm_plan is the launch's own planning rule; the workspace queries
+    (the caller-workspace one and the fixed-scratch entry point's size check)
+    size from the same plan."""
+    lib = _lib.load()
+    # bench shapes (M = 73728): every DiT projection on CTA pairs, no split-K
+    for n, k, mode in ((3072, 1024, 6), (1024, 1024, 4), (4096, 1024, 2), (1024, 4096, 4)):
+        rc, bn, sp, pair, by = _plan(lib, 73728, n, k, mode)
+        assert (rc, bn, sp, pair, by) == (0, 512, 1, 1, 0), (n, k, mode)
+    # B = 1 FC2 (M = 288, K = 4096): 128-wide tiles x 4 K splits in clusters
+    rc, bn, sp, pair, by = _plan(lib, 288, 1024, 4096, 4)
+    assert (rc, bn, sp, pair) == (0, 128, 4, 0)
+    assert by == 3 * 8 * 4 * 128 * 128 * 4
+    assert lib.oasis_gemm_workspace_size(288, 1024, 4096) == by
+    # B = 1 O projection: fp32 epilogue narrows to 32-wide tiles, no split
+    rc, bn, sp, pair, by = _plan(lib, 288, 1024, 1024, 4)
+    assert (rc, bn, sp, by) == (0, 32, 1, 0)
+    # explicit overrides are what the launch uses
+    rc, bn, sp, pair, by = _plan(lib, 300, 1024, 4096, 4, block_n=64, splits=4)
+    assert (rc, bn, sp) == (0, 64, 4) and by == 3 * 16 * 4 * 128 * 64 * 4
+    rc, bn, sp, pair, by = _plan(lib, 4096, 4096, 4096, 0, block_n=64, splits=8)
+    assert by == 32 * 64 * 8 * 128 * 64 * 4 and by > lib.oasis_gemm_static_scratch_capacity()
+    # rejected overrides: bf16 output on 32-wide tiles, splits that do not divide K
+    assert _plan(lib, 288, 1024, 1024, 1, block_n=32)[0] == -1
+    assert _plan(lib, 288, 1024, 1024, 0, block_n=64, splits=3)[0] == -1
+    assert _plan(lib, 288, 1024, 1000, 0)[0] == -1

@@ -96,7 +96,10 @@ def _frame_inputs(sd, B, T, seed):
 
 
 def test_frame_c3(dit_full, vae_full):
-    """C3: one frame, B=1, T=2: 4 DDIM steps (v checked at every step) + VAE decode."""
+    """C3: one frame, B=1, T=2: 4 DDIM steps + VAE decode. Each step's
+    v-prediction (the DiT forward on the step's own input) meets rel-L2 <= 1e-2
+    and cosine >= 0.999 against the oracle's; the step itself goes through
+    oasis_ddim_step and must equal ddim_update(chunk, that v)."""
     dsd, dw = dit_full
     vsd, vw = vae_full
     B, T = 1, 2
@@ -108,10 +111,20 @@ def test_frame_c3(dit_full, vae_full):
         fe.cond[i].copy_(c)
     c_ref = chunk.clone()
     step_ws = E.workspace(E.step_workspace_bytes(B, T), DEV)
+    dit_ws = E.workspace(E.dit_workspace_bytes(B, T), DEV)
+    z = torch.empty(B, T, H.N_PATCHES, H.D_MODEL, device=DEV)
+    v = torch.empty(B, H.N_PATCHES, H.OUT_DIM, device=DEV)
     for i, st in enumerate(steps):
         c_ref, v_ref = O.ddim_step(c_ref, ctx_z, conds[i], st.at_sqrt ** 2, st.an_sqrt ** 2, dsd)
+        z[:, :T - 1].copy_(fe.context_z)
+        E.patch_embed(dw, fe.chunk.reshape(-1, H.OUT_DIM), z, T * H.N_PATCHES, (T - 1) * H.N_PATCHES)
+        E.dit_forward(dw, z, fe.cond[i], v, dit_ws, last_frame_only=True)
+        expect = fe.chunk.clone()
+        E.ddim_update(expect, v, st)
         E.ddim_step(dw, fe.chunk, fe.context_z, fe.cond[i], st, step_ws)
         torch.cuda.synchronize()
+        assert rel_l2(v, v_ref) < REL_L2_TOL and cosine(v, v_ref) > COS_TOL, (i, rel_l2(v, v_ref), cosine(v, v_ref))
+        assert rel_l2(fe.chunk, expect) < 1e-5, (i, rel_l2(fe.chunk, expect))
         assert rel_l2(fe.chunk, c_ref) < REL_L2_TOL, (i, rel_l2(fe.chunk, c_ref))
     img_ref = O.vae_decode(O.bridge(c_ref), vsd)
     fe.run_decode()
