@@ -40,10 +40,11 @@ FRAMES_T = 8
 METRIC = "frames_per_sec (4 DDIM steps + VAE decode per frame, 64 sessions)"
 UNIT = "frames/s"
 # DRAM traffic (read + write during the launch) of one FC1 gemm_pair_kernel launch
-# at the bench shape (M=73728, N=4096, K=1024): an ncu capture of the same launch
-# at M=16384 (42.05 MB read, 78.88 MB written) scaled by rows
-# for the M-proportional parts (A, output); W (8.4 MB) is read once either way.
-GEMM_TRAFFIC_BYTES_PER_LAUNCH = int((42.05e6 - 8.39e6) * 4.5 + 8.39e6 + 78.88e6 * 4.5)
+# at the bench shape (M=73728, N=4096, K=1024), from one ncu capture of that launch
+# (profiles/gemm_pair_kernel_fc1_bench_shape.md): 159.5 MB read (A 151.0 MB + W
+# 8.4 MB, each read once) + 549.4 MB written (of the 604.0 MB bf16 output; the
+# rest is still dirty in L2 when the launch ends).
+GEMM_TRAFFIC_BYTES_PER_LAUNCH = 159524608 + 549399808
 
 
 def parse():

@@ -134,6 +134,16 @@ typedef struct OasisVaeEncoderWeights {
   const float* rope;                        /* [16, 576, 4], as OasisVaeWeights.rope */
 } OasisVaeEncoderWeights;
 
+/* Conditioning weights (t_embedder and external_cond of the DiT checkpoint), fp32,
+ * nn.Linear [out, in] layout. Replaces the host copies compute_cond_for_frame
+ * reads (dev["t_emb_w0_host"] etc., oasis_inference.py:1406-1427). */
+typedef struct OasisCondWeights {
+  const float* t_freqs;             /* [128] exp(-ln(10000) i / 128), the timestep embedding frequencies */
+  const float* t_w0; const float* t_b0; /* [1024, 256], [1024] t_embedder.mlp.0 */
+  const float* t_w2; const float* t_b2; /* [1024, 1024], [1024] t_embedder.mlp.2 */
+  const float* ext_w; const float* ext_b; /* [1024, 25], [1024] external_cond (may be NULL without actions) */
+} OasisCondWeights;
+
 /* ---------------------------------------------------------- composite ---- */
 
 /* DiT forward over B sessions x T frames (T <= 32).
@@ -257,6 +267,19 @@ typedef struct OasisFrameArgs {
 size_t oasis_frame_workspace_size(int batch, int frames, int steps);
 int oasis_generate_frame(const OasisDitWeights* w, const OasisVaeWeights* vw, const OasisFrameArgs* a,
                          oasis_stream_t stream);
+
+/* Frame conditioning on the GPU, fp32 (compute_cond_for_frame,
+ * oasis_inference.py:1406-1427, which the reference runs on the host):
+ *   cond[r] = t_mlp([cos(t f) | sin(t f)], t = levels[r])
+ *             + (actions ? actions[r % action_rows] . ext_w^T + ext_b : 0)
+ *   levels  [n] fp32 noise levels (integers as floats), device
+ *   actions [action_rows, 25] fp32 or NULL; row r uses actions[r % action_rows],
+ *           so a [B, T, 25] action window serves rows laid out [S][B][T]
+ *   cond    [n, 1024] fp32
+ * Workspace: oasis_cond_workspace_size(n) bytes (the hidden layer). */
+size_t oasis_cond_workspace_size(int n);
+int oasis_compute_cond(const OasisCondWeights* w, const float* levels, int n, const float* actions, int action_rows,
+                       float* cond, void* workspace, size_t workspace_bytes, oasis_stream_t stream);
 
 /* ---------------------------------------------------- context caching --- */
 /* The context frames attend only to earlier frames (causal temporal attention)

@@ -51,6 +51,11 @@ class OasisDitWeights(C.Structure):
                 ("embed_w", fp), ("embed_b", fp), ("rope_spatial", fp), ("rope_temporal", fp)]
 
 
+class OasisCondWeights(C.Structure):
+    _fields_ = [("t_freqs", fp), ("t_w0", fp), ("t_b0", fp), ("t_w2", fp), ("t_b2", fp), ("ext_w", fp),
+                ("ext_b", fp)]
+
+
 class OasisVaeBlock(C.Structure):
     _fields_ = [("norm1_w", fp), ("norm1_b", fp), ("qkv_w", vp), ("qkv_b", fp), ("proj_w", vp),
                 ("proj_b", fp), ("norm2_w", fp), ("norm2_b", fp), ("fc1_w", vp), ("fc1_b", fp),
@@ -150,6 +155,8 @@ SIGNATURES = {
                                        C.POINTER(OasisFrameArgs), vp]),
     "oasis_tp_workspace_size": (C.c_size_t, [C.c_int, C.c_int, C.c_int]),
     "oasis_dit_forward_tp": (C.c_int, [C.POINTER(OasisDitWeights), C.POINTER(OasisTpArgs), vp]),
+    "oasis_cond_workspace_size": (C.c_size_t, [C.c_int]),
+    "oasis_compute_cond": (C.c_int, [C.POINTER(OasisCondWeights), fp, C.c_int, fp, C.c_int, fp, vp, C.c_size_t, vp]),
     "oasis_kv_cache_size": (C.c_size_t, [C.c_int, C.c_int]),
     "oasis_dit_precompute_past": (C.c_int, [C.POINTER(OasisDitWeights), C.POINTER(OasisDitArgs), vp, C.c_size_t, vp]),
     "oasis_dit_forward_current": (C.c_int, [C.POINTER(OasisDitWeights), C.POINTER(OasisDitArgs), vp, C.c_size_t,

@@ -54,10 +54,15 @@ STABILIZATION_LEVEL = 15  # context frames are conditioned at t = 14
 
 
 # --- conditioning -----------------------------------------------------------
+def timestep_freqs(dim: int = FREQ_DIM, max_period: float = 10000.0) -> torch.Tensor:
+    """The embedding's frequencies exp(-ln(max_period) i / (dim/2)), i < dim/2 (fp32)."""
+    half = dim // 2
+    return torch.exp(-math.log(max_period) * torch.arange(0, half, dtype=torch.float32) / half)
+
+
 def timestep_embedding(t: torch.Tensor, dim: int = FREQ_DIM, max_period: float = 10000.0) -> torch.Tensor:
     """[cos | sin] sinusoidal embedding, freqs exp(-ln(max_period) i / (dim/2))."""
-    half = dim // 2
-    freqs = torch.exp(-math.log(max_period) * torch.arange(0, half, dtype=torch.float32) / half)
+    freqs = timestep_freqs(dim, max_period)
     args = t[:, None].float() * freqs[None]
     return torch.cat([torch.cos(args), torch.sin(args)], dim=-1)
 

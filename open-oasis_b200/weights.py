@@ -194,6 +194,16 @@ class DitDeviceWeights:
         self.host = {k: sd[k].float() for k in ("t_embedder.mlp.0.weight", "t_embedder.mlp.0.bias",
                                                  "t_embedder.mlp.2.weight", "t_embedder.mlp.2.bias",
                                                  "external_cond.weight", "external_cond.bias")}
+        # the same weights on the device for oasis_compute_cond (conditioning inside the frame graph)
+        self.cond_tensors = {
+            "t_freqs": f32(H.timestep_freqs()),
+            "t_w0": f32(sd["t_embedder.mlp.0.weight"]), "t_b0": f32(sd["t_embedder.mlp.0.bias"]),
+            "t_w2": f32(sd["t_embedder.mlp.2.weight"]), "t_b2": f32(sd["t_embedder.mlp.2.bias"]),
+            "ext_w": f32(sd["external_cond.weight"]), "ext_b": f32(sd["external_cond.bias"])}
+        cw = _lib.OasisCondWeights()
+        for k, t in self.cond_tensors.items():
+            setattr(cw, k, t.data_ptr())
+        self.cond_struct = cw
         self.conv_w = sd["x_embedder.proj.weight"].float()
         self.conv_b = sd["x_embedder.proj.bias"].float()
 
