@@ -213,7 +213,8 @@ def run_reference(args, rank, world):
 # --------------------------------------------------------------------------- GPU arm
 def make_inputs(fe, dw, sess0, B, T):
     """Seeded per-session inputs (session seeds sess0..sess0+B-1): noise chunk,
-    embedded context frames, conditioning for each DDIM step."""
+    embedded context frames, conditioning for each DDIM step (host fp32, as the
+    reference computes it) and the action window [B, T, 25] it comes from."""
     from oasis_b200 import engine as E
     from oasis_b200 import host as H
 
@@ -236,9 +237,11 @@ def make_inputs(fe, dw, sess0, B, T):
         c_gen = H.compute_cond(torch.full((B,), st.noise_level), acts[:, -1], dw.host).reshape(B, 1, -1)
         conds[i] = torch.cat([c_ctx, c_gen], 1)
     fe.cond.copy_(conds)
+    if getattr(fe, "device_cond", False):  # the frame computes `cond` itself from the action window
+        fe.actions.copy_(acts)
     fe.chunk.copy_(chunk)
     torch.cuda.synchronize()
-    return chunk, fe.context_z.cpu(), conds
+    return chunk, fe.context_z.cpu(), conds, acts
 
 
 def time_graph(fn, k):
@@ -303,7 +306,7 @@ def latency_extras(dw, vw, peaks):
     """C3 (one session, T=2: 4 DDIM steps + VAE) and C2 (one DiT step, B=1, T=2)."""
     from oasis_b200 import engine as E
 
-    fe = E.FrameEngine(dw, vw, 1, 2)
+    fe = E.FrameEngine(dw, vw, 1, 2, device_cond=True)
     make_inputs(fe, dw, 0, 1, 2)
     fe.capture()
     for _ in range(3):
@@ -318,7 +321,7 @@ def latency_extras(dw, vw, peaks):
     dit_bytes += dw.adaln_w.numel() * 2 + dw.final_w.numel() * 2
     ms_step = ms_steps / 4
     del fe
-    fk = E.FrameEngine(dw, vw, 1, 2, kv=True)
+    fk = E.FrameEngine(dw, vw, 1, 2, kv=True, device_cond=True)
     make_inputs(fk, dw, 0, 1, 2)
     fk.capture()
     for _ in range(3):
@@ -340,8 +343,8 @@ def kv_frame(dw, vw, sess0, B, T, steps, PAR, sessions):
     FLOP count, reported beside the full-T number, never mixed into it."""
     from oasis_b200 import engine as E
 
-    fe = E.FrameEngine(dw, vw, B, T, kv=True)
-    make_inputs(fe, dw, sess0, B, T)
+    fe = E.FrameEngine(dw, vw, B, T, kv=True, device_cond=True)
+    _, _, _, acts = make_inputs(fe, dw, sess0, B, T)
     fe.capture()
     for _ in range(3):
         fe.replay()
@@ -357,16 +360,16 @@ def kv_frame(dw, vw, sess0, B, T, steps, PAR, sessions):
            "path": "oasis_generate_frame_kv: context rows once per frame, generated frame per DDIM step"}
     # the autoregressive loop: the same frames plus the on-device context roll
     # (patch embed of the generated latent into the window), one graph per frame
-    ve = E.VideoEngine(dw, vw, B, T, kv=True)
+    ve = E.VideoEngine(dw, vw, B, T, kv=True, device_cond=True)
     ve.capture()
-    ve.set_context(fe.context_z, fe.cond[0, :, :T - 1])
-    noise, gen, new_ctx = fe.chunk.clone(), fe.cond[:, :, T - 1].clone(), fe.cond[0, :, 0].clone()
+    ve.set_context(fe.context_z, acts[:, :T - 1].to(dw.device))
+    noise, act = fe.chunk.clone(), acts[:, T - 1].to(dw.device)
     del fe
     for _ in range(2):
-        ve.step(noise, gen, new_ctx)
+        ve.step_actions(noise, act)
     torch.cuda.synchronize()
     PAR.barrier()
-    ms_v = PAR.max_over_ranks(time_graph(lambda: ve.step(noise, gen, new_ctx), steps))
+    ms_v = PAR.max_over_ranks(time_graph(lambda: ve.step_actions(noise, act), steps))
     out["video_loop_frames_per_sec"] = round(sessions * steps / (ms_v / 1000.0), 3)
     del ve
     torch.cuda.empty_cache()
@@ -460,8 +463,8 @@ def main():
     peaks = measured_peaks()
     dw = DitDeviceWeights(init_dit_weights(seed=0), dev)
     vw = VaeDeviceWeights(init_vae_weights(seed=0), dev)
-    fe = E.FrameEngine(dw, vw, B, T)
-    chunk0, ctx0, conds0 = make_inputs(fe, dw, sess0, B, T)
+    fe = E.FrameEngine(dw, vw, B, T, device_cond=True)
+    chunk0, ctx0, conds0, acts0 = make_inputs(fe, dw, sess0, B, T)
     n0 = _lib.load().oasis_launch_count()
     fe.capture()
     launches_per_frame = (_lib.load().oasis_launch_count() - n0) // 2  # eager frame + captured frame
@@ -492,18 +495,21 @@ def main():
     ms_steps = time_graph(fe.graph_steps.replay, 3) / 3
     ms_dec = time_graph(fe.graph_decode.replay, 3) / 3
 
-    # e2e through the public API with host buffers
-    pin = {"chunk": chunk0.pin_memory(), "ctx": ctx0.pin_memory(), "cond": conds0.pin_memory()}
-    img_host = torch.empty(fe.image.shape, dtype=torch.float32).pin_memory()
+    # e2e through the public API with host buffers: the video loop (VideoEngine,
+    # the same frame plus the on-device context roll, conditioning computed in
+    # the graph), fed each frame's noise chunk and actions from pinned host memory
+    # and reading each decoded frame back to pinned host memory
+    ve = E.VideoEngine(dw, vw, B, T, device_cond=True)
+    ve.capture()
+    ve.set_context(fe.context_z, acts0[:, :T - 1].to(dev))
+    pin = {"noise": chunk0.pin_memory(), "action": acts0[:, T - 1].contiguous().pin_memory()}
+    img_host = torch.empty(ve.image.shape, dtype=torch.float32).pin_memory()
     h2d = sum(v.numel() * v.element_size() for v in pin.values())
     d2h = img_host.numel() * 4
 
     def e2e_frame():
-        fe.chunk.copy_(pin["chunk"], non_blocking=True)
-        fe.context_z.copy_(pin["ctx"], non_blocking=True)
-        fe.cond.copy_(pin["cond"], non_blocking=True)
-        fe.replay()
-        img_host.copy_(fe.image, non_blocking=True)
+        ve.step_actions(pin["noise"], pin["action"])
+        img_host.copy_(ve.image, non_blocking=True)
 
     for _ in range(2):
         e2e_frame()
@@ -514,6 +520,8 @@ def main():
     ev[2].record()
     barrier()
     e2e_value = args.sessions * args.steps / (PAR.max_over_ranks(ev[0].elapsed_time(ev[2])) / 1000.0)
+    del ve
+    torch.cuda.empty_cache()
 
     roof = gemm_roofline(B * T * 144, 10, peaks)
     kv = kv_frame(dw, vw, sess0, B, T, args.steps, PAR, args.sessions)
@@ -539,7 +547,9 @@ def main():
             "ms_per_dit_step": round(ms_steps / 4, 3), "ms_vae_decode": round(ms_dec, 3),
             "dit_tflops_achieved": round(dit_flops / (ms_steps / 1000) / 1e12, 1),
             "clocks": clk,
-            "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "path": "VideoEngine.step_actions: pinned noise + actions in, conditioning + frame + context "
+                            "roll in one CUDA graph, decoded frames out to pinned host memory"},
             "gpu_launches": int(launches_per_frame * args.steps),
             "roofline": roof, "cpu_baseline": cpu, "kv_cache": kv, **extras, "c5_tp_vs_dp": c5,
         }

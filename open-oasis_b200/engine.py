@@ -15,7 +15,7 @@ import torch
 
 from . import _lib
 from . import host as H
-from .weights import DitDeviceWeights, VaeDeviceWeights, VaeEncoderDeviceWeights
+from .weights import CondDeviceWeights, DitDeviceWeights, VaeDeviceWeights, VaeEncoderDeviceWeights
 
 
 def _stream(stream=None) -> int:
@@ -205,6 +205,33 @@ def frame_kv_workspace_bytes(batch: int, frames: int, steps: int) -> int:
     return int(_lib.load().oasis_frame_kv_workspace_size(batch, frames, steps))
 
 
+def cond_workspace_bytes(rows: int) -> int:
+    return int(_lib.load().oasis_cond_workspace_size(rows))
+
+
+def compute_cond(dw: DitDeviceWeights | CondDeviceWeights, levels: torch.Tensor, cond: torch.Tensor, ws: torch.Tensor,
+                 actions: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """Frame conditioning on the GPU (compute_cond_for_frame, oasis_inference.py:1406-1427):
+    cond[r] = t_mlp(timestep_embedding(levels[r])) + external_cond(actions[r % A]).
+    levels: fp32 [n] (any shape, flattened); cond: fp32 [n, 1024] (any shape with
+    n * 1024 elements); actions: fp32 [..., 25] with A rows, or None (no action term)."""
+    _check_cuda(levels, "levels")
+    _check_cuda(cond, "cond")
+    n = levels.numel()
+    if cond.numel() != n * H.D_MODEL:
+        raise ValueError(f"cond must hold {n} x {H.D_MODEL} values")
+    a_rows = 0
+    if actions is not None:
+        _check_cuda(actions, "actions")
+        if actions.shape[-1] != H.EXT_COND_DIM:
+            raise ValueError(f"actions must end in {H.EXT_COND_DIM}")
+        a_rows = actions.numel() // H.EXT_COND_DIM
+    cw = dw.cond if isinstance(dw, DitDeviceWeights) else dw
+    _lib.call("oasis_compute_cond", cw.ref(), levels.data_ptr(), n, _lib.ptr(actions), a_rows,
+              cond.data_ptr(), ws.data_ptr(), ws.numel(), _stream(stream))
+    return cond
+
+
 def generate_frame(dw: DitDeviceWeights, vw: VaeDeviceWeights | None, chunk: torch.Tensor,
                    context_z: torch.Tensor | None, cond: torch.Tensor, steps: list[H.DdimStep],
                    image: torch.Tensor | None, ws: torch.Tensor, skip_decode: bool = False, stream=None,
@@ -237,10 +264,15 @@ class FrameEngine:
     context windows (kv=True: context rows run once per frame). `run()` issues the whole frame through oasis_generate_frame
     (4 DDIM steps with all adaLN tables from one GEMM, bridge, VAE decode);
     `capture()` records it (and, for timing breakdowns, the steps alone and the
-    decode alone) as CUDA graphs."""
+    decode alone) as CUDA graphs.
+
+    device_cond=True computes `cond` inside the frame (and its graph) from the
+    per-frame action window `actions` [B, T, 25]: context frames at the
+    stabilisation level, the generated frame at each step's noise level
+    (oasis_compute_cond); otherwise the caller fills `cond`."""
 
     def __init__(self, dw: DitDeviceWeights, vw: VaeDeviceWeights, batch: int, frames: int,
-                 steps: list[H.DdimStep] | None = None, kv: bool = False):
+                 steps: list[H.DdimStep] | None = None, kv: bool = False, device_cond: bool = False):
         self.dw, self.vw, self.kv = dw, vw, kv
         self.B, self.T = batch, frames
         self.steps = steps if steps is not None else H.ddim_schedule()
@@ -253,6 +285,15 @@ class FrameEngine:
         self.image = torch.zeros(B, 3, H.VAE_H * H.VAE_PATCH, H.VAE_W * H.VAE_PATCH, device=dev)
         nbytes = (frame_kv_workspace_bytes if kv else frame_workspace_bytes)(B, T, len(self.steps))
         self.frame_ws = workspace(nbytes, dev)
+        self.device_cond = device_cond
+        if device_cond:
+            S = len(self.steps)
+            lv = torch.full((S, B, T), float(H.STABILIZATION_LEVEL - 1))
+            for i, st in enumerate(self.steps):
+                lv[i, :, T - 1] = float(st.noise_level)
+            self.levels = lv.to(dev)
+            self.actions = torch.zeros(B, T, H.EXT_COND_DIM, device=dev)
+            self.cond_ws = workspace(cond_workspace_bytes(S * B * T), dev)
         self.step_ws = None
         self.vae_ws = None
         self.graph = None
@@ -260,11 +301,17 @@ class FrameEngine:
     def _ctx(self):
         return self.context_z if self.T > 1 else None
 
+    def run_cond(self, stream=None):
+        if self.device_cond:
+            compute_cond(self.dw, self.levels, self.cond, self.cond_ws, self.actions, stream)
+
     def run(self, stream=None):
+        self.run_cond(stream)
         generate_frame(self.dw, self.vw, self.chunk, self._ctx(), self.cond, self.steps, self.image, self.frame_ws,
                        stream=stream, kv=self.kv)
 
     def run_steps(self, stream=None):
+        self.run_cond(stream)
         generate_frame(self.dw, None, self.chunk, self._ctx(), self.cond, self.steps, None, self.frame_ws,
                        skip_decode=True, stream=stream, kv=self.kv)
 
@@ -278,6 +325,7 @@ class FrameEngine:
         """The same steps through oasis_ddim_step (adaLN per step)."""
         if self.step_ws is None:
             self.step_ws = workspace(step_workspace_bytes(self.B, self.T), self.dw.device)
+        self.run_cond(stream)
         for i, st in enumerate(self.steps):
             ddim_step(self.dw, self.chunk, self._ctx(), self.cond[i], st, self.step_ws, stream)
 
@@ -322,18 +370,21 @@ class VideoEngine:
     (stabilisation level, same action) for when it joins the window."""
 
     def __init__(self, dw: DitDeviceWeights, vw: VaeDeviceWeights, batch: int, frames: int,
-                 steps: list[H.DdimStep] | None = None, kv: bool = False):
+                 steps: list[H.DdimStep] | None = None, kv: bool = False, device_cond: bool = False):
         if frames < 2:
             raise ValueError("the video loop needs a context window (frames >= 2)")
-        self.fe = FrameEngine(dw, vw, batch, frames, steps, kv=kv)
+        self.fe = FrameEngine(dw, vw, batch, frames, steps, kv=kv, device_cond=device_cond)
         self.dw, self.B, self.T = dw, batch, frames
+        self.device_cond = device_cond
         dev = dw.device
         S = len(self.fe.steps)
         self.ctx_cond = torch.zeros(batch, frames - 1, H.D_MODEL, device=dev)
         self.gen_cond = torch.zeros(S, batch, H.D_MODEL, device=dev)      # staging, per frame
         self.new_ctx_cond = torch.zeros(batch, H.D_MODEL, device=dev)    # staging, per frame
+        self.new_action = torch.zeros(batch, H.EXT_COND_DIM, device=dev)  # staging, per frame (device_cond)
         self._tmp_z = torch.empty(batch, max(frames - 2, 1), H.N_PATCHES, H.D_MODEL, device=dev)
         self._tmp_c = torch.empty(batch, max(frames - 2, 1), H.D_MODEL, device=dev)
+        self._tmp_a = torch.empty(batch, max(frames - 2, 1), H.EXT_COND_DIM, device=dev)
         self.graph = None
 
     @property
@@ -344,9 +395,19 @@ class VideoEngine:
     def image(self) -> torch.Tensor:
         return self.fe.image
 
+    @property
+    def ctx_actions(self) -> torch.Tensor:
+        """device_cond: the context frames' actions [B, T-1, 25] (a view)."""
+        return self.fe.actions[:, :self.T - 1]
+
     def set_context(self, context_z: torch.Tensor, ctx_cond: torch.Tensor):
+        """context_z [B, T-1, 144, 1024]; ctx_cond: the context conditioning
+        [B, T-1, 1024], or with device_cond the context frames' actions [B, T-1, 25]."""
         self.fe.context_z.copy_(context_z)
-        self.ctx_cond.copy_(ctx_cond)
+        if self.device_cond:
+            self.ctx_actions.copy_(ctx_cond)
+        else:
+            self.ctx_cond.copy_(ctx_cond)
 
     def set_prompt(self, ew: VaeEncoderDeviceWeights, image: torch.Tensor, prompt_cond: torch.Tensor,
                    ws: torch.Tensor | None = None):
@@ -367,10 +428,15 @@ class VideoEngine:
         for slot in range(T - 1):
             patch_embed(self.dw, chunk.view(-1, H.OUT_DIM), self.fe.context_z, (T - 1) * H.N_PATCHES,
                         slot * H.N_PATCHES)
-        self.ctx_cond.copy_(prompt_cond.to(dev).unsqueeze(1).expand(-1, T - 1, -1))
+        if self.device_cond:
+            self.ctx_actions.zero_()  # the prompt frames carry no action (oasis_inference.py:1801)
+        else:
+            self.ctx_cond.copy_(prompt_cond.to(dev).unsqueeze(1).expand(-1, T - 1, -1))
         return chunk
 
     def _frame_and_roll(self, stream=None):
+        if self.device_cond:
+            return self._frame_and_roll_device_cond(stream)
         fe, T = self.fe, self.T
         fe.cond[:, :, :T - 1].copy_(self.ctx_cond.unsqueeze(0).expand(fe.cond.shape[0], -1, -1, -1))
         fe.cond[:, :, T - 1].copy_(self.gen_cond)
@@ -385,9 +451,42 @@ class VideoEngine:
                     (T - 2) * H.N_PATCHES, stream)
         self.ctx_cond[:, -1].copy_(self.new_ctx_cond)
 
+    def _frame_and_roll_device_cond(self, stream=None):
+        """The frame with its conditioning computed on the GPU from the action
+        window: context frames at the stabilisation level with their own actions,
+        the generated frame at each step's noise level with the new action; the
+        new action then joins the window with the frame."""
+        fe, T = self.fe, self.T
+        fe.actions[:, T - 1].copy_(self.new_action)
+        fe.run(stream)
+        if T > 2:
+            self._tmp_z.copy_(fe.context_z[:, 1:])
+            fe.context_z[:, :-1].copy_(self._tmp_z)
+            self._tmp_a.copy_(fe.actions[:, 1:T - 1])
+            fe.actions[:, :T - 2].copy_(self._tmp_a)
+        patch_embed(self.dw, fe.chunk.view(-1, H.OUT_DIM), fe.context_z, (T - 1) * H.N_PATCHES,
+                    (T - 2) * H.N_PATCHES, stream)
+        fe.actions[:, T - 2].copy_(self.new_action)
+
+    def step_actions(self, noise: torch.Tensor, action: torch.Tensor) -> torch.Tensor:
+        """device_cond: one frame from its noise chunk [B, 144, 64] and action
+        [B, 25] (host or device tensors); returns the decoded image buffer
+        [B, 3, 360, 640] (overwritten by the next step)."""
+        if not self.device_cond:
+            raise RuntimeError("step_actions needs VideoEngine(..., device_cond=True)")
+        self.fe.chunk.copy_(noise, non_blocking=True)
+        self.new_action.copy_(action, non_blocking=True)
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self._frame_and_roll()
+        return self.fe.image
+
     def step(self, noise: torch.Tensor, gen_cond: torch.Tensor, new_ctx_cond: torch.Tensor) -> torch.Tensor:
         """One frame; returns the decoded image buffer [B, 3, 360, 640] (overwritten
         by the next step)."""
+        if self.device_cond:
+            raise RuntimeError("this engine computes the conditioning on the GPU: use step_actions")
         self.fe.chunk.copy_(noise, non_blocking=True)
         self.gen_cond.copy_(gen_cond, non_blocking=True)
         self.new_ctx_cond.copy_(new_ctx_cond, non_blocking=True)

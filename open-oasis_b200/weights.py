@@ -145,6 +145,32 @@ def count_blocks(sd: dict, prefix: str = "blocks.") -> int:
     return max(ids) + 1 if ids else 0
 
 
+class CondDeviceWeights:
+    """The conditioning weights (t_embedder MLP, external_cond) on one GPU in fp32,
+    plus the ctypes OasisCondWeights struct (the device copies of the host
+    tensors compute_cond_for_frame reads, oasis_inference.py:1406-1427)."""
+
+    def __init__(self, sd: dict, device: torch.device | str = "cuda"):
+        dev = torch.device(device)
+        self.device = dev
+
+        def f32(t):
+            return t.to(dev, torch.float32).contiguous()
+
+        self.tensors = {
+            "t_freqs": f32(H.timestep_freqs()),
+            "t_w0": f32(sd["t_embedder.mlp.0.weight"]), "t_b0": f32(sd["t_embedder.mlp.0.bias"]),
+            "t_w2": f32(sd["t_embedder.mlp.2.weight"]), "t_b2": f32(sd["t_embedder.mlp.2.bias"]),
+            "ext_w": f32(sd["external_cond.weight"]), "ext_b": f32(sd["external_cond.bias"])}
+        st = _lib.OasisCondWeights()
+        for k, t in self.tensors.items():
+            setattr(st, k, t.data_ptr())
+        self.struct = st
+
+    def ref(self):
+        return C.byref(self.struct)
+
+
 class DitDeviceWeights:
     """DiT weights resident on one GPU in the kernels' layout, plus the ctypes
     OasisDitWeights struct pointing at them (replaces the `dev` dict of
@@ -195,15 +221,7 @@ class DitDeviceWeights:
                                                  "t_embedder.mlp.2.weight", "t_embedder.mlp.2.bias",
                                                  "external_cond.weight", "external_cond.bias")}
         # the same weights on the device for oasis_compute_cond (conditioning inside the frame graph)
-        self.cond_tensors = {
-            "t_freqs": f32(H.timestep_freqs()),
-            "t_w0": f32(sd["t_embedder.mlp.0.weight"]), "t_b0": f32(sd["t_embedder.mlp.0.bias"]),
-            "t_w2": f32(sd["t_embedder.mlp.2.weight"]), "t_b2": f32(sd["t_embedder.mlp.2.bias"]),
-            "ext_w": f32(sd["external_cond.weight"]), "ext_b": f32(sd["external_cond.bias"])}
-        cw = _lib.OasisCondWeights()
-        for k, t in self.cond_tensors.items():
-            setattr(cw, k, t.data_ptr())
-        self.cond_struct = cw
+        self.cond = CondDeviceWeights(sd, dev)
         self.conv_w = sd["x_embedder.proj.weight"].float()
         self.conv_b = sd["x_embedder.proj.bias"].float()
 

@@ -7,7 +7,8 @@ against the oracle run at B = 1 on the same per-session seeds:
   - each DDIM step's v-prediction (the GPU and the oracle each follow their own
     trajectory), rel-L2 <= 1e-2 and cosine >= 0.999;
   - the decoded frame after the 4 steps;
-  - the whole frame as the benchmark runs it (FrameEngine, one CUDA graph).
+  - the whole frame as the benchmark runs it (FrameEngine, one CUDA graph with
+    the conditioning computed on the GPU from the action window).
 C5: 16 sessions x T = 32 (M = 73 728, the long-T temporal kernel), one full-depth
 DiT forward, sessions 0 and 15 against the oracle.
 
@@ -50,8 +51,8 @@ def _session_context(T, s):
 def test_c4_bench_frame_matches_oracle(c4_weights):
     dsd, vsd, dw, vw = c4_weights
     B, T = 64, 8
-    fe = E.FrameEngine(dw, vw, B, T)
-    chunk0, ctx_z, conds = bench.make_inputs(fe, dw, 0, B, T)
+    fe = E.FrameEngine(dw, vw, B, T, device_cond=True)  # as bench.py: conditioning inside the frame graph
+    chunk0, ctx_z, conds, _ = bench.make_inputs(fe, dw, 0, B, T)
     steps = fe.steps
     idx = list(C4_SESSIONS)
 
