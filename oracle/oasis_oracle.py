@@ -293,13 +293,19 @@ def _vae_rope(sd: dict) -> torch.Tensor:
     return sd["rotary_angles"].float() if "rotary_angles" in sd else vae_rope_freqs(sd["rotary_freqs"].float())
 
 
-def vae_decode(latent: torch.Tensor, sd: dict) -> torch.Tensor:
-    """latent (B, 576, 16) -> image (B, 3, 360, 640) clamped to [-1, 1]."""
+def vae_decode_patches(latent: torch.Tensor, sd: dict) -> torch.Tensor:
+    """latent (B, 576, 16) -> predictor output (B, 576, 1200): post_quant_conv,
+    the decoder blocks, dec_norm, predictor (vae_decode_forward,
+    oasis_inference.py:1546-1618)."""
     x = F.linear(latent, sd["post_quant_conv.weight"], sd["post_quant_conv.bias"])
     x = _vae_blocks(x, sd, "decoder", _vae_rope(sd))
     x = F.layer_norm(x, (D,), sd["dec_norm.weight"], sd["dec_norm.bias"], eps=1e-6)
-    pred = F.linear(x, sd["predictor.weight"], sd["predictor.bias"])
-    return vae_unpatchify(pred).clamp(-1, 1)
+    return F.linear(x, sd["predictor.weight"], sd["predictor.bias"])
+
+
+def vae_decode(latent: torch.Tensor, sd: dict) -> torch.Tensor:
+    """latent (B, 576, 16) -> image (B, 3, 360, 640) clamped to [-1, 1]."""
+    return vae_unpatchify(vae_decode_patches(latent, sd)).clamp(-1, 1)
 
 
 def vae_encode(image: torch.Tensor, sd: dict) -> torch.Tensor:

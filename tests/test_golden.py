@@ -261,3 +261,25 @@ def test_temporal_attention_matches_reference_causal_bias(T):
     causal = torch.tril(torch.ones(T, T, dtype=torch.bool))
     per_group = O._attn(q.view(groups, T, 64), k.view(groups, T, 64), v.view(groups, T, 64), causal).reshape(32, 64)
     assert torch.allclose(per_group, packed, atol=1e-6)
+
+
+def test_vae_decoder_matches_reference_dataflow():
+    """The oracle's VAE decoder against the reference's own vae_decode_forward
+    (weight packing with the [Q|K|V|Q_swap|K_swap] RoPE trick, heads-first
+    vae_rope_fused layout, SDPA, residual order, final LN, predictor), run by
+    make_golden.py at fp32 on the same seeded weights, angles and latent."""
+    from tests.golden.make_golden import VAE_OUT, vae_fixture_weights
+
+    g = np.load(VAE_OUT)
+    sd, angles, latent = vae_fixture_weights()
+    assert abs(float(latent.double().sum()) - float(g["latent_sum"])) < 1e-9
+    assert abs(float(angles.double().sum()) - float(g["angles_sum"])) < 1e-6
+    sd = dict(sd, rotary_angles=angles)
+    with torch.no_grad():
+        pred = O.vae_decode_patches(latent[None], sd)[0]
+    rows = g["rows"]
+    np.testing.assert_allclose(pred[rows].numpy(), g["pred_rows"], rtol=0, atol=2e-5)
+    np.testing.assert_allclose(pred.double().sum(1).numpy(), g["pred_rowsum"], rtol=1e-5, atol=1e-4)
+    np.testing.assert_allclose(pred.double().norm(dim=1).numpy(), g["pred_rownorm"], rtol=1e-5)
+    img = O.vae_unpatchify(pred[None])
+    np.testing.assert_allclose(img.double().sum((0, 2, 3)).numpy(), g["image_channel_sum"], rtol=1e-5, atol=1e-3)
