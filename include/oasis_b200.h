@@ -342,6 +342,52 @@ typedef struct OasisTpArgs {
 size_t oasis_tp_workspace_size(int batch, int frames, int heads);
 int oasis_dit_forward_tp(const OasisDitWeights* shard, const OasisTpArgs* a, oasis_stream_t stream);
 
+/* Sequence-parallel form of the same n-way tensor parallelism (Megatron-style):
+ * the residual stream stays sharded by session - rank r owns sessions
+ * [r B / n, (r + 1) B / n) - so LayerNorm, adaLN and the gated residuals run on
+ * 1/n of the rows. Per sub-block the collectives are an all-gather of the
+ * LayerNorm output (bf16) before each column-parallel projection (QKV, FC1) and a
+ * reduce-scatter of the row-parallel partials (O, FC2) back to the owned rows,
+ * in place of the all-reduce: half the bytes at fp32 partials, a quarter at bf16.
+ * Same weight shards as oasis_dit_forward_tp. Replaces the same reference code
+ * (oasis_inference.py:289-305, 1153-1201).
+ *
+ * Collective callbacks, issued in order on `stream` (NCCL, torch.distributed,
+ * a peer-memory kernel); `count` is elements per rank, `dtype` an OASIS_DTYPE_*:
+ *   reduce_scatter: recv[i] = sum over ranks k of send_k[rank count + i]
+ *                   (send: world x count, recv: count)
+ *   all_gather:     recv[k count + i] = send_k[i] (send: count, recv: world x count)
+ * A non-zero return aborts the forward with that status. The communication
+ * buffers are caller-owned so the callbacks can name them. */
+#define OASIS_DTYPE_F32 0
+#define OASIS_DTYPE_BF16 1
+typedef int (*oasis_collective_fn)(const void* send, void* recv, size_t count, int dtype, void* user,
+                                   oasis_stream_t stream);
+
+typedef struct OasisTpSpArgs {
+  int batch;          /* B sessions over all ranks; B % world == 0 */
+  int frames;         /* T <= 32 */
+  int heads;          /* this rank's heads: 16 / world */
+  int rank, world;
+  float* z;           /* [B / world, T, 144, 1024] fp32: this rank's sessions, overwritten */
+  const float* cond;  /* [B / world, T, 1024] */
+  float* v_out;       /* [B, 144, 64] fp32: the last frame of every session (gathered) */
+  int partial_dtype;  /* OASIS_DTYPE_BF16 or OASIS_DTYPE_F32: type of partial / shard */
+  void* partial;      /* [B T 144, 1024] partial_dtype: row-parallel output, reduce_scatter send */
+  void* shard;        /* [B T 144 / world, 1024] partial_dtype: reduce_scatter recv */
+  void* xn_local;     /* [B T 144 / world, 1024] bf16: LayerNorm of the owned rows, all_gather send */
+  void* xn;           /* [B T 144, 1024] bf16: all_gather recv, the projections' input */
+  float* v_local;     /* [B / world, 144, 64] fp32: all_gather send of v_out */
+  oasis_collective_fn reduce_scatter;
+  oasis_collective_fn all_gather;
+  void* user;
+  void* workspace;
+  size_t workspace_bytes;
+} OasisTpSpArgs;
+
+size_t oasis_tp_sp_workspace_size(int batch, int frames, int heads, int world);
+int oasis_dit_forward_tp_sp(const OasisDitWeights* shard, const OasisTpSpArgs* a, oasis_stream_t stream);
+
 /* ------------------------------------------------------------ op level --- */
 
 /* tcgen05 GEMM: acc = A[M,K] . W[N,K]^T (bf16 in, fp32 accumulate) + bias, then

@@ -125,6 +125,18 @@ class OasisTpArgs(C.Structure):
                 ("workspace", vp), ("workspace_bytes", C.c_size_t)]
 
 
+COLLECTIVE_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_void_p, C.c_size_t, C.c_int, C.c_void_p, C.c_void_p)
+OASIS_DTYPE_F32 = 0
+OASIS_DTYPE_BF16 = 1
+
+
+class OasisTpSpArgs(C.Structure):
+    _fields_ = [("batch", C.c_int), ("frames", C.c_int), ("heads", C.c_int), ("rank", C.c_int), ("world", C.c_int),
+                ("z", fp), ("cond", fp), ("v_out", fp), ("partial_dtype", C.c_int), ("partial", vp), ("shard", vp),
+                ("xn_local", vp), ("xn", vp), ("v_local", fp), ("reduce_scatter", COLLECTIVE_FN),
+                ("all_gather", COLLECTIVE_FN), ("user", vp), ("workspace", vp), ("workspace_bytes", C.c_size_t)]
+
+
 class OasisLayerNormArgs(C.Structure):
     _fields_ = [("x", fp), ("y", vp), ("rows_out", C.c_int), ("P", C.c_int), ("in_group", C.c_longlong),
                 ("in_off", C.c_longlong), ("frame_mul", C.c_longlong), ("frame_add", C.c_longlong),
@@ -157,6 +169,8 @@ SIGNATURES = {
     "oasis_dit_forward_tp": (C.c_int, [C.POINTER(OasisDitWeights), C.POINTER(OasisTpArgs), vp]),
     "oasis_cond_workspace_size": (C.c_size_t, [C.c_int]),
     "oasis_compute_cond": (C.c_int, [C.POINTER(OasisCondWeights), fp, C.c_int, fp, C.c_int, fp, vp, C.c_size_t, vp]),
+    "oasis_tp_sp_workspace_size": (C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int]),
+    "oasis_dit_forward_tp_sp": (C.c_int, [C.POINTER(OasisDitWeights), C.POINTER(OasisTpSpArgs), vp]),
     "oasis_kv_cache_size": (C.c_size_t, [C.c_int, C.c_int]),
     "oasis_dit_precompute_past": (C.c_int, [C.POINTER(OasisDitWeights), C.POINTER(OasisDitArgs), vp, C.c_size_t, vp]),
     "oasis_dit_forward_current": (C.c_int, [C.POINTER(OasisDitWeights), C.POINTER(OasisDitArgs), vp, C.c_size_t,

@@ -703,6 +703,155 @@ int tp_forward_impl(const OasisDitWeights* w, const OasisTpArgs* a, cudaStream_t
   return gemm_launch(p, st);
 }
 
+// ---- sequence-parallel tensor parallelism ----
+// Per-rank scratch: the adaLN table of the owned frames, the local heads' QKV,
+// attention output and MLP hidden over all rows, split-K partials. The
+// communication buffers are the caller's (OasisTpSpArgs).
+struct TpSpScratch {
+  __nv_bfloat16* silu;
+  float* adaln;
+  __nv_bfloat16* qkv;
+  __nv_bfloat16* attn;
+  __nv_bfloat16* h;
+  void* splitk;
+  size_t splitk_bytes;
+};
+
+size_t carve_tp_sp(Carve& c, int B, int T, int heads, int world, TpSpScratch* s) {
+  const size_t Fl = (size_t)(B / world) * T, M = (size_t)B * T * kP, HD = (size_t)heads * 64;
+  TpSpScratch d;
+  d.silu = c.take<__nv_bfloat16>(Fl * kD);
+  d.adaln = c.take<float>(Fl * OASIS_ADALN_ROWS);
+  d.qkv = c.take<__nv_bfloat16>(M * 3 * HD);
+  d.attn = c.take<__nv_bfloat16>(M * HD);
+  d.h = c.take<__nv_bfloat16>(M * 4 * HD);
+  size_t m = 0;
+  auto upd = [&](size_t x) { m = x > m ? x : m; };
+  upd(gemm_workspace_bytes((int)M, (int)(3 * HD), kD));
+  upd(gemm_workspace_bytes((int)M, kD, (int)HD));
+  upd(gemm_workspace_bytes((int)M, (int)(4 * HD), kD));
+  upd(gemm_workspace_bytes((int)M, kD, (int)(4 * HD)));
+  upd(gemm_workspace_bytes((int)Fl, OASIS_ADALN_ROWS, kD));
+  upd(gemm_workspace_bytes((B / world) * kP, kOut, kD));
+  d.splitk_bytes = m;
+  d.splitk = m ? c.take<uint8_t>(m) : nullptr;
+  if (s) *s = d;
+  return c.used;
+}
+
+int tp_sp_forward_impl(const OasisDitWeights* w, const OasisTpSpArgs* a, cudaStream_t st) {
+  OASIS_REQUIRE(w && a, "dit_forward_tp_sp: null argument");
+  const int B = a->batch, T = a->frames, H = a->heads, n = a->world, rk = a->rank;
+  OASIS_REQUIRE(n >= 1 && rk >= 0 && rk < n && H * n == 16, "dit_forward_tp_sp: rank %d of %d with %d heads", rk, n, H);
+  OASIS_REQUIRE(B > 0 && B % n == 0 && T > 0 && T <= OASIS_MAX_FRAMES,
+                "dit_forward_tp_sp: batch=%d (a multiple of world=%d) frames=%d", B, n, T);
+  OASIS_REQUIRE(a->partial_dtype == OASIS_DTYPE_F32 || a->partial_dtype == OASIS_DTYPE_BF16,
+                "dit_forward_tp_sp: partial_dtype=%d", a->partial_dtype);
+  OASIS_REQUIRE(a->z && a->cond && a->v_out && a->partial && a->shard && a->xn_local && a->xn && a->v_local,
+                "dit_forward_tp_sp: null tensor");
+  OASIS_REQUIRE(a->reduce_scatter && a->all_gather, "dit_forward_tp_sp: null collective");
+  OASIS_REQUIRE(w->num_subblocks >= 0 && w->num_subblocks <= OASIS_DIT_SUBBLOCKS, "dit_forward_tp_sp: num_subblocks");
+  Carve c(a->workspace, a->workspace_bytes);
+  TpSpScratch s;
+  carve_tp_sp(c, B, T, H, n, &s);
+  if (!a->workspace || !c.ok())
+    return set_error(OASIS_ERR_WORKSPACE, "dit_forward_tp_sp: workspace %zu bytes < %zu", a->workspace_bytes, c.used);
+  const int Bl = B / n, Fl = Bl * T, Ml = Fl * kP, M = B * T * kP, HD = H * 64;
+  const bool bf16_part = a->partial_dtype == OASIS_DTYPE_BF16;
+  const long long ldm = (long long)w->num_subblocks * OASIS_ADALN_WIDTH + 2 * kD;
+  OASIS_TRY(compute_adaln(w, a->cond, Fl, s.silu, s.adaln, s.splitk, s.splitk_bytes, st));
+  float* z = a->z;
+  auto xn_loc = static_cast<__nv_bfloat16*>(a->xn_local);
+  auto xn = static_cast<__nv_bfloat16*>(a->xn);
+  auto collective = [&](oasis_collective_fn fn, const void* send, void* recv, size_t count, int dtype,
+                        const char* what) -> int {
+    const int rc = fn(send, recv, count, dtype, a->user, st);
+    if (rc != 0) return set_error(rc < 0 ? rc : OASIS_ERR_CUDA, "dit_forward_tp_sp: %s returned %d", what, rc);
+    return OASIS_OK;
+  };
+  // LayerNorm + modulate of the owned rows, then all-gather: every rank holds xn of all rows
+  auto ln_gather = [&](long long shift, long long scale, const char* what) -> int {
+    LayerNormParams ln;
+    ln.rows_out = Ml;
+    ln.P = kP;
+    ln.in_group = kP;
+    ln.mod = s.adaln;
+    ln.ld_mod = ldm;
+    ln.shift_off = shift;
+    ln.scale_off = scale;
+    OASIS_TRY(layernorm_launch(z, xn_loc, ln, st));
+    return collective(a->all_gather, xn_loc, xn, (size_t)Ml * kD, OASIS_DTYPE_BF16, what);
+  };
+  // row-parallel projection -> reduce-scatter to the owned rows -> bias, gate, residual
+  auto project_reduce = [&](const __nv_bfloat16* in, const void* wt, int K, const float* bias, long long gate_off,
+                            const char* what) -> int {
+    GemmProblem p = gemm(in, wt, M, kD, K, s.splitk, s.splitk_bytes);
+    p.epi.mode = bf16_part ? kEpiBF16 : kEpiF32;
+    p.epi.out = a->partial;
+    p.epi.ldo = kD;
+    OASIS_TRY(gemm_launch(p, st));
+    OASIS_TRY(collective(a->reduce_scatter, a->partial, a->shard, (size_t)Ml * kD, a->partial_dtype, what));
+    if (bf16_part)
+      return gated_residual_bf16_launch(z, static_cast<const __nv_bfloat16*>(a->shard), bias, s.adaln + gate_off, ldm,
+                                        kP, Ml, st);
+    return gated_residual_launch(z, static_cast<const float*>(a->shard), bias, s.adaln + gate_off, ldm, kP, Ml, st);
+  };
+  for (int i = 0; i < w->num_subblocks; ++i) {
+    const OasisDitSubBlock& sb = w->sub[i];
+    const bool spatial = (i % 2) == 0;
+    const long long off = (long long)i * OASIS_ADALN_WIDTH;
+    OASIS_TRY(ln_gather(off, off + kD, "all_gather before QKV"));
+    {
+      GemmProblem p = gemm(xn, sb.qkv_w, M, 3 * HD, kD, s.splitk, s.splitk_bytes);
+      p.epi.mode = kEpiRopeBF16;
+      p.epi.out = s.qkv;
+      p.epi.ldo = 3 * HD;
+      p.epi.rope = spatial ? w->rope_spatial : w->rope_temporal;
+      p.epi.rope_div = spatial ? 1 : kP;
+      p.epi.rope_mod = spatial ? kP : T;
+      p.epi.rope_stride = spatial ? kP : OASIS_MAX_FRAMES;
+      p.epi.rope_dim = HD;
+      OASIS_TRY(gemm_launch(p, st));
+    }
+    if (spatial)
+      OASIS_TRY(attention_full_launch(s.qkv, s.attn, B * T, kP, H, st));
+    else
+      OASIS_TRY(attention_temporal_launch(s.qkv, s.attn, B, T, kP, H, st));
+    OASIS_TRY(project_reduce(s.attn, sb.out_w, HD, sb.out_b, off + 2 * kD, "reduce_scatter after O"));
+    OASIS_TRY(ln_gather(off + 3 * kD, off + 4 * kD, "all_gather before FC1"));
+    {
+      GemmProblem p = gemm(xn, sb.fc1_w, M, 4 * HD, kD, s.splitk, s.splitk_bytes);
+      p.epi.mode = kEpiGeluTanhBF16;
+      p.epi.out = s.h;
+      p.epi.ldo = 4 * HD;
+      p.epi.bias = sb.fc1_b;
+      OASIS_TRY(gemm_launch(p, st));
+    }
+    OASIS_TRY(project_reduce(s.h, sb.fc2_w, 4 * HD, sb.fc2_b, off + 5 * kD, "reduce_scatter after FC2"));
+  }
+  // final layer over the owned sessions' last frames, then gather v of all sessions
+  const long long foff = (long long)w->num_subblocks * OASIS_ADALN_WIDTH;
+  LayerNormParams ln;
+  ln.P = kP;
+  ln.mod = s.adaln;
+  ln.ld_mod = ldm;
+  ln.shift_off = foff;
+  ln.scale_off = foff + kD;
+  ln.rows_out = Bl * kP;
+  ln.in_group = (long long)T * kP;
+  ln.in_off = (long long)(T - 1) * kP;
+  ln.frame_mul = T;
+  ln.frame_add = T - 1;
+  OASIS_TRY(layernorm_launch(z, xn_loc, ln, st));
+  GemmProblem p = gemm(xn_loc, w->final_w, Bl * kP, kOut, kD, s.splitk, s.splitk_bytes);
+  p.epi.mode = kEpiF32;
+  p.epi.out = a->v_local;
+  p.epi.ldo = kOut;
+  p.epi.bias = w->final_b;
+  OASIS_TRY(gemm_launch(p, st));
+  return collective(a->all_gather, a->v_local, a->v_out, (size_t)Bl * kP * kOut, OASIS_DTYPE_F32, "all_gather of v");
+}
+
 // ---- context caching (precompute_past_state / dit_forward_currentonly) ----
 
 size_t kv_cache_bytes(int B, int Tp) { return (size_t)(OASIS_DIT_SUBBLOCKS / 2) * kv_slot_elems(B, Tp) * 2; }
@@ -981,6 +1130,16 @@ size_t oasis_tp_workspace_size(int batch, int frames, int heads) {
 int oasis_dit_forward_tp(const OasisDitWeights* shard, const OasisTpArgs* a, oasis_stream_t stream) {
   g_msg[0] = 0;
   return tp_forward_impl(shard, a, S(stream));
+}
+
+size_t oasis_tp_sp_workspace_size(int batch, int frames, int heads, int world) {
+  if (world < 1 || heads < 1 || batch < world || batch % world) return 0;
+  Carve c(nullptr, 0);
+  return carve_tp_sp(c, batch, frames, heads, world, nullptr);
+}
+
+int oasis_dit_forward_tp_sp(const OasisDitWeights* shard, const OasisTpSpArgs* a, oasis_stream_t stream) {
+  return tp_sp_forward_impl(shard, a, S(stream));
 }
 
 size_t oasis_kv_cache_size(int batch, int past_frames) {

@@ -5,6 +5,8 @@
 //
 // All are HBM-bound row/element kernels: fp32 vectorised loads (float4),
 // warp-shuffle reductions, bf16 stores where the consumer is a GEMM operand.
+#include <cstdlib>
+
 #include "common.cuh"
 #include "pointwise.cuh"
 #include "status.h"
@@ -14,23 +16,35 @@ namespace {
 
 constexpr int D = 1024;  // model width of both the DiT and the VAE decoder
 
-// One warp per output row. x is fp32 [*, 1024]; y is bf16 [rows_out, 1024].
-// Row map (gathers the last frame of each session for the final layer):
+// One warp per run of `R` consecutive output rows. x is fp32 [*, 1024]; y is
+// bf16 [rows_out, 1024]. Row map (gathers the last frame of each session for the
+// final layer):
 //   in_row = (r / P) * in_group + in_off + r % P
 //   frame  = (r / P) * frame_mul + frame_add
 // Modulated: y = LN(x) * scale1p[frame] + shift[frame] (scale1p holds 1+scale).
 // Affine:    y = LN(x) * w + b.
-__global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y,
-                                                        LayerNormParams p) {
+// A run never crosses a group of P rows (R divides P), so the warp loads its
+// lanes' 64 modulation (or affine) values once and reuses them for all R rows:
+// the per-row L2 traffic is the 4 KB row instead of the row plus 8 KB of
+// modulation. The next row's loads are issued before the current row's
+// reduction, so each warp keeps two rows in flight.
+__device__ __forceinline__ void ln_load_row(const float* xr, int lane, float4 (&v)[8]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) v[j] = reinterpret_cast<const float4*>(xr)[lane + 32 * j];
+}
+
+template <bool kPrefetch>
+__global__ void __launch_bounds__(256, kPrefetch ? 1 : 2)
+    layernorm_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, LayerNormParams p, int R) {
   pdl_trigger();
   pdl_wait();
   const int warp_global = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (warp_global >= p.rows_out) return;
-  const int r = warp_global;
-  const int grp = r / p.P, within = r - grp * p.P;
-  const long long in_row = (long long)grp * p.in_group + p.in_off + within;
-  const float* xr = x + in_row * D;
+  const int r0 = warp_global * R;
+  if (r0 >= p.rows_out) return;
+  const int r1 = min(r0 + R, p.rows_out);
+  const int grp = r0 / p.P;
+  auto in_row = [&](int r) { return (long long)grp * p.in_group + p.in_off + (r - grp * p.P); };
 
   const float* mul;
   const float* add;
@@ -42,41 +56,47 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict_
     mul = p.mod + frame * p.ld_mod + p.scale_off;
     add = p.mod + frame * p.ld_mod + p.shift_off;
   }
-  float4 v[8], m[8], a[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) v[j] = reinterpret_cast<const float4*>(xr)[lane + 32 * j];
-  // the modulation (or affine) vectors do not depend on the row statistics:
-  // fetch them now so their latency overlaps the reduction
+  float4 v[8], nv[8], m[8], a[8];
+  ln_load_row(x + in_row(r0) * D, lane, v);
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const int c = 4 * (lane + 32 * j);
     m[j] = __ldg(reinterpret_cast<const float4*>(mul + c));
     a[j] = add ? __ldg(reinterpret_cast<const float4*>(add + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  float s = 0.f;
+  for (int r = r0; r < r1; ++r) {
+    if (kPrefetch && r + 1 < r1) ln_load_row(x + in_row(r + 1) * D, lane, nv);
+    float s = 0.f;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+    for (int j = 0; j < 8; ++j) s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  const float mean = s * (1.f / D);
-  float q = 0.f;
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float mean = s * (1.f / D);
+    float q = 0.f;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const float a0 = v[j].x - mean, b0 = v[j].y - mean, c0 = v[j].z - mean, d0 = v[j].w - mean;
-    q += (a0 * a0 + b0 * b0) + (c0 * c0 + d0 * d0);
-  }
+    for (int j = 0; j < 8; ++j) {
+      const float a0 = v[j].x - mean, b0 = v[j].y - mean, c0 = v[j].z - mean, d0 = v[j].w - mean;
+      q += (a0 * a0 + b0 * b0) + (c0 * c0 + d0 * d0);
+    }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
-  const float rstd = rsqrtf(q * (1.f / D) + p.eps);
-  __nv_bfloat16* yr = y + (long long)r * D;
+    for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+    const float rstd = rsqrtf(q * (1.f / D) + p.eps);
+    __nv_bfloat16* yr = y + (long long)r * D;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int c = 4 * (lane + 32 * j);
-    const float o0 = (v[j].x - mean) * rstd * m[j].x + a[j].x;
-    const float o1 = (v[j].y - mean) * rstd * m[j].y + a[j].y;
-    const float o2 = (v[j].z - mean) * rstd * m[j].z + a[j].z;
-    const float o3 = (v[j].w - mean) * rstd * m[j].w + a[j].w;
-    *reinterpret_cast<uint2*>(yr + c) = make_uint2(pack_bf16x2(o0, o1), pack_bf16x2(o2, o3));
+    for (int j = 0; j < 8; ++j) {
+      const int c = 4 * (lane + 32 * j);
+      const float o0 = (v[j].x - mean) * rstd * m[j].x + a[j].x;
+      const float o1 = (v[j].y - mean) * rstd * m[j].y + a[j].y;
+      const float o2 = (v[j].z - mean) * rstd * m[j].z + a[j].z;
+      const float o3 = (v[j].w - mean) * rstd * m[j].w + a[j].w;
+      *reinterpret_cast<uint2*>(yr + c) = make_uint2(pack_bf16x2(o0, o1), pack_bf16x2(o2, o3));
+    }
+    if (kPrefetch) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = nv[j];
+    } else if (r + 1 < r1) {
+      ln_load_row(x + in_row(r + 1) * D, lane, v);
+    }
   }
 }
 
@@ -197,7 +217,8 @@ int grid_for(long long n, int threads) {
 
 // z[r, :] += gate[r / rows_per_frame, :] * (x[r, :] + bias)   (gate NULL: plain residual)
 // x is the all-reduced output of a row-parallel projection (tensor parallelism).
-__global__ void __launch_bounds__(256) gated_residual_kernel(float* __restrict__ z, const float* __restrict__ x,
+template <typename TX>
+__global__ void __launch_bounds__(256) gated_residual_kernel(float* __restrict__ z, const TX* __restrict__ x,
                                                              const float* __restrict__ bias,
                                                              const float* __restrict__ gate, long long ldg,
                                                              int rows_per_frame, long long n4) {
@@ -208,7 +229,14 @@ __global__ void __launch_bounds__(256) gated_residual_kernel(float* __restrict__
     const long long e = i * 4;
     const long long r = e / D;
     const int c = (int)(e - r * D);
-    float4 v = reinterpret_cast<const float4*>(x)[i];
+    float4 v;
+    if constexpr (sizeof(TX) == 4) {
+      v = reinterpret_cast<const float4*>(x)[i];
+    } else {  // bf16 partial sums (sequence-parallel tensor parallelism)
+      const uint2 u = reinterpret_cast<const uint2*>(x)[i];
+      v = make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u), __uint_as_float(u.y << 16),
+                      __uint_as_float(u.y & 0xffff0000u));
+    }
     if (bias) {
       const float4 b = __ldg(reinterpret_cast<const float4*>(bias + c));
       v.x += b.x; v.y += b.y; v.z += b.z; v.w += b.w;
@@ -287,7 +315,19 @@ int gated_residual_launch(float* z, const float* x, const float* bias, const flo
   OASIS_REQUIRE(!gate || rows_per_frame > 0, "gated_residual: rows_per_frame");
   const long long n4 = (long long)rows * D / 4;
   if (n4 == 0) return OASIS_OK;
-  launch_pdl(gated_residual_kernel, dim3(grid_for(n4, 256)), dim3(256), 0, s, z, x, bias, gate, ldg, rows_per_frame, n4);
+  launch_pdl(gated_residual_kernel<float>, dim3(grid_for(n4, 256)), dim3(256), 0, s, z, x, bias, gate, ldg,
+             rows_per_frame, n4);
+  return check_launch("gated_residual_kernel");
+}
+
+int gated_residual_bf16_launch(float* z, const __nv_bfloat16* x, const float* bias, const float* gate, long long ldg,
+                               int rows_per_frame, int rows, cudaStream_t s) {
+  OASIS_REQUIRE(z && x && rows >= 0, "gated_residual: bad arguments");
+  OASIS_REQUIRE(!gate || rows_per_frame > 0, "gated_residual: rows_per_frame");
+  const long long n4 = (long long)rows * D / 4;
+  if (n4 == 0) return OASIS_OK;
+  launch_pdl(gated_residual_kernel<__nv_bfloat16>, dim3(grid_for(n4, 256)), dim3(256), 0, s, z, x, bias, gate, ldg,
+             rows_per_frame, n4);
   return check_launch("gated_residual_kernel");
 }
 
@@ -296,9 +336,35 @@ int layernorm_launch(const float* x, __nv_bfloat16* y, const LayerNormParams& p,
   OASIS_REQUIRE(p.rows_out >= 0 && p.P > 0, "layernorm: bad row map");
   OASIS_REQUIRE(p.affine_w || p.mod, "layernorm: need affine weights or a modulation table");
   if (p.rows_out == 0) return OASIS_OK;
+  // Rows per warp: enough rows that every SM still gets several warps of eight
+  // rows (at 73 728 rows: 9 216 warps), else one row per warp; R divides P so a
+  // warp's rows share their modulation row.
+  static const int force_r = [] {
+    const char* e = getenv("OASIS_LN_ROWS");
+    return e ? atoi(e) : 0;
+  }();
+  int R = 1;
+  if (force_r > 0) {
+    R = p.P % force_r == 0 ? force_r : 1;
+  } else if (p.rows_out >= num_sms() * 8 * 16) {
+    const int cand[] = {4, 6, 3, 2};  // 73 728 rows: R = 1 / 2 / 4 / 8 / 16 -> 89.0 / 77.8 / 75.5 / 77.2 / 80.6 us
+    for (int c : cand)
+      if (p.P % c == 0) {
+        R = c;
+        break;
+      }
+  }
+  const int warps = (p.rows_out + R - 1) / R;
   const int warps_per_block = 8;
-  const int grid = (p.rows_out + warps_per_block - 1) / warps_per_block;
-  launch_pdl(layernorm_kernel, dim3(grid), dim3(32 * warps_per_block), 0, s, x, y, p);
+  const int grid = (warps + warps_per_block - 1) / warps_per_block;
+  static const bool prefetch = [] {
+    const char* e = getenv("OASIS_LN_PREFETCH");
+    return e && e[0] == '1';
+  }();
+  if (prefetch)
+    launch_pdl(layernorm_kernel<true>, dim3(grid), dim3(32 * warps_per_block), 0, s, x, y, p, R);
+  else
+    launch_pdl(layernorm_kernel<false>, dim3(grid), dim3(32 * warps_per_block), 0, s, x, y, p, R);
   return check_launch("layernorm_kernel");
 }
 

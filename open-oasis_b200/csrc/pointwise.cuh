@@ -49,6 +49,9 @@ int ddim_launch(float* chunk, const float* v, const DdimCoeffs& c, long long n, 
 int bridge_launch(const float* chunk, float* latent, int batch, float inv_scale, cudaStream_t s);
 int gated_residual_launch(float* z, const float* x, const float* bias, const float* gate, long long ldg,
                           int rows_per_frame, int rows, cudaStream_t s);
+// The same with bf16 x (the reduce-scattered partial of sequence-parallel TP).
+int gated_residual_bf16_launch(float* z, const __nv_bfloat16* x, const float* bias, const float* gate, long long ldg,
+                               int rows_per_frame, int rows, cudaStream_t s);
 int post_quant_launch(const float* lat, const float* w, const float* b, float* z, int rows, cudaStream_t s);
 // VAE encoder: image [B, 3, 360, 640] -> bf16 patch rows [B * 576, kp] (kp >= 1200, zero-padded);
 // moments [B * 576, 32] -> latent [B, 576, 16] and/or chunk [B, 144, 64], both scaled by `scale`.

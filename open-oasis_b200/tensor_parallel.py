@@ -127,3 +127,98 @@ def dit_forward_tp(tpw: TPDitWeights, z: torch.Tensor, cond: torch.Tensor, v_out
             raise errors[0]
         raise
     return v_out
+
+
+# --------------------------------------------------------------------------- sequence parallel
+class TPSpBuffers:
+    """Per-rank buffers of the sequence-parallel TP forward (oasis_dit_forward_tp_sp)
+    for B sessions x T frames over `world` ranks: the library workspace and the
+    caller-owned communication buffers the collectives read and write."""
+
+    def __init__(self, tpw: TPDitWeights, batch: int, frames: int, device, partial_dtype=torch.bfloat16):
+        n = tpw.n
+        if batch % n:
+            raise ValueError(f"{batch} sessions do not split over {n} ranks")
+        if partial_dtype not in (torch.bfloat16, torch.float32):
+            raise ValueError("partial_dtype must be bf16 or fp32")
+        dev = torch.device(device)
+        M = batch * frames * H.N_PATCHES
+        Ml = M // n
+        self.batch, self.frames, self.world, self.rank = batch, frames, n, tpw.r
+        nbytes = int(_lib.load().oasis_tp_sp_workspace_size(batch, frames, tpw.heads, n))
+        self.workspace = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
+        self.partial = torch.empty(M, D, dtype=partial_dtype, device=dev)
+        self.shard = torch.empty(Ml, D, dtype=partial_dtype, device=dev)
+        self.xn_local = torch.empty(Ml, D, dtype=torch.bfloat16, device=dev)
+        self.xn = torch.empty(M, D, dtype=torch.bfloat16, device=dev)
+        self.v_local = torch.empty(batch // n, H.N_PATCHES, H.OUT_DIM, device=dev)
+
+    def registry(self, v_out: torch.Tensor) -> dict[int, torch.Tensor]:
+        """Device pointer -> tensor of every buffer a collective callback may name."""
+        return {t.data_ptr(): t for t in (self.partial, self.shard, self.xn_local, self.xn, self.v_local, v_out)}
+
+
+def _reduce_scatter(recv: torch.Tensor, send: torch.Tensor, group=None) -> None:
+    if dist.get_backend(group) == "nccl":
+        dist.reduce_scatter_tensor(recv, send, group=group)
+    else:  # gloo has no reduce-scatter: all-reduce a copy, keep this rank's slice
+        tmp = send.clone()
+        dist.all_reduce(tmp, group=group)
+        r, n = dist.get_rank(group), dist.get_world_size(group)
+        recv.copy_(tmp.view(n, -1)[r].view_as(recv))
+
+
+def _all_gather(recv: torch.Tensor, send: torch.Tensor, group=None) -> None:
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(recv, send, group=group)
+    else:
+        dist.all_gather(list(recv.view(dist.get_world_size(group), -1).unbind(0)), send.reshape(-1), group=group)
+
+
+def dist_collectives(registry: dict[int, torch.Tensor], group=None, errors: list | None = None):
+    """The two callbacks of OasisTpSpArgs over torch.distributed (NCCL on GPUs,
+    gloo on the CPU): the library names buffers by pointer, `registry` maps them
+    back to tensors. A raised exception becomes a non-zero status (kept in
+    `errors`), which aborts the forward."""
+
+    def wrap(fn):
+        def cb(send, recv, count, dtype, user, stream):
+            try:
+                s, r = registry[send], registry[recv]
+                if s.numel() < count or r.numel() < count:
+                    raise ValueError(f"collective of {count} elements on buffers of {s.numel()} / {r.numel()}")
+                fn(r, s, group)
+                return 0
+            except Exception as e:  # noqa: BLE001  (reported through the C status)
+                if errors is not None:
+                    errors.append(e)
+                return -2
+        return _lib.COLLECTIVE_FN(cb)
+
+    return wrap(_reduce_scatter), wrap(_all_gather)
+
+
+def dit_forward_tp_sp(tpw: TPDitWeights, z_local: torch.Tensor, cond_local: torch.Tensor, v_out: torch.Tensor,
+                      bufs: TPSpBuffers, collectives=None, group=None, stream=None) -> torch.Tensor:
+    """Sequence-parallel TP DiT forward through oasis_dit_forward_tp_sp: this
+    rank's sessions z_local [B / n, T, 144, 1024] (overwritten) and cond_local
+    [B / n, T, 1024] -> v_out [B, 144, 64] for every session's last frame.
+    `collectives` = (reduce_scatter, all_gather) callbacks; by default
+    torch.distributed on `group`."""
+    errors: list = []
+    if collectives is None:
+        collectives = dist_collectives(bufs.registry(v_out), group, errors)
+    rs, ag = collectives
+    dtype = _lib.OASIS_DTYPE_BF16 if bufs.partial.dtype == torch.bfloat16 else _lib.OASIS_DTYPE_F32
+    a = _lib.OasisTpSpArgs(bufs.batch, bufs.frames, tpw.heads, bufs.rank, bufs.world, z_local.data_ptr(),
+                           cond_local.data_ptr(), v_out.data_ptr(), dtype, bufs.partial.data_ptr(),
+                           bufs.shard.data_ptr(), bufs.xn_local.data_ptr(), bufs.xn.data_ptr(),
+                           bufs.v_local.data_ptr(), rs, ag, None, bufs.workspace.data_ptr(), bufs.workspace.numel())
+    st = (stream or torch.cuda.current_stream()).cuda_stream
+    try:
+        _lib.call("oasis_dit_forward_tp_sp", C.byref(tpw.struct), C.byref(a), st)
+    except _lib.OasisError:
+        if errors:
+            raise errors[0]
+        raise
+    return v_out

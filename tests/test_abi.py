@@ -34,7 +34,7 @@ def test_library_exports_every_declared_symbol():
 
 STRUCTS = ["OasisDitSubBlock", "OasisDitWeights", "OasisVaeBlock", "OasisVaeWeights", "OasisDitArgs",
            "OasisDdimCoeffs", "OasisStepArgs", "OasisFrameArgs", "OasisVaeArgs", "OasisGemmArgs", "OasisLayerNormArgs",
-           "OasisTpArgs", "OasisVaeEncoderWeights", "OasisVaeEncodeArgs", "OasisCondWeights"]
+           "OasisTpArgs", "OasisVaeEncoderWeights", "OasisVaeEncodeArgs", "OasisCondWeights", "OasisTpSpArgs"]
 
 
 def test_ctypes_layouts_match_c():
