@@ -417,7 +417,17 @@ def c5_compare(rank, world, dev, PAR, reps=3):
         vt = torch.empty(S, H.N_PATCHES, H.OUT_DIM, device=dev)
         out["tp_ms_per_dit_step"] = round(timed(lambda: TP.dit_forward_tp(tpw, zt.copy_(z0), cond, vt, sc)), 3)
         out["tp_allreduce"] = "NCCL, fp32 partials [73728, 1024] after O and FC2 (64 per step)"
-        del tpw, sc
+        del sc
+        # sequence-parallel form: residual sharded by session, all-gather (bf16) before
+        # QKV / FC1 and reduce-scatter (bf16 partials) after O / FC2
+        bufs = TP.TPSpBuffers(tpw, S, T, dev)
+        zl = z0[s0:s0 + b].clone()
+        cl = cond[s0:s0 + b].contiguous()
+        out["tp_sp_ms_per_dit_step"] = round(
+            timed(lambda: TP.dit_forward_tp_sp(tpw, zl.copy_(z0[s0:s0 + b]), cl, vt, bufs)), 3)
+        out["tp_sp_collectives"] = ("NCCL, per sub-block: all-gather of the bf16 LayerNorm output twice, "
+                                    "reduce-scatter of bf16 partials twice")
+        del tpw, bufs
     torch.cuda.empty_cache()
     return out
 
