@@ -26,15 +26,14 @@ constexpr int D = 1024;  // model width of both the DiT and the VAE decoder
 // A run never crosses a group of P rows (R divides P), so the warp loads its
 // lanes' 64 modulation (or affine) values once and reuses them for all R rows:
 // the per-row L2 traffic is the 4 KB row instead of the row plus 8 KB of
-// modulation. The next row's loads are issued before the current row's
-// reduction, so each warp keeps two rows in flight.
+// modulation. (Issuing the next row's loads before the current row's reduction
+// measured slower: the extra 32 registers halve the resident warps.)
 __device__ __forceinline__ void ln_load_row(const float* xr, int lane, float4 (&v)[8]) {
 #pragma unroll
   for (int j = 0; j < 8; ++j) v[j] = reinterpret_cast<const float4*>(xr)[lane + 32 * j];
 }
 
-template <bool kPrefetch>
-__global__ void __launch_bounds__(256, kPrefetch ? 1 : 2)
+__global__ void __launch_bounds__(256, 2)
     layernorm_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, LayerNormParams p, int R) {
   pdl_trigger();
   pdl_wait();
@@ -56,7 +55,7 @@ __global__ void __launch_bounds__(256, kPrefetch ? 1 : 2)
     mul = p.mod + frame * p.ld_mod + p.scale_off;
     add = p.mod + frame * p.ld_mod + p.shift_off;
   }
-  float4 v[8], nv[8], m[8], a[8];
+  float4 v[8], m[8], a[8];
   ln_load_row(x + in_row(r0) * D, lane, v);
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
@@ -65,7 +64,6 @@ __global__ void __launch_bounds__(256, kPrefetch ? 1 : 2)
     a[j] = add ? __ldg(reinterpret_cast<const float4*>(add + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
   }
   for (int r = r0; r < r1; ++r) {
-    if (kPrefetch && r + 1 < r1) ln_load_row(x + in_row(r + 1) * D, lane, nv);
     float s = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; ++j) s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
@@ -91,12 +89,7 @@ __global__ void __launch_bounds__(256, kPrefetch ? 1 : 2)
       const float o3 = (v[j].w - mean) * rstd * m[j].w + a[j].w;
       *reinterpret_cast<uint2*>(yr + c) = make_uint2(pack_bf16x2(o0, o1), pack_bf16x2(o2, o3));
     }
-    if (kPrefetch) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = nv[j];
-    } else if (r + 1 < r1) {
-      ln_load_row(x + in_row(r + 1) * D, lane, v);
-    }
+    if (r + 1 < r1) ln_load_row(x + in_row(r + 1) * D, lane, v);
   }
 }
 
@@ -357,14 +350,7 @@ int layernorm_launch(const float* x, __nv_bfloat16* y, const LayerNormParams& p,
   const int warps = (p.rows_out + R - 1) / R;
   const int warps_per_block = 8;
   const int grid = (warps + warps_per_block - 1) / warps_per_block;
-  static const bool prefetch = [] {
-    const char* e = getenv("OASIS_LN_PREFETCH");
-    return e && e[0] == '1';
-  }();
-  if (prefetch)
-    launch_pdl(layernorm_kernel<true>, dim3(grid), dim3(32 * warps_per_block), 0, s, x, y, p, R);
-  else
-    launch_pdl(layernorm_kernel<false>, dim3(grid), dim3(32 * warps_per_block), 0, s, x, y, p, R);
+  launch_pdl(layernorm_kernel, dim3(grid), dim3(32 * warps_per_block), 0, s, x, y, p, R);
   return check_launch("layernorm_kernel");
 }
 
