@@ -79,18 +79,18 @@ def attn_temporal_cached(a):
 
 
 def frame(a):
-    """One whole frame (4 DDIM steps + VAE) for --batch sessions x --frames T,
-    full-T (default) or with the context rows cached (--kv)."""
+    """One whole frame (conditioning, 4 DDIM steps + VAE) for --batch sessions x
+    --frames T, full-T (default) or with the context rows cached (--kv)."""
     from oasis_b200 import engine as E
     from oasis_b200.weights import DitDeviceWeights, VaeDeviceWeights, init_dit_weights, init_vae_weights
 
     dev = torch.device("cuda")
     dw = DitDeviceWeights(init_dit_weights(seed=0), dev)
     vw = VaeDeviceWeights(init_vae_weights(seed=0), dev)
-    fe = E.FrameEngine(dw, vw, a.batch, a.frames, kv=a.kv)
+    fe = E.FrameEngine(dw, vw, a.batch, a.frames, kv=a.kv, device_cond=True)  # as bench.py
     fe.chunk.normal_()
     fe.context_z.normal_()
-    fe.cond.normal_()
+    fe.actions[..., 0] = 1.0
     a._keep = (dw, vw, fe)
     return fe.run
 
