@@ -18,7 +18,6 @@
 //
 // Waits are bounded (see common.cuh); no TMA multicast is used anywhere.
 #include <cudaTypedefs.h>
-#include <cstdlib>
 #include <mutex>
 #include <stdio.h>
 
@@ -714,32 +713,26 @@ __global__ void __launch_bounds__(kThreads, 1)
 // barrier; the MMA commit arrives on the `empty` and `acc_full` barriers of both
 // CTAs; both CTAs' epilogue warps release an accumulator on the leader's
 // `acc_empty`. No TMA multicast. Every wait is bounded as in gemm_kernel.
-// kStages mainloop stages, kNbuf staging buffers per epilogue warp. The
-// residual epilogue of a K = 1024 projection (O, VAE proj) is bound by how many
-// residual boxes each warp keeps in flight, not by the short mainloop, so it
-// trades mainloop stages for staging buffers (the other instantiation: 5 / 2).
-template <int kStages, int kNbuf>
-struct PairCfgT {
+struct PairCfg {
   static constexpr int BNP = 256;                 // output columns per tile
   static constexpr int A_BYTES = BM * BK * 2;     // this CTA's 128 A rows x 64 K
   static constexpr int B_BYTES = 128 * BK * 2;    // this CTA's 128 W rows x 64 K
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = kStages;
-  static constexpr int NBUF = kNbuf;
+  static constexpr int STAGES = 5;
+  static constexpr int NBUF = 2;
   static constexpr int TMEM_COLS = 2 * BNP;       // two accumulators
   static constexpr int STG_BYTES = kEpiWarps * kStgBytes * NBUF;
   static constexpr int BAR_BYTES = 512;
   static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + STG_BYTES + BAR_BYTES;
   static_assert(SMEM <= 232448, "shared memory per CTA");
-  static_assert(2 * STAGES + 4 + NBUF * kEpiWarps + 2 <= BAR_BYTES / 8, "barrier area");
+  static_assert(2 * STAGES + 4 + 2 * kEpiWarps + 2 <= BAR_BYTES / 8, "barrier area");
 };
-using PairCfg = PairCfgT<5, 2>;
 
-template <class C>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                      const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR, const int M,
                      const int N, const int K, const EpiParams epi) {
+  using C = PairCfg;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* staging = smem + C::STAGES * C::STAGE_BYTES;
@@ -748,7 +741,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_full = empty + C::STAGES;
   uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
-  uint64_t* rbar = reinterpret_cast<uint64_t*>(tmem_base_slot + 4);  // [kEpiWarps][NBUF]
+  uint64_t* rbar = reinterpret_cast<uint64_t*>(tmem_base_slot + 4);  // [kEpiWarps][2]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -775,7 +768,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&acc_full[a], 1);
       mbar_init(&acc_empty[a], 2 * kEpiWarps);  // both CTAs' epilogue warps (used on the leader)
     }
-    for (int i = 0; i < C::NBUF * kEpiWarps; ++i) mbar_init(&rbar[i], 1);
+    for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&rbar[i], 1);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -870,7 +863,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int half = (warp - 2) >> 2;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     uint8_t* stg = staging + (warp - 2) * kStgBytes * C::NBUF;
-    uint64_t* my_rbar = rbar + C::NBUF * (warp - 2);
+    uint64_t* my_rbar = rbar + 2 * (warp - 2);
     const bool resid_tma = reads_resid(epi.mode);
     const SplitK nosplit{nullptr, 1};
     int sbuf = 0;
@@ -1016,13 +1009,13 @@ int launch_bn(const GemmProblem& p, int splits, cudaStream_t stream) {
 }
 
 // 256 x 256 tiles on CTA pairs (gemm_pair_kernel); no split-K, no LN epilogue.
-template <class C>
-int launch_pair_cfg(const GemmProblem& p, cudaStream_t stream) {
+int launch_pair(const GemmProblem& p, cudaStream_t stream) {
+  using C = PairCfg;
   static std::atomic<bool> attr_set[64];
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return set_error(OASIS_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     attr_set[dev & 63] = true;
   }
@@ -1037,33 +1030,9 @@ int launch_pair_cfg(const GemmProblem& p, cudaStream_t stream) {
   const int units = ((p.M + 2 * BM - 1) / (2 * BM)) * ((p.N + C::BNP - 1) / C::BNP);
   const int max_pairs = num_sms() / 2;
   const int pairs = units < max_pairs ? units : max_pairs;
-  launch_pdl_cluster(gemm_pair_kernel<C>, dim3(2 * pairs), dim3(kThreads), C::SMEM, stream, 2, ta, tw, to, tr, p.M,
-                     p.N, p.K, p.epi);
+  launch_pdl_cluster(gemm_pair_kernel, dim3(2 * pairs), dim3(kThreads), C::SMEM, stream, 2, ta, tw, to, tr, p.M, p.N,
+                     p.K, p.epi);
   return check_launch("gemm_pair_kernel");
-}
-
-// Residual epilogues of short-K projections get the deep-staging configuration
-// (OASIS_PAIR_RESID = "SN": S mainloop stages, N staging buffers per warp, one of
-// 52 / 43 / 34; 0 = always 5 / 2).
-int pair_resid_cfg() {
-  static const int c = [] {
-    const char* e = getenv("OASIS_PAIR_RESID");
-    if (!e) return 34;
-    const int v = atoi(e);
-    return (v == 0 || v == 52 || v == 43 || v == 34) ? v : 34;
-  }();
-  return c;
-}
-
-int launch_pair(const GemmProblem& p, cudaStream_t stream) {
-  if (reads_resid(p.epi.mode) && p.K <= 1024) {
-    switch (pair_resid_cfg()) {
-      case 43: return launch_pair_cfg<PairCfgT<4, 3>>(p, stream);
-      case 34: return launch_pair_cfg<PairCfgT<3, 4>>(p, stream);
-      default: break;
-    }
-  }
-  return launch_pair_cfg<PairCfg>(p, stream);
 }
 
 // Which large GEMMs run on CTA pairs. Isolated launches at C4 shapes (TFLOP/s,
