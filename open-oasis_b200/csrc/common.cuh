@@ -449,10 +449,6 @@ __device__ __forceinline__ float gelu_tanh(float x) {
   return 0.5f * x * (1.f + tanh_approx(k0 * (x + k1 * x * x * x)));
 }
 
-__device__ __forceinline__ float gelu_erf(float x) {
-  return 0.5f * x * (1.f + erff(x * 0.7071067811865476f));
-}
-
 // 2^x with the hardware approximation (PTX ex2.approx.ftz.f32, relative error
 // about 2^-22; -inf gives 0): the softmax kernels feed it into bf16 P tiles or
 // fp32 sums, far coarser than its error.
@@ -460,6 +456,23 @@ __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Exact-form GELU 0.5 x (1 + erf(x / sqrt 2)) for bf16 results, with erf from
+// Abramowitz & Stegun 7.1.26 (|error| <= 1.5e-7 on erf): for z = |x| / sqrt 2,
+// t = 1 / (1 + p z), 1 - erf(z) = q = t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) exp(-z^2).
+// Then 1 + erf(x / sqrt 2) is 2 - q for x >= 0 and q for x < 0 (no cancellation
+// for negative x). Two MUFU operations (reciprocal, exp2) and six FMAs.
+__device__ __forceinline__ float gelu_erf(float x) {
+  const float z = fabsf(x) * 0.7071067811865476f;
+  const float t = __fdividef(1.f, fmaf(0.3275911f, z, 1.f));
+  float poly = fmaf(t, 1.061405429f, -1.453152027f);
+  poly = fmaf(t, poly, 1.421413741f);
+  poly = fmaf(t, poly, -0.284496736f);
+  poly = fmaf(t, poly, 0.254829592f);
+  poly *= t;
+  const float q = poly * ex2_approx(-z * z * 1.4426950408889634f);
+  return 0.5f * x * (x >= 0.f ? 2.f - q : q);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
