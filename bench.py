@@ -427,6 +427,16 @@ def c5_compare(rank, world, dev, PAR, reps=3):
             timed(lambda: TP.dit_forward_tp_sp(tpw, zl.copy_(z0[s0:s0 + b]), cl, vt, bufs)), 3)
         out["tp_sp_collectives"] = ("NCCL, per sub-block: all-gather of the bf16 LayerNorm output twice, "
                                     "reduce-scatter of bf16 partials twice")
+        # the same with the collectives on a second stream, overlapped chunk by chunk with the projections
+        comm = torch.cuda.Stream(dev)
+        best = None
+        for ch in (2, 4):
+            if b % ch == 0:
+                ms = round(timed(lambda: TP.dit_forward_tp_sp(tpw, zl.copy_(z0[s0:s0 + b]), cl, vt, bufs,
+                                                              comm_stream=comm, chunks=ch)), 3)
+                out[f"tp_sp_overlap_{ch}_ms_per_dit_step"] = ms
+                best = ms if best is None else min(best, ms)
+        out["tp_sp_overlap_ms_per_dit_step"] = best
         del tpw, bufs
     torch.cuda.empty_cache()
     return out

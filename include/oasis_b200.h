@@ -383,6 +383,15 @@ typedef struct OasisTpSpArgs {
   void* user;
   void* workspace;
   size_t workspace_bytes;
+  /* Overlap (optional): with comm_stream non-NULL the collectives are issued on
+   * comm_stream (the callbacks receive it as `stream`) and each rank's sessions
+   * are processed in `chunks` groups (chunks divides B / world, at most 8), so
+   * the all-gather / reduce-scatter of one group runs while the projections of
+   * the next compute; the library orders the two streams with events and
+   * returns with `stream` waiting for the last collective. NULL / chunks <= 1:
+   * everything in order on `stream`. */
+  oasis_stream_t comm_stream;
+  int chunks;
 } OasisTpSpArgs;
 
 size_t oasis_tp_sp_workspace_size(int batch, int frames, int heads, int world);

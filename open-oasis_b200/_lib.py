@@ -134,7 +134,8 @@ class OasisTpSpArgs(C.Structure):
     _fields_ = [("batch", C.c_int), ("frames", C.c_int), ("heads", C.c_int), ("rank", C.c_int), ("world", C.c_int),
                 ("z", fp), ("cond", fp), ("v_out", fp), ("partial_dtype", C.c_int), ("partial", vp), ("shard", vp),
                 ("xn_local", vp), ("xn", vp), ("v_local", fp), ("reduce_scatter", COLLECTIVE_FN),
-                ("all_gather", COLLECTIVE_FN), ("user", vp), ("workspace", vp), ("workspace_bytes", C.c_size_t)]
+                ("all_gather", COLLECTIVE_FN), ("user", vp), ("workspace", vp), ("workspace_bytes", C.c_size_t),
+                ("comm_stream", vp), ("chunks", C.c_int)]
 
 
 class OasisLayerNormArgs(C.Structure):

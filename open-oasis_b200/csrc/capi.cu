@@ -7,6 +7,7 @@
 #include <string.h>
 
 #include <atomic>
+#include <mutex>
 
 #include "../../include/oasis_b200.h"
 #include "gemm.cuh"
@@ -739,6 +740,23 @@ size_t carve_tp_sp(Carve& c, int B, int T, int heads, int world, TpSpScratch* s)
   return c.used;
 }
 
+// Stream handoff events of the overlapped sequence-parallel forward, created on
+// first use per device (events hold no device memory). Slot 0 orders compute ->
+// communication (recorded and waited at once, so one event serves); slots
+// 1 + k mark the completion of chunk k's latest collective. A wait takes the
+// event's state at the time it is enqueued, so every slot is reused.
+constexpr int kTpMaxChunks = 8;
+cudaEvent_t handoff_event(int slot) {
+  static std::mutex mu;
+  static cudaEvent_t ev[64][1 + kTpMaxChunks] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  cudaEvent_t& e = ev[dev & 63][slot];
+  if (!e && cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) e = nullptr;
+  return e;
+}
+
 int tp_sp_forward_impl(const OasisDitWeights* w, const OasisTpSpArgs* a, cudaStream_t st) {
   OASIS_REQUIRE(w && a, "dit_forward_tp_sp: null argument");
   const int B = a->batch, T = a->frames, H = a->heads, n = a->world, rk = a->rank;
@@ -751,58 +769,112 @@ int tp_sp_forward_impl(const OasisDitWeights* w, const OasisTpSpArgs* a, cudaStr
                 "dit_forward_tp_sp: null tensor");
   OASIS_REQUIRE(a->reduce_scatter && a->all_gather, "dit_forward_tp_sp: null collective");
   OASIS_REQUIRE(w->num_subblocks >= 0 && w->num_subblocks <= OASIS_DIT_SUBBLOCKS, "dit_forward_tp_sp: num_subblocks");
+  const int Bl = B / n;
+  const int C = a->chunks > 1 ? a->chunks : 1;
+  OASIS_REQUIRE(Bl % C == 0 && C <= kTpMaxChunks, "dit_forward_tp_sp: chunks=%d must divide the %d sessions per rank "
+                "(at most %d)", C, Bl, kTpMaxChunks);
   Carve c(a->workspace, a->workspace_bytes);
   TpSpScratch s;
   carve_tp_sp(c, B, T, H, n, &s);
   if (!a->workspace || !c.ok())
     return set_error(OASIS_ERR_WORKSPACE, "dit_forward_tp_sp: workspace %zu bytes < %zu", a->workspace_bytes, c.used);
-  const int Bl = B / n, Fl = Bl * T, Ml = Fl * kP, M = B * T * kP, HD = H * 64;
+  const int Fl = Bl * T, Ml = Fl * kP, HD = H * 64;
+  const int Bc = Bl / C, Mc = Bc * T * kP;  // one chunk: Bc sessions of this rank, Mc rows
+  const int Bg = Bc * n, Mg = Mc * n;       // the chunk gathered over the ranks
   const bool bf16_part = a->partial_dtype == OASIS_DTYPE_BF16;
+  const size_t pe = bf16_part ? 2 : 4;
   const long long ldm = (long long)w->num_subblocks * OASIS_ADALN_WIDTH + 2 * kD;
+  // Compute on `st`; with a communication stream the collectives go there and the
+  // two streams hand chunks over with events, so the collective of chunk k
+  // overlaps the compute of chunk k + 1.
+  cudaStream_t cs = a->comm_stream ? reinterpret_cast<cudaStream_t>(a->comm_stream) : st;
+  const bool two = cs != st;
+  cudaEvent_t ev[1 + kTpMaxChunks] = {};
+  if (two) {
+    for (int k = 0; k <= C; ++k)
+      if (!(ev[k] = handoff_event(k))) return set_error(OASIS_ERR_CUDA, "dit_forward_tp_sp: cudaEventCreate failed");
+  }
+  auto to_comm = [&]() -> int {  // the collective about to be issued sees everything computed so far
+    if (!two) return OASIS_OK;
+    if (cudaEventRecord(ev[0], st) != cudaSuccess || cudaStreamWaitEvent(cs, ev[0], 0) != cudaSuccess)
+      return set_error(OASIS_ERR_CUDA, "dit_forward_tp_sp: stream handoff failed");
+    return OASIS_OK;
+  };
+  auto mark = [&](int k) -> int {  // chunk k's collective is issued: remember where it ends
+    if (!two) return OASIS_OK;
+    if (cudaEventRecord(ev[1 + k], cs) != cudaSuccess) return set_error(OASIS_ERR_CUDA, "dit_forward_tp_sp: event");
+    return OASIS_OK;
+  };
+  auto await = [&](int k) -> int {  // compute on chunk k waits for its collective
+    if (!two) return OASIS_OK;
+    if (cudaStreamWaitEvent(st, ev[1 + k], 0) != cudaSuccess)
+      return set_error(OASIS_ERR_CUDA, "dit_forward_tp_sp: stream handoff failed");
+    return OASIS_OK;
+  };
   OASIS_TRY(compute_adaln(w, a->cond, Fl, s.silu, s.adaln, s.splitk, s.splitk_bytes, st));
   float* z = a->z;
   auto xn_loc = static_cast<__nv_bfloat16*>(a->xn_local);
   auto xn = static_cast<__nv_bfloat16*>(a->xn);
+  auto part = static_cast<uint8_t*>(a->partial);
+  auto shard = static_cast<uint8_t*>(a->shard);
   auto collective = [&](oasis_collective_fn fn, const void* send, void* recv, size_t count, int dtype,
                         const char* what) -> int {
-    const int rc = fn(send, recv, count, dtype, a->user, st);
+    const int rc = fn(send, recv, count, dtype, a->user, cs);
     if (rc != 0) return set_error(rc < 0 ? rc : OASIS_ERR_CUDA, "dit_forward_tp_sp: %s returned %d", what, rc);
     return OASIS_OK;
   };
-  // LayerNorm + modulate of the owned rows, then all-gather: every rank holds xn of all rows
-  auto ln_gather = [&](long long shift, long long scale, const char* what) -> int {
+  // chunk k: owned rows [k Mc, (k + 1) Mc); its gathered rows [k Mg, (k + 1) Mg) of xn / partial
+  auto ln_chunk = [&](int k, long long shift, long long scale) -> int {
     LayerNormParams ln;
-    ln.rows_out = Ml;
+    ln.rows_out = Mc;
     ln.P = kP;
     ln.in_group = kP;
-    ln.mod = s.adaln;
+    ln.mod = s.adaln + (size_t)k * Bc * T * ldm;
     ln.ld_mod = ldm;
     ln.shift_off = shift;
     ln.scale_off = scale;
-    OASIS_TRY(layernorm_launch(z, xn_loc, ln, st));
-    return collective(a->all_gather, xn_loc, xn, (size_t)Ml * kD, OASIS_DTYPE_BF16, what);
+    return layernorm_launch(z + (size_t)k * Mc * kD, xn_loc + (size_t)k * Mc * kD, ln, st);
   };
-  // row-parallel projection -> reduce-scatter to the owned rows -> bias, gate, residual
-  auto project_reduce = [&](const __nv_bfloat16* in, const void* wt, int K, const float* bias, long long gate_off,
-                            const char* what) -> int {
-    GemmProblem p = gemm(in, wt, M, kD, K, s.splitk, s.splitk_bytes);
+  auto gather_chunks = [&](long long shift, long long scale, const char* what) -> int {
+    for (int k = 0; k < C; ++k) {
+      OASIS_TRY(ln_chunk(k, shift, scale));
+      OASIS_TRY(to_comm());
+      OASIS_TRY(collective(a->all_gather, xn_loc + (size_t)k * Mc * kD, xn + (size_t)k * Mg * kD, (size_t)Mc * kD,
+                           OASIS_DTYPE_BF16, what));
+      OASIS_TRY(mark(k));
+    }
+    return OASIS_OK;
+  };
+  // row-parallel projection of chunk k into its partial rows, then their reduce-scatter
+  auto project_scatter = [&](int k, const __nv_bfloat16* in, const void* wt, int K, const char* what) -> int {
+    GemmProblem p = gemm(in, wt, Mg, kD, K, s.splitk, s.splitk_bytes);
     p.epi.mode = bf16_part ? kEpiBF16 : kEpiF32;
-    p.epi.out = a->partial;
+    p.epi.out = part + (size_t)k * Mg * kD * pe;
     p.epi.ldo = kD;
     OASIS_TRY(gemm_launch(p, st));
-    OASIS_TRY(collective(a->reduce_scatter, a->partial, a->shard, (size_t)Ml * kD, a->partial_dtype, what));
+    OASIS_TRY(to_comm());
+    OASIS_TRY(collective(a->reduce_scatter, part + (size_t)k * Mg * kD * pe, shard + (size_t)k * Mc * kD * pe,
+                         (size_t)Mc * kD, a->partial_dtype, what));
+    return mark(k);
+  };
+  auto residual_chunk = [&](int k, const float* bias, long long gate_off) -> int {
+    const float* gate = s.adaln + (size_t)k * Bc * T * ldm + gate_off;
+    float* zk = z + (size_t)k * Mc * kD;
     if (bf16_part)
-      return gated_residual_bf16_launch(z, static_cast<const __nv_bfloat16*>(a->shard), bias, s.adaln + gate_off, ldm,
-                                        kP, Ml, st);
-    return gated_residual_launch(z, static_cast<const float*>(a->shard), bias, s.adaln + gate_off, ldm, kP, Ml, st);
+      return gated_residual_bf16_launch(zk, reinterpret_cast<const __nv_bfloat16*>(shard + (size_t)k * Mc * kD * pe),
+                                        bias, gate, ldm, kP, Mc, st);
+    return gated_residual_launch(zk, reinterpret_cast<const float*>(shard + (size_t)k * Mc * kD * pe), bias, gate,
+                                 ldm, kP, Mc, st);
   };
   for (int i = 0; i < w->num_subblocks; ++i) {
     const OasisDitSubBlock& sb = w->sub[i];
     const bool spatial = (i % 2) == 0;
     const long long off = (long long)i * OASIS_ADALN_WIDTH;
-    OASIS_TRY(ln_gather(off, off + kD, "all_gather before QKV"));
-    {
-      GemmProblem p = gemm(xn, sb.qkv_w, M, 3 * HD, kD, s.splitk, s.splitk_bytes);
+    OASIS_TRY(gather_chunks(off, off + kD, "all_gather before QKV"));
+    for (int k = 0; k < C; ++k) {
+      OASIS_TRY(await(k));  // chunk k's xn has landed
+      const __nv_bfloat16* xk = xn + (size_t)k * Mg * kD;
+      GemmProblem p = gemm(xk, sb.qkv_w, Mg, 3 * HD, kD, s.splitk, s.splitk_bytes);
       p.epi.mode = kEpiRopeBF16;
       p.epi.out = s.qkv;
       p.epi.ldo = 3 * HD;
@@ -812,22 +884,35 @@ int tp_sp_forward_impl(const OasisDitWeights* w, const OasisTpSpArgs* a, cudaStr
       p.epi.rope_stride = spatial ? kP : OASIS_MAX_FRAMES;
       p.epi.rope_dim = HD;
       OASIS_TRY(gemm_launch(p, st));
+      if (spatial)
+        OASIS_TRY(attention_full_launch(s.qkv, s.attn, Bg * T, kP, H, st));
+      else
+        OASIS_TRY(attention_temporal_launch(s.qkv, s.attn, Bg, T, kP, H, st));
+      OASIS_TRY(project_scatter(k, s.attn, sb.out_w, HD, "reduce_scatter after O"));
     }
-    if (spatial)
-      OASIS_TRY(attention_full_launch(s.qkv, s.attn, B * T, kP, H, st));
-    else
-      OASIS_TRY(attention_temporal_launch(s.qkv, s.attn, B, T, kP, H, st));
-    OASIS_TRY(project_reduce(s.attn, sb.out_w, HD, sb.out_b, off + 2 * kD, "reduce_scatter after O"));
-    OASIS_TRY(ln_gather(off + 3 * kD, off + 4 * kD, "all_gather before FC1"));
-    {
-      GemmProblem p = gemm(xn, sb.fc1_w, M, 4 * HD, kD, s.splitk, s.splitk_bytes);
+    for (int k = 0; k < C; ++k) {
+      OASIS_TRY(await(k));  // chunk k's O rows are summed
+      OASIS_TRY(residual_chunk(k, sb.out_b, off + 2 * kD));
+      OASIS_TRY(ln_chunk(k, off + 3 * kD, off + 4 * kD));
+      OASIS_TRY(to_comm());
+      OASIS_TRY(collective(a->all_gather, xn_loc + (size_t)k * Mc * kD, xn + (size_t)k * Mg * kD, (size_t)Mc * kD,
+                           OASIS_DTYPE_BF16, "all_gather before FC1"));
+      OASIS_TRY(mark(k));
+    }
+    for (int k = 0; k < C; ++k) {
+      OASIS_TRY(await(k));
+      GemmProblem p = gemm(xn + (size_t)k * Mg * kD, sb.fc1_w, Mg, 4 * HD, kD, s.splitk, s.splitk_bytes);
       p.epi.mode = kEpiGeluTanhBF16;
       p.epi.out = s.h;
       p.epi.ldo = 4 * HD;
       p.epi.bias = sb.fc1_b;
       OASIS_TRY(gemm_launch(p, st));
+      OASIS_TRY(project_scatter(k, s.h, sb.fc2_w, 4 * HD, "reduce_scatter after FC2"));
     }
-    OASIS_TRY(project_reduce(s.h, sb.fc2_w, 4 * HD, sb.fc2_b, off + 5 * kD, "reduce_scatter after FC2"));
+    for (int k = 0; k < C; ++k) {
+      OASIS_TRY(await(k));
+      OASIS_TRY(residual_chunk(k, sb.fc2_b, off + 5 * kD));
+    }
   }
   // final layer over the owned sessions' last frames, then gather v of all sessions
   const long long foff = (long long)w->num_subblocks * OASIS_ADALN_WIDTH;
@@ -849,7 +934,11 @@ int tp_sp_forward_impl(const OasisDitWeights* w, const OasisTpSpArgs* a, cudaStr
   p.epi.ldo = kOut;
   p.epi.bias = w->final_b;
   OASIS_TRY(gemm_launch(p, st));
-  return collective(a->all_gather, a->v_local, a->v_out, (size_t)Bl * kP * kOut, OASIS_DTYPE_F32, "all_gather of v");
+  OASIS_TRY(to_comm());
+  OASIS_TRY(collective(a->all_gather, a->v_local, a->v_out, (size_t)Bl * kP * kOut, OASIS_DTYPE_F32,
+                       "all_gather of v"));
+  OASIS_TRY(mark(0));
+  return await(0);  // the caller's stream sees v and every collective's buffers released
 }
 
 // ---- context caching (precompute_past_state / dit_forward_currentonly) ----

@@ -175,19 +175,38 @@ def _all_gather(recv: torch.Tensor, send: torch.Tensor, group=None) -> None:
         dist.all_gather(list(recv.view(dist.get_world_size(group), -1).unbind(0)), send.reshape(-1), group=group)
 
 
+def buffer_view(registry: dict[int, torch.Tensor], ptr: int, numel: int) -> torch.Tensor:
+    """The `numel` elements at device address `ptr` inside one of the registered
+    buffers (the library passes chunk offsets into them), as a flat view."""
+    for base, t in registry.items():
+        es = t.element_size()
+        if base <= ptr < base + t.numel() * es:
+            off = (ptr - base) // es
+            if (ptr - base) % es or off + numel > t.numel():
+                raise ValueError(f"collective buffer at +{ptr - base} bytes, {numel} elements, outside its tensor")
+            return t.view(-1)[off:off + numel]
+    raise KeyError(f"collective buffer {ptr:#x} is not one of the registered tensors")
+
+
 def dist_collectives(registry: dict[int, torch.Tensor], group=None, errors: list | None = None):
     """The two callbacks of OasisTpSpArgs over torch.distributed (NCCL on GPUs,
-    gloo on the CPU): the library names buffers by pointer, `registry` maps them
-    back to tensors. A raised exception becomes a non-zero status (kept in
-    `errors`), which aborts the forward."""
+    gloo on the CPU): the library names buffers (or chunks of them) by pointer,
+    `registry` maps them back to tensors. The collective runs with the stream the
+    library passes as the current stream, so it is ordered on it. A raised
+    exception becomes a non-zero status (kept in `errors`), which aborts the
+    forward."""
 
-    def wrap(fn):
+    def wrap(fn, send_ranks, recv_ranks):
         def cb(send, recv, count, dtype, user, stream):
             try:
-                s, r = registry[send], registry[recv]
-                if s.numel() < count or r.numel() < count:
-                    raise ValueError(f"collective of {count} elements on buffers of {s.numel()} / {r.numel()}")
-                fn(r, s, group)
+                n = dist.get_world_size(group)
+                s = buffer_view(registry, send, count * (n if send_ranks else 1))
+                r = buffer_view(registry, recv, count * (n if recv_ranks else 1))
+                if stream and torch.cuda.is_available():
+                    with torch.cuda.stream(torch.cuda.ExternalStream(stream)):
+                        fn(r, s, group)
+                else:
+                    fn(r, s, group)
                 return 0
             except Exception as e:  # noqa: BLE001  (reported through the C status)
                 if errors is not None:
@@ -195,16 +214,19 @@ def dist_collectives(registry: dict[int, torch.Tensor], group=None, errors: list
                 return -2
         return _lib.COLLECTIVE_FN(cb)
 
-    return wrap(_reduce_scatter), wrap(_all_gather)
+    return wrap(_reduce_scatter, True, False), wrap(_all_gather, False, True)
 
 
 def dit_forward_tp_sp(tpw: TPDitWeights, z_local: torch.Tensor, cond_local: torch.Tensor, v_out: torch.Tensor,
-                      bufs: TPSpBuffers, collectives=None, group=None, stream=None) -> torch.Tensor:
+                      bufs: TPSpBuffers, collectives=None, group=None, stream=None, comm_stream=None,
+                      chunks: int = 1) -> torch.Tensor:
     """Sequence-parallel TP DiT forward through oasis_dit_forward_tp_sp: this
     rank's sessions z_local [B / n, T, 144, 1024] (overwritten) and cond_local
     [B / n, T, 1024] -> v_out [B, 144, 64] for every session's last frame.
     `collectives` = (reduce_scatter, all_gather) callbacks; by default
-    torch.distributed on `group`."""
+    torch.distributed on `group`. With `comm_stream` (a torch.cuda.Stream) the
+    collectives run there and each rank's sessions go in `chunks` groups, so the
+    communication of one group overlaps the projections of the next."""
     errors: list = []
     if collectives is None:
         collectives = dist_collectives(bufs.registry(v_out), group, errors)
@@ -213,7 +235,8 @@ def dit_forward_tp_sp(tpw: TPDitWeights, z_local: torch.Tensor, cond_local: torc
     a = _lib.OasisTpSpArgs(bufs.batch, bufs.frames, tpw.heads, bufs.rank, bufs.world, z_local.data_ptr(),
                            cond_local.data_ptr(), v_out.data_ptr(), dtype, bufs.partial.data_ptr(),
                            bufs.shard.data_ptr(), bufs.xn_local.data_ptr(), bufs.xn.data_ptr(),
-                           bufs.v_local.data_ptr(), rs, ag, None, bufs.workspace.data_ptr(), bufs.workspace.numel())
+                           bufs.v_local.data_ptr(), rs, ag, None, bufs.workspace.data_ptr(), bufs.workspace.numel(),
+                           None if comm_stream is None else comm_stream.cuda_stream, chunks)
     st = (stream or torch.cuda.current_stream()).cuda_stream
     try:
         _lib.call("oasis_dit_forward_tp_sp", C.byref(tpw.struct), C.byref(a), st)

@@ -84,7 +84,7 @@ def _tp_worker(rank, world, port, q):
     try:
         dev = torch.device("cuda", rank)
         sd = init_dit_weights(seed=3, n_blocks=2, bias_std=0.02)
-        B, T = 2, 3
+        B, T = 4, 3
         g = torch.Generator().manual_seed(1)
         z = torch.randn(B, T, H.N_PATCHES, H.D_MODEL, generator=g).to(dev)
         cond = torch.randn(B, T, H.D_MODEL, generator=g).to(dev)
@@ -101,10 +101,14 @@ def _tp_worker(rank, world, port, q):
         v_sp = torch.empty_like(v_tp)
         TP.dit_forward_tp_sp(tpw, z[rank * Bl:(rank + 1) * Bl].clone(), cond[rank * Bl:(rank + 1) * Bl].contiguous(),
                              v_sp, bufs)
+        # overlapped: collectives on a second stream, one session per group
+        v_ov = torch.empty_like(v_tp)
+        TP.dit_forward_tp_sp(tpw, z[rank * Bl:(rank + 1) * Bl].clone(), cond[rank * Bl:(rank + 1) * Bl].contiguous(),
+                             v_ov, bufs, comm_stream=torch.cuda.Stream(dev), chunks=Bl)
         torch.cuda.synchronize()
         from oracle import oasis_oracle as O
         ref = O.dit_forward(z.cpu(), cond.cpu(), sd)[:, -1]
-        q.put((rank, rel_l2(v_tp, v_1), rel_l2(v_tp, ref), rel_l2(v_sp, ref)))
+        q.put((rank, rel_l2(v_tp, v_1), rel_l2(v_tp, ref), rel_l2(v_sp, ref), rel_l2(v_ov, ref)))
     finally:
         dist.destroy_process_group()
 
@@ -124,9 +128,9 @@ def test_tp2_matches_single_gpu():
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    for _, err, err_tp, err_sp in res:
+    for _, err, err_tp, err_sp, err_ov in res:
         assert err < 5e-3, res  # bf16 operands; partial sums re-associated across ranks
-        assert err_tp < 1e-2 and err_sp < 1e-2, res  # both TP forms against the fp32 oracle
+        assert err_tp < 1e-2 and err_sp < 1e-2 and err_ov < 1e-2, res  # every TP form against the fp32 oracle
 
 
 # ----------------------------------------------------------------- sequence-parallel TP
@@ -229,28 +233,32 @@ class _EmulatedGroup:
         self.comm = torch.cuda.Stream()
         self.done = None
 
-    def collectives(self, rank: int, registry: dict, stream):
+    def collectives(self, rank: int, registry: dict):
         from oasis_b200 import _lib
 
         def make(kind):
             def cb(send, recv, count, dtype, user, st):
                 try:
+                    stream = torch.cuda.ExternalStream(st)  # the stream the library orders this collective on
+                    n = self.world
+                    s = TP.buffer_view(registry, send, count * (n if kind == "rs" else 1))
+                    r = TP.buffer_view(registry, recv, count * (1 if kind == "rs" else n))
                     ev = torch.cuda.Event()
                     ev.record(stream)
-                    self.slots[rank] = (registry[send], registry[recv], ev, count)
+                    self.slots[rank] = (s, r, ev, count)
                     self.barrier.wait()
                     if rank == 0:
                         with torch.cuda.stream(self.comm):
                             for *_, e, _ in self.slots:
                                 self.comm.wait_event(e)
                             if kind == "rs":
-                                total = sum(s.reshape(self.world, -1).float() for s, *_ in self.slots)
-                                for k, (_, r, _, _) in enumerate(self.slots):
-                                    r.reshape(-1).copy_(total[k])
+                                total = sum(s2.reshape(self.world, -1).float() for s2, *_ in self.slots)
+                                for k, (_, r2, _, _) in enumerate(self.slots):
+                                    r2.reshape(-1).copy_(total[k])
                             else:
-                                for _, r, _, _ in self.slots:
-                                    for j, (s, *_) in enumerate(self.slots):
-                                        r.reshape(self.world, -1)[j].copy_(s.reshape(-1))
+                                for _, r2, _, _ in self.slots:
+                                    for j, (s2, *_) in enumerate(self.slots):
+                                        r2.reshape(self.world, -1)[j].copy_(s2.reshape(-1))
                             self.done = torch.cuda.Event()
                             self.done.record(self.comm)
                     self.barrier.wait()
@@ -265,7 +273,7 @@ class _EmulatedGroup:
         return make("rs"), make("ag")
 
 
-def _tp_sp_emulated(sd, world, z, cond, partial_dtype):
+def _tp_sp_emulated(sd, world, z, cond, partial_dtype, chunks=1):
     import threading
 
     B, T = z.shape[0], z.shape[1]
@@ -280,14 +288,15 @@ def _tp_sp_emulated(sd, world, z, cond, partial_dtype):
         Bl = B // world
         zl = z[r * Bl:(r + 1) * Bl].contiguous().to(dev)
         cl = cond[r * Bl:(r + 1) * Bl].contiguous().to(dev)
-        ranks.append((tpw, bufs, v, zl, cl, torch.cuda.Stream()))
+        ranks.append((tpw, bufs, v, zl, cl, torch.cuda.Stream(), torch.cuda.Stream() if chunks > 1 else None))
     torch.cuda.synchronize()
 
     def run(r):
-        tpw, bufs, v, zl, cl, st = ranks[r]
+        tpw, bufs, v, zl, cl, st, cst = ranks[r]
         try:
             with torch.cuda.stream(st):
-                TP.dit_forward_tp_sp(tpw, zl, cl, v, bufs, grp.collectives(r, bufs.registry(v), st), stream=st)
+                TP.dit_forward_tp_sp(tpw, zl, cl, v, bufs, grp.collectives(r, bufs.registry(v)), stream=st,
+                                     comm_stream=cst, chunks=chunks)
             st.synchronize()
             outs[r] = v.cpu()
         except Exception as e:  # noqa: BLE001
@@ -304,8 +313,9 @@ def _tp_sp_emulated(sd, world, z, cond, partial_dtype):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("world,dtype", [(2, torch.bfloat16), (2, torch.float32), (4, torch.bfloat16)])
-def test_tp_sp_emulated_ranks_match_oracle(world, dtype):
+@pytest.mark.parametrize("world,dtype,chunks", [(2, torch.bfloat16, 1), (2, torch.float32, 1), (4, torch.bfloat16, 1),
+                                                (2, torch.bfloat16, 2)])
+def test_tp_sp_emulated_ranks_match_oracle(world, dtype, chunks):
     """Sequence-parallel TP, full 16-block DiT, `world` ranks emulated on one GPU
     (host threads + streams; the collectives as torch ops), against the fp32
     oracle: every rank's gathered v of the last frame."""
@@ -319,7 +329,7 @@ def test_tp_sp_emulated_ranks_match_oracle(world, dtype):
     g = torch.Generator().manual_seed(5)
     z = torch.randn(B, T, H.N_PATCHES, H.D_MODEL, generator=g)
     cond = torch.randn(B, T, H.D_MODEL, generator=g)
-    outs = _tp_sp_emulated(sd, world, z, cond, dtype)
+    outs = _tp_sp_emulated(sd, world, z, cond, dtype, chunks)  # chunks > 1: communication stream + 2 groups
     ref = O.dit_forward(z, cond, sd)[:, -1]
     for r, v in enumerate(outs):
         assert rel_l2(v, ref) < REL_L2_TOL and cosine(v, ref) > COS_TOL, (r, rel_l2(v, ref), cosine(v, ref))
