@@ -47,7 +47,9 @@ def gemm(a):
     args.resid, args.ldr, args.gate, args.ldg, args.rows_per_frame = out.data_ptr(), N, gate.data_ptr(), N, 144
     args.rope, args.rope_div, args.rope_mod = rope.data_ptr(), 1, 144
     args.block_n, args.splits = a.block_n, a.splits
-    ws = torch.empty(max(_lib.load().oasis_gemm_workspace_size(M, N, K), 256), dtype=torch.uint8, device="cuda")
+    need = C.c_size_t(0)
+    _lib.call("oasis_gemm_plan", M, N, K, a.mode, a.block_n, a.splits, None, None, None, C.byref(need))
+    ws = torch.empty(max(need.value, 256), dtype=torch.uint8, device="cuda")
     args.workspace, args.workspace_bytes = ws.data_ptr(), ws.numel()
     a._keep = (A, W, out, bias, gate, rope, ws, args)
     return lambda: _lib.call("oasis_gemm", C.byref(args), _st())
