@@ -130,16 +130,25 @@ def main():
     a = ap.parse_args()
     launch = globals()[a.case](a)
     if a.time:
+        # the reps launches recorded as one CUDA graph, so the time is the
+        # device's (host launch cost would dominate a few-microsecond kernel)
         for _ in range(3):
             launch()
         torch.cuda.synchronize()
+        s_ = torch.cuda.Stream()
+        with torch.cuda.stream(s_):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s_):
+                for _ in range(a.reps):
+                    launch()
+        g.replay()
+        torch.cuda.synchronize()
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
         ev[0].record()
-        for _ in range(a.reps):
-            launch()
+        g.replay()
         ev[1].record()
         ev[1].synchronize()
-        print(f"{a.case}: {ev[0].elapsed_time(ev[1]) * 1000 / a.reps:.2f} us per launch")
+        print(f"{a.case}: {ev[0].elapsed_time(ev[1]) * 1000 / a.reps:.2f} us per launch (graph)")
     else:
         for _ in range(a.reps):
             launch()
