@@ -430,11 +430,11 @@ def c5_compare(rank, world, dev, PAR, reps=3):
         # the same with the collectives on a second stream, overlapped chunk by chunk with the projections
         comm = torch.cuda.Stream(dev)
         best = None
-        for ch in (2, 4):
+        for ch, res in ((2, 0), (2, 8), (2, 16), (4, 16)):
             if b % ch == 0:
                 ms = round(timed(lambda: TP.dit_forward_tp_sp(tpw, zl.copy_(z0[s0:s0 + b]), cl, vt, bufs,
-                                                              comm_stream=comm, chunks=ch)), 3)
-                out[f"tp_sp_overlap_{ch}_ms_per_dit_step"] = ms
+                                                              comm_stream=comm, chunks=ch, reserve_sms=res)), 3)
+                out[f"tp_sp_overlap_{ch}chunks_{res}sms_ms_per_dit_step"] = ms
                 best = ms if best is None else min(best, ms)
         out["tp_sp_overlap_ms_per_dit_step"] = best
         del tpw, bufs

@@ -392,6 +392,9 @@ typedef struct OasisTpSpArgs {
    * everything in order on `stream`. */
   oasis_stream_t comm_stream;
   int chunks;
+  /* With comm_stream: SMs the GEMM and attention kernels leave free so that the
+   * collective kernels (NCCL's run on SMs) can execute beside them; 0 = none. */
+  int reserve_sms;
 } OasisTpSpArgs;
 
 size_t oasis_tp_sp_workspace_size(int batch, int frames, int heads, int world);

@@ -135,7 +135,7 @@ class OasisTpSpArgs(C.Structure):
                 ("z", fp), ("cond", fp), ("v_out", fp), ("partial_dtype", C.c_int), ("partial", vp), ("shard", vp),
                 ("xn_local", vp), ("xn", vp), ("v_local", fp), ("reduce_scatter", COLLECTIVE_FN),
                 ("all_gather", COLLECTIVE_FN), ("user", vp), ("workspace", vp), ("workspace_bytes", C.c_size_t),
-                ("comm_stream", vp), ("chunks", C.c_int)]
+                ("comm_stream", vp), ("chunks", C.c_int), ("reserve_sms", C.c_int)]
 
 
 class OasisLayerNormArgs(C.Structure):

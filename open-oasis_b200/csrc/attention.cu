@@ -666,7 +666,7 @@ int attention_full_launch(const __nv_bfloat16* qkv, __nv_bfloat16* out, int grou
       attr[dev & 63] = true;
     }
     const int items = groups * H;
-    const int g2 = items < 2 * num_sms() ? items : 2 * num_sms();  // two CTAs per SM
+    const int g2 = items < 2 * grid_sms() ? items : 2 * grid_sms();  // two CTAs per SM
     launch_pdl(attention_spatial_kernel, dim3(g2), dim3(kSpatialWarps * 32), smem, s, qkv, out, items, H);
   } else if (seq <= 160) {
     constexpr int NW = 3;  // 48 query rows per CTA

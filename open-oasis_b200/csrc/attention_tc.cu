@@ -457,7 +457,7 @@ int launch_tc(const __nv_bfloat16* qkv, __nv_bfloat16* out, int groups, int seq,
   OASIS_TRY(make_tma_bf16_2d(&tq, qkv, ld, rows, ld, 64, kTcRows));
   OASIS_TRY(make_tma_bf16_2d(&tkv, qkv, ld, rows, ld, 64, KB));
   const int units = (int)((rows + kTcRows - 1) / kTcRows) * H;
-  const int grid = units < num_sms() ? units : num_sms();
+  const int grid = units < grid_sms() ? units : grid_sms();
   launch_pdl(attention_tc_kernel<KB>, dim3(grid), dim3(kTcThreads), C::SMEM, s, tq, tkv, out, (int)rows, seq, H);
   return check_launch("attention_tc_kernel");
 }

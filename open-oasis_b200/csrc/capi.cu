@@ -811,6 +811,12 @@ int tp_sp_forward_impl(const OasisDitWeights* w, const OasisTpSpArgs* a, cudaStr
       return set_error(OASIS_ERR_CUDA, "dit_forward_tp_sp: stream handoff failed");
     return OASIS_OK;
   };
+  // With overlap, the persistent kernels leave `reserve_sms` SMs to the collectives
+  // (restored when this call returns, on every path).
+  struct Reserve {
+    explicit Reserve(int n) { set_sm_reserve(n); }
+    ~Reserve() { set_sm_reserve(0); }
+  } reserve(two ? a->reserve_sms : 0);
   OASIS_TRY(compute_adaln(w, a->cond, Fl, s.silu, s.adaln, s.splitk, s.splitk_bytes, st));
   float* z = a->z;
   auto xn_loc = static_cast<__nv_bfloat16*>(a->xn_local);

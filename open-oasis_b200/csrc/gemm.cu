@@ -18,6 +18,7 @@
 //
 // Waits are bounded (see common.cuh); no TMA multicast is used anywhere.
 #include <cudaTypedefs.h>
+#include <cstdlib>
 #include <mutex>
 #include <stdio.h>
 
@@ -39,16 +40,20 @@ constexpr int kGroups = kEpiWarps / 4;
 constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer + MMA + epilogue
 constexpr int kStgBytes = 32 * 128;          // per-warp store staging: 32 rows x 128 B
 
-template <int BN>
+// kDeep: the configuration for launches where every CTA has at most one output
+// tile (a few hundred rows, e.g. one session). There is no next tile for the
+// epilogue to overlap, so the epilogue keeps one staging buffer per warp and the
+// shared memory goes to more mainloop stages.
+template <int BN, bool kDeep = false>
 struct Cfg {
   // Two staging buffers per epilogue warp (the store of one chunk overlaps the
   // next; residual tiles are TMA-loaded into them ahead of time). Measured on
   // B200: worth a pipeline stage even at BN = 256.
-  static constexpr int NBUF = kEpiWarps >= 16 ? 1 : 2;
+  static constexpr int NBUF = (kDeep || kEpiWarps >= 16) ? 1 : 2;
   // Narrow tiles load two 64-wide K atoms per TMA instruction (a stage covers
   // K = 128): the per-instruction cost, not bytes, bounds small-M GEMMs.
   static constexpr int KA = BN <= 128 ? 2 : 1;
-  static constexpr int STAGES = BN == 256 ? 3 : (BN == 128 ? 2 : (BN == 64 ? 3 : 4));
+  static constexpr int BASE_STAGES = BN == 256 ? 3 : (BN == 128 ? 2 : (BN == 64 ? 3 : 4));
   static constexpr int A_ATOM = BM * BK * 2;  // bytes of one 64-wide K atom of the A tile
   static constexpr int B_ATOM = BN * BK * 2;
   static constexpr int A_BYTES = A_ATOM * KA;
@@ -59,6 +64,8 @@ struct Cfg {
   static constexpr int BAR_BYTES = 512;
   // row-statistic exchange of the LN epilogue: [2 row blocks][4 quarters][2 halves][32 rows] float2
   static constexpr int LN_BYTES = BN == 256 ? 2 * 4 * 2 * 32 * 8 : 0;
+  static constexpr int DEEP_STAGES = (232448 - 1024 - STG_BYTES - BAR_BYTES - LN_BYTES) / STAGE_BYTES;
+  static constexpr int STAGES = kDeep ? (DEEP_STAGES > 6 ? 6 : DEEP_STAGES) : BASE_STAGES;
   static constexpr int SMEM = 1024 /*align slack*/ + STAGES * STAGE_BYTES + STG_BYTES + BAR_BYTES + LN_BYTES;
   static_assert(SMEM <= 232448, "shared memory per CTA");
 };
@@ -478,14 +485,14 @@ __device__ __forceinline__ int unit_at(int k, bool row_blocks, int units, int n_
 // kLN: the kEpiGatedResidLN instantiation (whole-row blocks, row statistics and
 // the LayerNorm pass); kept separate so the other epilogues' register budget is
 // not shared with it.
-template <int BN, bool kLN>
+template <int BN, bool kLN, bool kDeep = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                 const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR,
                 const __grid_constant__ CUtensorMap tmX, const int M,
                 const int N, const int K,
                 const EpiParams epi, const SplitK sk, const LnParams lnp) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, kDeep>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* staging = smem + C::STAGES * C::STAGE_BYTES;  // 1024-aligned
@@ -964,14 +971,14 @@ int make_out_map(CUtensorMap* map, void* ptr, long long M, long long N, long lon
 
 std::atomic<int> g_num_sms[64];  // per device, zero until first queried
 
-template <int BN, bool kLN>
+template <int BN, bool kLN, bool kDeep = false>
 int launch_bn(const GemmProblem& p, int splits, cudaStream_t stream) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, kDeep>;
   static std::atomic<bool> attr_set[64];  // per device; host threads may launch concurrently
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN, kLN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN, kLN, kDeep>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return set_error(OASIS_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     attr_set[dev & 63] = true;
   }
@@ -997,13 +1004,13 @@ int launch_bn(const GemmProblem& p, int splits, cudaStream_t stream) {
                        p.workspace_bytes);
     sk.partials = static_cast<float*>(p.workspace);
     // one CTA per (tile, split); the splits of a tile are one cluster
-    launch_pdl_cluster(gemm_kernel<BN, kLN>, dim3(tiles * splits), dim3(kThreads), C::SMEM, stream, splits, ta, tw, to,
+    launch_pdl_cluster(gemm_kernel<BN, kLN, kDeep>, dim3(tiles * splits), dim3(kThreads), C::SMEM, stream, splits, ta, tw, to,
                        tr, tx, p.M, p.N, p.K, p.epi, sk, p.ln);
     return check_launch("gemm_kernel");
   }
   const int work = p.epi.mode == kEpiGatedResidLN ? (p.M + BM - 1) / BM : tiles;  // row blocks or tiles
-  const int grid = work < num_sms() ? work : num_sms();
-  launch_pdl(gemm_kernel<BN, kLN>, dim3(grid), dim3(kThreads), C::SMEM, stream, ta, tw, to, tr, tx, p.M, p.N, p.K, p.epi,
+  const int grid = work < grid_sms() ? work : grid_sms();
+  launch_pdl(gemm_kernel<BN, kLN, kDeep>, dim3(grid), dim3(kThreads), C::SMEM, stream, ta, tw, to, tr, tx, p.M, p.N, p.K, p.epi,
              sk, p.ln);
   return check_launch("gemm_kernel");
 }
@@ -1028,7 +1035,7 @@ int launch_pair(const GemmProblem& p, cudaStream_t stream) {
   else
     tr = to;
   const int units = ((p.M + 2 * BM - 1) / (2 * BM)) * ((p.N + C::BNP - 1) / C::BNP);
-  const int max_pairs = num_sms() / 2;
+  const int max_pairs = grid_sms() / 2;
   const int pairs = units < max_pairs ? units : max_pairs;
   launch_pdl_cluster(gemm_pair_kernel, dim3(2 * pairs), dim3(kThreads), C::SMEM, stream, 2, ta, tw, to, tr, p.M, p.N,
                      p.K, p.epi);
@@ -1051,6 +1058,17 @@ int pair_mode() {
     return (int)kPairAll;
   }();
   return m;
+}
+
+// The deep-pipeline configuration for single-wave launches (OASIS_GEMM_DEEP=0:
+// never). Measured on one session at T = 2 (three A/B pairs): C3 frame 8.515 ->
+// 8.235 ms, C2 step 1.918 -> 1.850 ms.
+bool deep_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("OASIS_GEMM_DEEP");
+    return !(e && e[0] == '0');
+  }();
+  return on;
 }
 
 struct Plan {
@@ -1122,6 +1140,15 @@ size_t plan_splitk_bytes(int M, int N, const Plan& pl) {
 
 }  // namespace
 
+thread_local int t_sm_reserve = 0;
+
+void set_sm_reserve(int n) { t_sm_reserve = n > 0 ? n : 0; }
+
+int grid_sms() {
+  const int n = num_sms() - t_sm_reserve;
+  return n >= 2 ? n : 2;
+}
+
 int num_sms() {
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1186,6 +1213,16 @@ int gemm_launch(const GemmProblem& p, cudaStream_t stream) {
   Plan pl;
   OASIS_TRY(resolve_plan(p, &pl));
   if (pl.pair) return launch_pair(p, stream);
+  // one output tile per CTA at most: the deep-pipeline configuration
+  const int units = ((p.M + BM - 1) / BM) * ((p.N + pl.bn - 1) / pl.bn) * pl.splits;
+  if (deep_enabled() && p.epi.mode != kEpiGatedResidLN && units <= num_sms()) {
+    switch (pl.bn) {
+      case 32: return launch_bn<32, false, true>(p, pl.splits, stream);
+      case 64: return launch_bn<64, false, true>(p, pl.splits, stream);
+      case 128: return launch_bn<128, false, true>(p, pl.splits, stream);
+      default: break;
+    }
+  }
   switch (pl.bn) {
     case 32: return launch_bn<32, false>(p, pl.splits, stream);
     case 64: return launch_bn<64, false>(p, pl.splits, stream);

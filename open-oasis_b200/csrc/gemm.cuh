@@ -83,6 +83,12 @@ int gemm_plan(int M, int N, int K, int mode, int block_n, int splits, int* bn, i
 
 int num_sms();
 
+// SMs the persistent kernels (GEMMs, tcgen05 attention) size their grids for:
+// num_sms() minus a reserve set on this host thread, which leaves SMs free for
+// kernels of another stream (the collectives of overlapped tensor parallelism).
+int grid_sms();
+void set_sm_reserve(int n);
+
 // 2-D bf16 TMA map with the 128-byte swizzle over a row-major matrix of `outer`
 // rows x `inner` columns (row stride `ld` elements), box {box_inner, box_outer}.
 int make_tma_bf16_2d(CUtensorMap* map, const void* ptr, long long inner, long long outer, long long ld,

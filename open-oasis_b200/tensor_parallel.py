@@ -219,14 +219,16 @@ def dist_collectives(registry: dict[int, torch.Tensor], group=None, errors: list
 
 def dit_forward_tp_sp(tpw: TPDitWeights, z_local: torch.Tensor, cond_local: torch.Tensor, v_out: torch.Tensor,
                       bufs: TPSpBuffers, collectives=None, group=None, stream=None, comm_stream=None,
-                      chunks: int = 1) -> torch.Tensor:
+                      chunks: int = 1, reserve_sms: int = 0) -> torch.Tensor:
     """Sequence-parallel TP DiT forward through oasis_dit_forward_tp_sp: this
     rank's sessions z_local [B / n, T, 144, 1024] (overwritten) and cond_local
     [B / n, T, 1024] -> v_out [B, 144, 64] for every session's last frame.
     `collectives` = (reduce_scatter, all_gather) callbacks; by default
     torch.distributed on `group`. With `comm_stream` (a torch.cuda.Stream) the
     collectives run there and each rank's sessions go in `chunks` groups, so the
-    communication of one group overlaps the projections of the next."""
+    communication of one group overlaps the projections of the next;
+    `reserve_sms` SMs are then kept free of the persistent kernels for the
+    collectives' own kernels."""
     errors: list = []
     if collectives is None:
         collectives = dist_collectives(bufs.registry(v_out), group, errors)
@@ -236,7 +238,7 @@ def dit_forward_tp_sp(tpw: TPDitWeights, z_local: torch.Tensor, cond_local: torc
                            cond_local.data_ptr(), v_out.data_ptr(), dtype, bufs.partial.data_ptr(),
                            bufs.shard.data_ptr(), bufs.xn_local.data_ptr(), bufs.xn.data_ptr(),
                            bufs.v_local.data_ptr(), rs, ag, None, bufs.workspace.data_ptr(), bufs.workspace.numel(),
-                           None if comm_stream is None else comm_stream.cuda_stream, chunks)
+                           None if comm_stream is None else comm_stream.cuda_stream, chunks, reserve_sms)
     st = (stream or torch.cuda.current_stream()).cuda_stream
     try:
         _lib.call("oasis_dit_forward_tp_sp", C.byref(tpw.struct), C.byref(a), st)

@@ -296,7 +296,7 @@ def _tp_sp_emulated(sd, world, z, cond, partial_dtype, chunks=1):
         try:
             with torch.cuda.stream(st):
                 TP.dit_forward_tp_sp(tpw, zl, cl, v, bufs, grp.collectives(r, bufs.registry(v)), stream=st,
-                                     comm_stream=cst, chunks=chunks)
+                                     comm_stream=cst, chunks=chunks, reserve_sms=16 if chunks > 1 else 0)
             st.synchronize()
             outs[r] = v.cpu()
         except Exception as e:  # noqa: BLE001
