@@ -1127,6 +1127,7 @@ int resolve_plan(const GemmProblem& p, Plan* out) {
   const int pm = pair_mode();
   pl.pair = !p.block_n && pl.bn == 256 && pl.splits == 1 && pm != kPairOff && p.epi.mode != kEpiImage &&
             p.epi.mode != kEpiGatedResidLN && (pm == kPairAll || reads_resid(p.epi.mode)) && p.N % 256 == 0 &&
+            p.M >= 2 * BM &&  // a pair's second CTA would hold no rows (M = 8 adaLN rows: 104.7 -> 88.1 us)
             ((p.M + 2 * BM - 1) / (2 * BM)) * (p.N / 256) >= num_sms() / 2;
   *out = pl;
   return OASIS_OK;
