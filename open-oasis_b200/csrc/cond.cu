@@ -108,6 +108,74 @@ __global__ void __launch_bounds__(256) cond_gemm_kernel(const float* __restrict_
   }
 }
 
+// Few rows (one session's frame: 4 steps x 2 frames = 8): the tiled kernel
+// would put 16 CTAs on a 4 MB weight stream, 64 dependent K steps each. Here a
+// warp owns one output column and its 32 lanes stride K, so each weight row is
+// read as whole 128-byte runs by 256 warps at once; the kRows A rows sit in
+// shared memory (generated, for stage 0). Same arithmetic as the tiled kernel,
+// summed in another order.
+constexpr int kGemvRows = 8;
+template <int kStage>
+__global__ void __launch_bounds__(256) cond_gemv_kernel(const float* __restrict__ levels,
+                                                        const float* __restrict__ freqs,
+                                                        const float* __restrict__ a_in,
+                                                        const float* __restrict__ w, const float* __restrict__ b,
+                                                        const float* __restrict__ actions, int action_rows,
+                                                        const float* __restrict__ ext_w,
+                                                        const float* __restrict__ ext_b, float* __restrict__ out,
+                                                        int n) {
+  constexpr int K = kStage == 0 ? kFreq : kD;
+  __shared__ float As[kGemvRows][K];
+  pdl_trigger();
+  pdl_wait();
+  for (int i = threadIdx.x; i < n * K; i += blockDim.x) {
+    const int r = i / K, k = i - r * K;
+    if constexpr (kStage == 0) {
+      const float arg = levels[r] * freqs[k & 127];
+      As[r][k] = k < 128 ? cosf(arg) : sinf(arg);
+    } else {
+      As[r][k] = a_in[(size_t)r * K + k];
+    }
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  {
+    const int c = blockIdx.x * 8 + warp;
+    const float* wr = w + (size_t)c * K;
+    float acc[kGemvRows];
+#pragma unroll
+    for (int r = 0; r < kGemvRows; ++r) acc[r] = 0.f;
+    for (int k = lane; k < K; k += 32) {
+      const float wv = __ldg(wr + k);
+#pragma unroll
+      for (int r = 0; r < kGemvRows; ++r)
+        if (r < n) acc[r] = fmaf(As[r][k], wv, acc[r]);
+    }
+#pragma unroll
+    for (int r = 0; r < kGemvRows; ++r)
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+    if (lane < n) {
+      float v = b[c];
+#pragma unroll
+      for (int r = 0; r < kGemvRows; ++r)
+        if (r == lane) v += acc[r];
+      const int r = lane;
+      if constexpr (kStage == 0) {
+        v = v / (1.f + expf(-v));  // SiLU
+      } else if (actions) {
+        const float* ar_ = actions + (size_t)(r % action_rows) * kAct;
+        const float* we = ext_w + (size_t)c * kAct;
+        float e = 0.f;
+#pragma unroll
+        for (int q = 0; q < kAct; ++q) e = fmaf(ar_[q], we[q], e);
+        v += e + ext_b[c];
+      }
+      out[(size_t)r * kD + c] = v;
+    }
+  }
+}
+
 }  // namespace
 
 int cond_launch(const OasisCondWeights* w, const float* levels, int n, const float* actions, int action_rows,
@@ -121,6 +189,14 @@ int cond_launch(const OasisCondWeights* w, const float* levels, int n, const flo
   if (!ws || ws_bytes < need)
     return set_error(OASIS_ERR_WORKSPACE, "compute_cond: workspace %zu bytes < %zu", ws_bytes, need);
   float* h = static_cast<float*>(ws);
+  if (n <= kGemvRows) {
+    launch_pdl(cond_gemv_kernel<0>, dim3(kD / 8), dim3(256), 0, st, levels, w->t_freqs, (const float*)nullptr,
+               w->t_w0, w->t_b0, (const float*)nullptr, 1, (const float*)nullptr, (const float*)nullptr, h, n);
+    OASIS_TRY(check_launch("cond_gemv_kernel<0>"));
+    launch_pdl(cond_gemv_kernel<1>, dim3(kD / 8), dim3(256), 0, st, levels, w->t_freqs, (const float*)h, w->t_w2,
+               w->t_b2, actions, action_rows > 0 ? action_rows : 1, w->ext_w, w->ext_b, cond, n);
+    return check_launch("cond_gemv_kernel<1>");
+  }
   const dim3 grid(kD / TN, (n + TM - 1) / TM);
   launch_pdl(cond_gemm_kernel<0>, grid, dim3(256), 0, st, levels, w->t_freqs, (const float*)nullptr, w->t_w0,
              w->t_b0, (const float*)nullptr, 1, (const float*)nullptr, (const float*)nullptr, h, n);
