@@ -108,8 +108,9 @@ __global__ void silu_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __r
 }
 
 // z[out_row, :] = chunk[r, :64] . W[64, 1024] + b, fp32 throughout.
-// Block: 256 threads x 4 columns = one full row width; kRows rows per block.
-constexpr int kEmbedRows = 16;
+// Block: 256 threads x 4 columns = one full row width; kEmbedRows rows per block
+// (16; 2 for a few hundred rows, so a single frame still spreads over ~70 SMs).
+template <int kEmbedRows>
 __global__ void __launch_bounds__(256) patch_embed_kernel(const float* __restrict__ chunk, const float* __restrict__ w,
                                                           const float* __restrict__ b, float* __restrict__ z,
                                                           PatchEmbedParams p) {
@@ -127,7 +128,7 @@ __global__ void __launch_bounds__(256) patch_embed_kernel(const float* __restric
   const float4 bias = b ? *reinterpret_cast<const float4*>(b + c) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
   for (int i = 0; i < kEmbedRows; ++i) acc[i] = bias;
-#pragma unroll 4
+#pragma unroll 8
   for (int k = 0; k < 64; ++k) {
     const float4 wk = __ldg(reinterpret_cast<const float4*>(w + k * D + c));
 #pragma unroll
@@ -365,7 +366,10 @@ int patch_embed_launch(const float* chunk, const float* w, const float* b, float
                        cudaStream_t s) {
   OASIS_REQUIRE(chunk && w && z, "patch_embed: null pointer");
   if (p.rows == 0) return OASIS_OK;
-  launch_pdl(patch_embed_kernel, dim3((p.rows + kEmbedRows - 1) / kEmbedRows), dim3(256), 0, s, chunk, w, b, z, p);
+  if (p.rows <= 2304)
+    launch_pdl(patch_embed_kernel<2>, dim3((p.rows + 1) / 2), dim3(256), 0, s, chunk, w, b, z, p);
+  else
+    launch_pdl(patch_embed_kernel<16>, dim3((p.rows + 15) / 16), dim3(256), 0, s, chunk, w, b, z, p);
   return check_launch("patch_embed_kernel");
 }
 
