@@ -349,7 +349,8 @@ int layernorm_launch(const float* x, __nv_bfloat16* y, const LayerNormParams& p,
       }
   }
   const int warps = (p.rows_out + R - 1) / R;
-  const int warps_per_block = 8;
+  // a few hundred rows: 2 warps per block, so the rows spread over every SM
+  const int warps_per_block = warps < num_sms() * 8 ? 2 : 8;
   const int grid = (warps + warps_per_block - 1) / warps_per_block;
   launch_pdl(layernorm_kernel, dim3(grid), dim3(32 * warps_per_block), 0, s, x, y, p, R);
   return check_launch("layernorm_kernel");
