@@ -636,8 +636,9 @@ int attention_temporal_cached_launch(const __nv_bfloat16* past, const __nv_bfloa
   OASIS_REQUIRE(H >= 1 && H <= 16, "attention_temporal_cached: heads=%d outside [1, 16]", H);
   const long long warps = (long long)batch * P * ((H * kDh + kCachedWarpCols - 1) / kCachedWarpCols);
   if (warps == 0) return OASIS_OK;
-  const int grid = (int)((warps * 32 + 255) / 256);
-  launch_pdl(attention_temporal_cached_kernel, dim3(grid), dim3(256), 0, s, past, cur, out, batch, past_frames, P, H);
+  const int tpb = warps < 8LL * num_sms() ? 64 : 256;  // few rows: small blocks spread over every SM
+  const int grid = (int)((warps * 32 + tpb - 1) / tpb);
+  launch_pdl(attention_temporal_cached_kernel, dim3(grid), dim3(tpb), 0, s, past, cur, out, batch, past_frames, P, H);
   return check_launch("attention_temporal_cached_kernel");
 }
 
