@@ -518,25 +518,43 @@ def main():
     # e2e through the public API with host buffers: the video loop (VideoEngine,
     # the same frame plus the on-device context roll, conditioning computed in
     # the graph), fed each frame's noise chunk and actions from pinned host memory
-    # and reading each decoded frame back to pinned host memory
+    # and reading each decoded frame back to pinned host memory. The read-back of
+    # frame i runs on a copy stream (from a device snapshot of the image, two
+    # alternating) while frame i + 1 computes; the timed region ends when the
+    # last frame has landed in host memory.
     ve = E.VideoEngine(dw, vw, B, T, device_cond=True)
     ve.capture()
     ve.set_context(fe.context_z, acts0[:, :T - 1].to(dev))
     pin = {"noise": chunk0.pin_memory(), "action": acts0[:, T - 1].contiguous().pin_memory()}
-    img_host = torch.empty(ve.image.shape, dtype=torch.float32).pin_memory()
+    img_host = [torch.empty(ve.image.shape, dtype=torch.float32).pin_memory() for _ in range(2)]
+    img_snap = [torch.empty_like(ve.image) for _ in range(2)]
+    copy_stream = torch.cuda.Stream(dev)
+    done = [torch.cuda.Event() for _ in range(2)]
     h2d = sum(v.numel() * v.element_size() for v in pin.values())
-    d2h = img_host.numel() * 4
+    d2h = img_host[0].numel() * 4
+    frame_no = [0]
 
     def e2e_frame():
+        k = frame_no[0] % 2
+        frame_no[0] += 1
         ve.step_actions(pin["noise"], pin["action"])
-        img_host.copy_(ve.image, non_blocking=True)
+        torch.cuda.current_stream().wait_event(done[k])  # snapshot k's previous read-back has finished
+        img_snap[k].copy_(ve.image)
+        ready = torch.cuda.Event()
+        ready.record()
+        with torch.cuda.stream(copy_stream):
+            copy_stream.wait_event(ready)
+            img_host[k].copy_(img_snap[k], non_blocking=True)
+            done[k].record(copy_stream)
 
     for _ in range(2):
         e2e_frame()
+    torch.cuda.synchronize()
     barrier()
     ev[0].record()
     for _ in range(args.steps):
         e2e_frame()
+    torch.cuda.current_stream().wait_stream(copy_stream)
     ev[2].record()
     barrier()
     e2e_value = args.sessions * args.steps / (PAR.max_over_ranks(ev[0].elapsed_time(ev[2])) / 1000.0)
@@ -569,7 +587,8 @@ def main():
             "clocks": clk,
             "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "path": "VideoEngine.step_actions: pinned noise + actions in, conditioning + frame + context "
-                            "roll in one CUDA graph, decoded frames out to pinned host memory"},
+                            "roll in one CUDA graph, decoded frames out to pinned host memory (read-back of "
+                            "frame i on a copy stream while frame i + 1 computes)"},
             "gpu_launches": int(launches_per_frame * args.steps),
             "roofline": roof, "cpu_baseline": cpu, "kv_cache": kv, **extras, "c5_tp_vs_dp": c5,
         }
