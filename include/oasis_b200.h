@@ -400,6 +400,35 @@ typedef struct OasisTpSpArgs {
 size_t oasis_tp_sp_workspace_size(int batch, int frames, int heads, int world);
 int oasis_dit_forward_tp_sp(const OasisDitWeights* shard, const OasisTpSpArgs* a, oasis_stream_t stream);
 
+/* Peer-memory collectives over NVLink (an alternative to NCCL behind the same
+ * two callbacks; replaces the reference's multi-chip all-reduce,
+ * oasis_inference.py:1153-1201, on the mesh of :289-305). The bulk data moves
+ * on the copy engines (cudaMemcpyAsync into a peer's buffer opened through CUDA
+ * IPC); these entry points carry the rest:
+ *   oasis_peer_alloc / free:      device memory that can be shared by IPC (zeroed)
+ *   oasis_ipc_get / open / close: the CUDA IPC handle of such an allocation
+ *   oasis_peer_copy:   cudaMemcpyAsync (unified addressing) on `stream`: over
+ *       NVLink on the copy engines when dst or src is a peer's memory
+ *   oasis_peer_signal: one thread stores `value` to `flag` (this GPU's memory or
+ *       a peer's, release at system scope) after the work before it on `stream`
+ *   oasis_peer_wait:   waits on `stream` until flags[i] >= target for every
+ *       i < n except `skip` (acquire, system scope); after timeout_ns it gives
+ *       up, records a device error (oasis_device_error() returns 16) and returns
+ *   oasis_reduce_slots: dst[i] = sum over k < n, in rank order and in fp32, of
+ *       slot_k[i], slot_k = staging + k slot_stride (elements) except
+ *       slot own_slot = own; written in `dtype` (count, slot_stride multiples of 8) */
+#define OASIS_IPC_HANDLE_BYTES 64
+int oasis_peer_alloc(size_t bytes, void** ptr);
+int oasis_peer_free(void* ptr);
+int oasis_ipc_get_handle(void* ptr, void* handle_out);
+int oasis_ipc_open_handle(const void* handle, void** ptr);
+int oasis_ipc_close_handle(void* ptr);
+int oasis_peer_copy(void* dst, const void* src, size_t bytes, oasis_stream_t stream);
+int oasis_peer_signal(int* flag, int value, oasis_stream_t stream);
+int oasis_peer_wait(const int* flags, int n, int skip, int target, long long timeout_ns, oasis_stream_t stream);
+int oasis_reduce_slots(void* dst, const void* staging, long long slot_stride, const void* own, int own_slot, int n,
+                       long long count, int dtype, oasis_stream_t stream);
+
 /* ------------------------------------------------------------ op level --- */
 
 /* tcgen05 GEMM: acc = A[M,K] . W[N,K]^T (bf16 in, fp32 accumulate) + bias, then

@@ -128,6 +128,7 @@ class OasisTpArgs(C.Structure):
 COLLECTIVE_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_void_p, C.c_size_t, C.c_int, C.c_void_p, C.c_void_p)
 OASIS_DTYPE_F32 = 0
 OASIS_DTYPE_BF16 = 1
+OASIS_IPC_HANDLE_BYTES = 64
 
 
 class OasisTpSpArgs(C.Structure):
@@ -172,6 +173,15 @@ SIGNATURES = {
     "oasis_compute_cond": (C.c_int, [C.POINTER(OasisCondWeights), fp, C.c_int, fp, C.c_int, fp, vp, C.c_size_t, vp]),
     "oasis_tp_sp_workspace_size": (C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int]),
     "oasis_dit_forward_tp_sp": (C.c_int, [C.POINTER(OasisDitWeights), C.POINTER(OasisTpSpArgs), vp]),
+    "oasis_peer_alloc": (C.c_int, [C.c_size_t, C.POINTER(vp)]),
+    "oasis_peer_free": (C.c_int, [vp]),
+    "oasis_ipc_get_handle": (C.c_int, [vp, vp]),
+    "oasis_ipc_open_handle": (C.c_int, [vp, C.POINTER(vp)]),
+    "oasis_ipc_close_handle": (C.c_int, [vp]),
+    "oasis_peer_copy": (C.c_int, [vp, vp, C.c_size_t, vp]),
+    "oasis_peer_signal": (C.c_int, [vp, C.c_int, vp]),
+    "oasis_peer_wait": (C.c_int, [vp, C.c_int, C.c_int, C.c_int, C.c_longlong, vp]),
+    "oasis_reduce_slots": (C.c_int, [vp, vp, C.c_longlong, vp, C.c_int, C.c_int, C.c_longlong, C.c_int, vp]),
     "oasis_kv_cache_size": (C.c_size_t, [C.c_int, C.c_int]),
     "oasis_dit_precompute_past": (C.c_int, [C.POINTER(OasisDitWeights), C.POINTER(OasisDitArgs), vp, C.c_size_t, vp]),
     "oasis_dit_forward_current": (C.c_int, [C.POINTER(OasisDitWeights), C.POINTER(OasisDitArgs), vp, C.c_size_t,

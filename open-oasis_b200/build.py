@@ -16,7 +16,7 @@ CSRC = os.path.join(HERE, "csrc")
 OBJ_DIR = os.path.join(HERE, "_build")
 LIB_NAME = "liboasis_b200.so"
 LIB_PATH = os.path.join(HERE, LIB_NAME)
-SOURCES = ["gemm.cu", "attention.cu", "attention_tc.cu", "pointwise.cu", "capi.cu", "static_scratch.cu", "cond.cu"]
+SOURCES = ["gemm.cu", "attention.cu", "attention_tc.cu", "pointwise.cu", "capi.cu", "static_scratch.cu", "cond.cu", "peer.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -30,6 +30,7 @@ int set_error(int code, const char* fmt, ...) {
 }
 
 int read_device_error(int reset);  // gemm.cu
+int read_device_error_peer(int reset);  // peer.cu
 
 bool pdl_enabled() {
   static const bool on = [] {
@@ -1110,7 +1111,8 @@ const char* oasis_get_last_error(void) { return g_msg; }
 int oasis_device_error(int reset) {
   const int a = read_device_error(reset);
   const int b = read_device_error_tc(reset);
-  return a ? a : b;
+  const int c = read_device_error_peer(reset);
+  return a ? a : (b ? b : c);
 }
 
 unsigned long long oasis_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }

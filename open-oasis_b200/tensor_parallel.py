@@ -217,6 +217,166 @@ def dist_collectives(registry: dict[int, torch.Tensor], group=None, errors: list
     return wrap(_reduce_scatter, True, False), wrap(_all_gather, False, True)
 
 
+class _DeviceBytes:
+    """A raw device allocation seen by torch (CUDA array interface, uint8)."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False), "version": 3,
+                                         "strides": None}
+
+
+def _device_bytes(ptr: int, nbytes: int, device) -> torch.Tensor:
+    return torch.as_tensor(_DeviceBytes(ptr, nbytes), device=device)
+
+
+class PeerCollectives:
+    """The two collective callbacks of OasisTpSpArgs over peer memory: the bulk
+    data crosses NVLink on the copy engines (one copy per peer into its buffer,
+    opened through CUDA IPC) and the library's own peer kernels carry the
+    handshakes and the reduce-scatter sum, so no collective kernel competes with
+    the projections for SMs.
+
+    Every rank shares one device region: the gathered LayerNorm rows (which
+    replace `bufs.xn`, so peers write the all-gather straight into the
+    projections' input), a staging area of `world` slots for reduce-scatter
+    blocks and gathers into other buffers, and two rows of flags. Per collective,
+    with the epoch e counted identically on every rank: each rank signals READY=e
+    to every peer (its receive region is free: everything before the collective
+    on its stream has run), waits for READY=e from every peer, copies its blocks
+    into the peers' regions, signals DONE=e, waits for DONE=e from every peer,
+    and (reduce-scatter) sums the world's blocks in rank order in fp32.
+    Construction and `close` are collective over `group`."""
+
+    READY, DONE = 0, 1
+
+    def __init__(self, bufs: TPSpBuffers, group=None, timeout_s: float = 30.0):
+        lib = _lib.load()
+        self.lib, self.group = lib, group
+        self.n, self.r = bufs.world, bufs.rank
+        if dist.get_world_size(group) != self.n or dist.get_rank(group) != self.r:
+            raise ValueError("PeerCollectives: the group does not match the buffers' rank / world")
+        dev = bufs.xn.device
+        self.timeout_ns = int(timeout_s * 1e9)
+        es = bufs.partial.element_size()
+        self.xn_bytes = bufs.xn.numel() * 2
+        slot = max(bufs.shard.numel() * es, bufs.v_local.numel() * 4)
+        self.slot_bytes = (slot + 255) // 256 * 256
+        self.stage_off = (self.xn_bytes + 255) // 256 * 256
+        self.flag_off = self.stage_off + self.n * self.slot_bytes
+        total = self.flag_off + 2 * 32 * 4
+        base = C.c_void_p()
+        _lib.call("oasis_peer_alloc", total, C.byref(base))
+        self.base, self.total = base.value, total
+        handle = (C.c_char * _lib.OASIS_IPC_HANDLE_BYTES)()
+        _lib.call("oasis_ipc_get_handle", C.c_void_p(self.base), handle)
+        handles = [None] * self.n
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.peer_base = []
+        for p, h in enumerate(handles):
+            if p == self.r:
+                self.peer_base.append(self.base)
+                continue
+            ptr = C.c_void_p()
+            _lib.call("oasis_ipc_open_handle", C.create_string_buffer(h, len(h)), C.byref(ptr))
+            self.peer_base.append(ptr.value)
+        # the projections read the gathered rows from the shared region
+        bufs.xn = _device_bytes(self.base, self.xn_bytes, dev).view(torch.bfloat16).view(bufs.xn.shape)
+        self.bufs = bufs
+        self.epoch = 0
+        self.errors: list = []
+        self._cbs = (_lib.COLLECTIVE_FN(self._guard(self._reduce_scatter)),
+                     _lib.COLLECTIVE_FN(self._guard(self._all_gather)))
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=group)
+
+    @property
+    def callbacks(self):
+        """(reduce_scatter, all_gather) for dit_forward_tp_sp's `collectives`."""
+        return self._cbs
+
+    def _guard(self, fn):
+        def cb(send, recv, count, dtype, user, stream):
+            try:
+                fn(send, recv, count, dtype, stream)
+                return 0
+            except Exception as e:  # noqa: BLE001  (reported through the C status)
+                self.errors.append(e)
+                return -2
+        return cb
+
+    def _flag(self, p: int, kind: int, src: int) -> int:
+        return self.peer_base[p] + self.flag_off + (kind * 32 + src) * 4
+
+    def _handshake(self, kind: int, stream) -> None:
+        for p in range(self.n):
+            if p != self.r:
+                _lib.call("oasis_peer_signal", C.c_void_p(self._flag(p, kind, self.r)), self.epoch, stream)
+        _lib.call("oasis_peer_wait", C.c_void_p(self._flag(self.r, kind, 0)), self.n, self.r, self.epoch,
+                  self.timeout_ns, stream)
+
+    def _copy(self, dst: int, src: int, nbytes: int, stream) -> None:
+        _lib.call("oasis_peer_copy", C.c_void_p(dst), C.c_void_p(src), nbytes, stream)
+
+    def _next_epoch(self) -> None:
+        self.epoch = (self.epoch + 1) & 0x7FFFFFFF
+
+    def _all_gather(self, send, recv, count, dtype, stream) -> None:
+        nbytes = count * (2 if dtype == _lib.OASIS_DTYPE_BF16 else 4)
+        direct = self.base <= recv and recv + self.n * nbytes <= self.base + self.xn_bytes
+        if not direct and nbytes > self.slot_bytes:
+            raise ValueError(f"all_gather of {nbytes} bytes per rank exceeds the staging slot ({self.slot_bytes})")
+        self._next_epoch()
+        self._handshake(self.READY, stream)
+        for p in range(self.n):
+            if p == self.r:
+                self._copy(recv + self.r * nbytes, send, nbytes, stream)
+            elif direct:  # the same offset in the peer's gathered rows
+                self._copy(self.peer_base[p] + (recv - self.base) + self.r * nbytes, send, nbytes, stream)
+            else:
+                self._copy(self.peer_base[p] + self.stage_off + self.r * self.slot_bytes, send, nbytes, stream)
+        self._handshake(self.DONE, stream)
+        if not direct:
+            for p in range(self.n):
+                if p != self.r:
+                    self._copy(recv + p * nbytes, self.base + self.stage_off + p * self.slot_bytes, nbytes, stream)
+
+    def _reduce_scatter(self, send, recv, count, dtype, stream) -> None:
+        nbytes = count * (2 if dtype == _lib.OASIS_DTYPE_BF16 else 4)
+        if nbytes > self.slot_bytes:
+            raise ValueError(f"reduce_scatter of {nbytes} bytes per rank exceeds the staging slot ({self.slot_bytes})")
+        self._next_epoch()
+        self._handshake(self.READY, stream)
+        for p in range(self.n):
+            if p != self.r:  # my partial of p's rows into p's slot r
+                self._copy(self.peer_base[p] + self.stage_off + self.r * self.slot_bytes, send + p * nbytes, nbytes,
+                           stream)
+        self._handshake(self.DONE, stream)
+        es = 2 if dtype == _lib.OASIS_DTYPE_BF16 else 4
+        _lib.call("oasis_reduce_slots", C.c_void_p(recv), C.c_void_p(self.base + self.stage_off),
+                  self.slot_bytes // es, C.c_void_p(send + self.r * nbytes), self.r, self.n, count, dtype, stream)
+
+    def check(self) -> None:
+        """Raises if a callback failed or a peer wait gave up (device error 16)."""
+        if self.errors:
+            raise self.errors[0]
+        err = self.lib.oasis_device_error(1)
+        if err:
+            raise RuntimeError(f"peer collectives: device error {err} (16: a peer did not signal in time)")
+
+    def close(self) -> None:
+        """Collective: every rank finished with the shared region, then unmap and free."""
+        if self.base is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        for p, ptr in enumerate(self.peer_base):
+            if p != self.r:
+                _lib.call("oasis_ipc_close_handle", C.c_void_p(ptr))
+        dist.barrier(group=self.group)
+        _lib.call("oasis_peer_free", C.c_void_p(self.base))
+        self.base = None
+
+
 def dit_forward_tp_sp(tpw: TPDitWeights, z_local: torch.Tensor, cond_local: torch.Tensor, v_out: torch.Tensor,
                       bufs: TPSpBuffers, collectives=None, group=None, stream=None, comm_stream=None,
                       chunks: int = 1, reserve_sms: int = 0) -> torch.Tensor:

@@ -12,6 +12,7 @@ import torch.multiprocessing as mp
 import __graft_entry__
 
 __graft_entry__.load_package()  # spawned workers import this module without conftest
+from oasis_b200 import _lib  # noqa: E402
 from oasis_b200 import tensor_parallel as TP  # noqa: E402
 from tests.helpers import rel_l2  # noqa: E402
 
@@ -105,10 +106,36 @@ def _tp_worker(rank, world, port, q):
         v_ov = torch.empty_like(v_tp)
         TP.dit_forward_tp_sp(tpw, z[rank * Bl:(rank + 1) * Bl].clone(), cond[rank * Bl:(rank + 1) * Bl].contiguous(),
                              v_ov, bufs, comm_stream=torch.cuda.Stream(dev), chunks=Bl)
+        # the same over peer memory: copy-engine transfers + the library's handshake kernels
+        pc = TP.PeerCollectives(bufs)
+        v_pc = torch.empty_like(v_tp)
+        TP.dit_forward_tp_sp(tpw, z[rank * Bl:(rank + 1) * Bl].clone(), cond[rank * Bl:(rank + 1) * Bl].contiguous(),
+                             v_pc, bufs, collectives=pc.callbacks)
+        v_pco = torch.empty_like(v_tp)
+        TP.dit_forward_tp_sp(tpw, z[rank * Bl:(rank + 1) * Bl].clone(), cond[rank * Bl:(rank + 1) * Bl].contiguous(),
+                             v_pco, bufs, collectives=pc.callbacks, comm_stream=torch.cuda.Stream(dev), chunks=Bl)
+        # the callbacks alone, as the library calls them: exact small integers
+        st = torch.cuda.current_stream().cuda_stream
+        rs, ag = pc.callbacks
+        prims = {}
+        for dt, code in ((torch.float32, _lib.OASIS_DTYPE_F32), (torch.bfloat16, _lib.OASIS_DTYPE_BF16)):
+            count = 4096
+            send = ((torch.arange(world * count, device=dev) % 17) * (rank + 1)).to(dt)
+            recv = torch.full((count,), -1.0, device=dev, dtype=dt)
+            rc1 = rs(send.data_ptr(), recv.data_ptr(), count, code, None, st)
+            exp = (torch.arange(count, device=dev) + rank * count) % 17 * sum(range(1, world + 1))
+            mine = torch.full((count,), float(rank + 1), device=dev, dtype=dt)
+            into = torch.zeros(world * count, device=dev, dtype=dt)  # outside the shared region: staged
+            rc2 = ag(mine.data_ptr(), into.data_ptr(), count, code, None, st)
+            prims[str(dt)] = (rc1, rc2, torch.equal(recv.float(), exp.float()),
+                              torch.equal(into.float(), torch.arange(world, device=dev).repeat_interleave(count) + 1.0))
         torch.cuda.synchronize()
+        pc.check()
+        pc.close()
         from oracle import oasis_oracle as O
         ref = O.dit_forward(z.cpu(), cond.cpu(), sd)[:, -1]
-        q.put((rank, rel_l2(v_tp, v_1), rel_l2(v_tp, ref), rel_l2(v_sp, ref), rel_l2(v_ov, ref)))
+        q.put((rank, rel_l2(v_tp, v_1), rel_l2(v_tp, ref), rel_l2(v_sp, ref), rel_l2(v_ov, ref), rel_l2(v_pc, ref),
+               rel_l2(v_pco, ref), rel_l2(v_pc, v_sp), prims))
     finally:
         dist.destroy_process_group()
 
@@ -116,8 +143,11 @@ def _tp_worker(rank, world, port, q):
 @pytest.mark.gpu
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_tp2_matches_single_gpu():
-    """2 GPUs over NCCL: the all-reduce TP forward against the single-GPU forward
-    and the oracle, and the sequence-parallel forward against the oracle."""
+    """2 GPUs: the all-reduce TP forward (NCCL) against the single-GPU forward and
+    the oracle; the sequence-parallel forward against the oracle over NCCL and
+    over peer memory (copy engines + handshake kernels), in order and
+    overlapped; the peer-memory reduce-scatter / all-gather callbacks on exact
+    small integers."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
@@ -128,9 +158,13 @@ def test_tp2_matches_single_gpu():
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    for _, err, err_tp, err_sp, err_ov in res:
+    for _, err, err_tp, err_sp, err_ov, err_pc, err_pco, pc_vs_nccl, prims in res:
         assert err < 5e-3, res  # bf16 operands; partial sums re-associated across ranks
-        assert err_tp < 1e-2 and err_sp < 1e-2 and err_ov < 1e-2, res  # every TP form against the fp32 oracle
+        # every TP form against the fp32 oracle (NCCL and peer-memory collectives)
+        assert max(err_tp, err_sp, err_ov, err_pc, err_pco) < 1e-2, res
+        assert pc_vs_nccl < 5e-3, res  # the two collective back ends differ only in summation rounding
+        for rc1, rc2, rs_ok, ag_ok in prims.values():
+            assert rc1 == 0 and rc2 == 0 and rs_ok and ag_ok, prims
 
 
 # ----------------------------------------------------------------- sequence-parallel TP
