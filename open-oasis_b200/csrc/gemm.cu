@@ -95,9 +95,20 @@ __device__ __forceinline__ void load_resid(const EpiParams& e, int r, int nb, in
 }
 
 // Applies the epilogue to 32 consecutive accumulator columns [nb, nb + 32) of row r, in place.
+// bpre / blane: the bias of these columns spread over the warp's lanes (four
+// consecutive columns per lane, starting at lane blane), broadcast by shuffles.
 __device__ __forceinline__ void epilogue_math(const EpiParams& e, int r, int nb, float (&v)[32],
-                                              const float4 (&res)[8], const float4* gpre = nullptr) {
-  if (e.bias) {
+                                              const float4 (&res)[8], const float4* gpre = nullptr,
+                                              const float4* bpre = nullptr, int blane = 0) {
+  if (bpre) {
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+      v[i] += __shfl_sync(0xffffffffu, bpre->x, blane + i / 4);
+      v[i + 1] += __shfl_sync(0xffffffffu, bpre->y, blane + i / 4);
+      v[i + 2] += __shfl_sync(0xffffffffu, bpre->z, blane + i / 4);
+      v[i + 3] += __shfl_sync(0xffffffffu, bpre->w, blane + i / 4);
+    }
+  } else if (e.bias) {
 #pragma unroll
     for (int i = 0; i < 32; i += 4) {
       const float4 b = __ldg(reinterpret_cast<const float4*>(e.bias + nb + i));
@@ -220,7 +231,8 @@ __device__ __forceinline__ void stage_commit(const CUtensorMap* tm_out, uint8_t*
 __device__ __forceinline__ void epilogue_tile(const EpiParams& e, const SplitK& sk, const CUtensorMap* tm_out,
                                               uint8_t* stg, int nbuf, int& sbuf, uint32_t t_acc, int M, int N,
                                               int BN, int m0q, int n0, int tile, int split, int quarter, int half,
-                                              int lane, uint64_t* acc_bar, uint32_t acc_parity, bool& ok) {
+                                              int lane, uint64_t* acc_bar, uint32_t acc_parity, bool& ok,
+                                              bool spread_bias = false) {
   const int r = m0q + lane;
   const bool bf16 = bf16_out(e.mode);
   const int W = bf16 ? 64 : 32;
@@ -228,6 +240,17 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& e, const SplitK& 
   const bool resid = reads_resid(e.mode) && sk.splits == 1;  // fp32 modes: W == 32
   float4 rcur[8];
   if (resid && half < nchunks && n0 + half * W < N) load_resid(e, r, n0 + half * W, M, rcur);
+  // spread_bias (single-tile launches, where the epilogue is a serial tail):
+  // the bias of this warp's chunks, four columns per lane, read while the
+  // accumulator is still being computed (chunk k of the warp: lanes k W/4 ..).
+  // Measured slower at large M, where the epilogue overlaps the next tile.
+  const int per = W / 4;
+  const bool bias_pre = spread_bias && e.bias && sk.splits == 1 && e.mode != kEpiImage;
+  float4 bpre = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (bias_pre) {
+    const int c = half + (lane / per) * kGroups, col = n0 + c * W + (lane % per) * 4;
+    if (c < nchunks && col < N) bpre = __ldg(reinterpret_cast<const float4*>(e.bias + col));
+  }
   bool acc_ready;
   {
     acc_ready = mbar_wait(acc_bar, acc_parity, kDevTimeoutAccFull);
@@ -257,7 +280,8 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& e, const SplitK& 
 #pragma unroll
         for (int i = 0; i < 8; ++i) __stcg(dst + i, make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
       } else {
-        epilogue_math(e, r, nb + g * 32, v, rcur);
+        epilogue_math(e, r, nb + g * 32, v, rcur, nullptr, bias_pre ? &bpre : nullptr,
+                      ((c - half) / kGroups) * per + g * 8);
         if (e.mode == kEpiImage) {
           if (r < M) store_image(e, r, nb, N, v);
         } else {
@@ -660,7 +684,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             &acc_full[acc], acc_phase, ok, kLN ? stats : nullptr);
       else
         epilogue_tile(epi, sk, &tmO, stg, C::NBUF, sbuf, t_acc, M, N, BN, m0q, n0, tile, split, quarter, half,
-                      lane, &acc_full[acc], acc_phase, ok);
+                      lane, &acc_full[acc], acc_phase, ok, kDeep);
       if (!ok) break;
       tc_fence_before();
       __syncwarp();
