@@ -310,11 +310,28 @@ __device__ __forceinline__ void epilogue_tile_resid(const EpiParams& e, const CU
                                                     const CUtensorMap* tm_res, uint8_t* stg, int nbuf, uint64_t* rbar,
                                                     uint32_t& rphase, uint32_t t_acc, int M, int N, int BN, int m0q,
                                                     int n0, int half, int lane, uint64_t* acc_bar,
-                                                    uint32_t acc_parity, bool& ok, float* stats = nullptr) {
+                                                    uint32_t acc_parity, bool& ok, float* stats = nullptr,
+                                                    bool early = false) {
   const int r = m0q + lane;
   const int nchunks = BN / 32;
   int mine = 0;  // this warp's chunks: c = half + kGroups i, i < mine
   while (half + kGroups * mine < nchunks && n0 + (half + kGroups * mine) * 32 < N) ++mine;
+  // early (single-tile launches, where the epilogue is a serial tail): the first
+  // chunk's gate row and the warp's bias (four columns per lane, broadcast by
+  // shuffles) are read before the accumulator wait
+  float4 gate[8];
+  auto load_gate = [&](int nb) {
+    const float4* g = reinterpret_cast<const float4*>(e.gate + (long long)((r < M ? r : M - 1) / e.rows_per_frame) * e.ldg + nb);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) gate[j] = __ldg(g + j);
+  };
+  const bool bias_pre = early && e.bias;
+  float4 bpre = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (early) {
+    if (gated(e.mode) && mine > 0) load_gate(n0 + half * 32);
+    const int c = half + (lane >> 3) * kGroups, col = n0 + c * 32 + (lane & 7) * 4;
+    if (bias_pre && c < nchunks && col < N) bpre = __ldg(reinterpret_cast<const float4*>(e.bias + col));
+  }
   if (lane == 0) {
     bulk_wait_read0();  // earlier stores no longer read the buffers
     for (int i = 0; i < nbuf && i < mine; ++i) {
@@ -338,12 +355,8 @@ __device__ __forceinline__ void epilogue_tile_resid(const EpiParams& e, const CU
     const int c = half + kGroups * i;
     const int nb = n0 + c * 32;
     uint8_t* buf = stg + b * kStgBytes;
-    float4 gate[8];  // issued before the waits so its latency overlaps them
-    if (gated(e.mode)) {
-      const float4* g = reinterpret_cast<const float4*>(e.gate + (long long)((r < M ? r : M - 1) / e.rows_per_frame) * e.ldg + nb);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) gate[j] = __ldg(g + j);
-    }
+    // issued before the waits so its latency overlaps them
+    if (gated(e.mode) && !(early && i == 0)) load_gate(nb);
     if (!mbar_wait(&rbar[b], (rphase >> b) & 1, kDevTimeoutAccFull)) {
       ok = false;
       return;
@@ -356,7 +369,7 @@ __device__ __forceinline__ void epilogue_tile_resid(const EpiParams& e, const CU
     float4 res[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) res[j] = *reinterpret_cast<const float4*>(row + ((j ^ (lane & 7)) << 4));
-    epilogue_math(e, r, nb, v, res, gated(e.mode) ? gate : nullptr);
+    epilogue_math(e, r, nb, v, res, gated(e.mode) ? gate : nullptr, bias_pre ? &bpre : nullptr, i * 8);
     if (stats) {  // row statistics of the new values: chunk mean / M2, then Chan's combination
       float cm = 0.f;
 #pragma unroll
@@ -681,7 +694,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t t_acc = tmem_base + lane_off + acc * BN;
       if (resid_tma)
         epilogue_tile_resid(epi, &tmO, &tmR, stg, C::NBUF, my_rbar, rphase, t_acc, M, N, BN, m0q, n0, half, lane,
-                            &acc_full[acc], acc_phase, ok, kLN ? stats : nullptr);
+                            &acc_full[acc], acc_phase, ok, kLN ? stats : nullptr, kDeep && BN == 32);
       else
         epilogue_tile(epi, sk, &tmO, stg, C::NBUF, sbuf, t_acc, M, N, BN, m0q, n0, tile, split, quarter, half,
                       lane, &acc_full[acc], acc_phase, ok, kDeep);
